@@ -1,0 +1,150 @@
+/*
+ * libgq -- B200 (sm_100a) kernels for the jax_gptq quantization hot path.
+ *
+ * C ABI: plain pointers, sizes and a CUDA stream passed as void*.  Every
+ * function returns a gq_status; on failure gq_last_error() describes it.
+ * All array pointers are DEVICE pointers unless stated otherwise.  Matrices
+ * are row-major with an explicit leading dimension (elements).  Calls are
+ * stream-ordered and return before the work finishes unless documented as
+ * blocking.  No function allocates device memory: scratch space is passed in
+ * by the caller (query it with the matching *_workspace_size function).
+ *
+ * The reference (davidtweedle/jax_gptq) is pure Python/JAX and has no FFI of
+ * its own; each entry point names the reference function whose array
+ * contract it implements (paths relative to the reference's src/jax_gptq/).
+ */
+#ifndef GQ_H_
+#define GQ_H_
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef enum {
+  GQ_OK = 0,
+  GQ_EINVAL = 1,        /* bad argument (shape, size, mode); nothing launched */
+  GQ_ENOTPD = 2,        /* damped Hessian not positive definite after all retries */
+  GQ_ETIMEOUT = 3,      /* a bounded device-side wait expired */
+  GQ_ECUDA = 4,         /* CUDA runtime error */
+  GQ_EUNSUPPORTED = 5   /* valid input outside what this build supports */
+} gq_status;
+
+/* Library version (major*10000 + minor*100 + patch). */
+int gq_version(void);
+
+/* Message for the most recent failing call on this host thread. */
+const char* gq_last_error(void);
+
+/* ------------------------------------------------------------------------
+ * quant.py:6-37 quantize_dequantize, and the RTN core of
+ * gptq_ref.py:152-155 gptq_forward_step (permute -> RTN -> un-permute).
+ *
+ * w       [m, n] float32 (ldw).  n % group_size == 0, group_size > 0.
+ * perm    [n] int32 column order, or NULL for the identity.  Groups are
+ *         group_size consecutive columns of w[:, perm].
+ * dequant [m, n] float32, original column order (NULL to skip).
+ * codes   [m, n] uint8 = q - qmin, original column order (NULL to skip).
+ * scales, zeros  [m, n / group_size] float32, groups in permuted order
+ *         (NULL to skip).
+ * Bit-exact with the reference's float32 arithmetic: IEEE division,
+ * round-half-to-even, scale floor 1e-8.
+ */
+int gq_rtn(const float* w, int64_t m, int64_t n, int64_t ldw, const int32_t* perm,
+           int w_bits, int group_size, int sym,
+           float* dequant, uint8_t* codes, float* scales, float* zeros, void* stream);
+
+/* ------------------------------------------------------------------------
+ * FP32 GEMM on the CUDA cores: C = alpha * op(A) op(B) + beta * C with
+ * op(A) M x K, op(B) K x N, row-major storage (trans_* = 1 means the stored
+ * matrix is the transpose).  uplo = 0 computes all of C, 1 only tiles that
+ * touch the lower triangle, 2 only tiles that touch the upper triangle
+ * (tiles on the diagonal are computed whole).  Used for the GPTQ lazy
+ * trailing update, Cholesky/inverse updates and the QR compact-WY update.
+ */
+int gq_sgemm(int trans_a, int trans_b, int64_t M, int64_t N, int64_t K, float alpha,
+             const float* a, int64_t lda, const float* b, int64_t ldb, float beta,
+             float* c, int64_t ldc, int uplo, void* stream);
+
+/* stats.py:4-18 for float32 activations (CUDA-core fp32 GEMM). */
+int gq_syrk_f32(const float* x, int64_t tokens, int64_t d, int64_t ldx,
+                float* h, int64_t ldh, int accumulate, void* stream);
+int gq_gemm_tn_f32(const float* xa, int64_t lda, const float* xb, int64_t ldb,
+                   int64_t tokens, int64_t da, int64_t db,
+                   float* g, int64_t ldg, int accumulate, void* stream);
+
+/* Mirror the upper triangle of h[d, d] into the lower triangle. */
+int gq_symmetrize_upper(float* h, int64_t d, int64_t ldh, void* stream);
+
+/* ------------------------------------------------------------------------
+ * gptq_ref.py:67-70: ordering = 0 ("none") writes arange(d); ordering = 1
+ * ("diag_h") writes argsort(diag(h))[::-1] with a stable sort, i.e.
+ * descending diagonal, equal values highest-index-first.
+ */
+int gq_act_order_perm(const float* h, int64_t d, int64_t ldh, int ordering,
+                      int32_t* perm, void* stream);
+
+/* ------------------------------------------------------------------------
+ * gptq_ref.py:72-92 (the damped-Cholesky branch, working): for attempt
+ * e = 0..4 with damp = 10^e * damp_percent * mean(diag(h)) (mean 0 -> 1),
+ * factor Hd = h[perm][:, perm] + damp I and return the upper factor
+ * u = chol(Hd^-1, upper) (u^T u = Hd^-1), computed as the inverse of the
+ * upper factor R of Hd = R R^T.  BLOCKING: synchronizes the stream once per
+ * attempt to read the positive-definiteness flag.  Returns GQ_ENOTPD (u
+ * untouched) when all five attempts fail; *attempt_out receives the
+ * exponent used.  hd_out (nullable) receives the damped, permuted Hessian
+ * of the successful attempt.
+ */
+int64_t gq_hessian_factor_workspace_size(int64_t d);
+int gq_hessian_factor(const float* h, int64_t d, int64_t ldh, const int32_t* perm,
+                      double damp_percent, float* u, int64_t ldu, float* hd_out,
+                      void* workspace, int64_t workspace_bytes, int* attempt_out,
+                      void* stream);
+
+/* ------------------------------------------------------------------------
+ * GPTQ column sweep (the computation gptq_ref.py:136-155 stands in for).
+ * With u = I it reproduces gptq_forward_step bit-exactly.
+ *
+ * w        [m, n] float32 original weights (ldw).
+ * start    NULL, or [m, n] float32 (ld n) initial estimate already in permuted
+ *          column order (replaces w[:, perm]).
+ * u        [n, n] float32 upper factor in permuted coordinates (ldu).
+ * perm     [n] int32 (NULL = identity).
+ * block    lazy-batch width; 128 is supported.
+ * group_size must divide n and either divide 128 (>= 4) or be a multiple of 128.
+ * group0_scale/group0_zero  NULL, or [m] presets for group 0's parameters.
+ * noprop_cols  leading (permuted) columns whose error is not propagated.
+ * Outputs (each nullable): dequant/codes [m, n] original column order;
+ * scales/zeros [m, n / group_size] permuted group order; g_idx [n] =
+ * group of each original column.
+ */
+int64_t gq_gptq_sweep_workspace_size(int64_t m, int64_t n);
+int gq_gptq_sweep(const float* w, int64_t m, int64_t n, int64_t ldw, const float* start,
+                  const float* u, int64_t ldu, const int32_t* perm,
+                  int w_bits, int group_size, int sym, int block,
+                  const float* group0_scale, const float* group0_zero, int noprop_cols,
+                  float* dequant, uint8_t* codes, float* scales, float* zeros,
+                  int32_t* g_idx, void* workspace, int64_t workspace_bytes, void* stream);
+
+/* ------------------------------------------------------------------------
+ * Qronos update (the computation qronos_ref.py:7-25 stands in for), with
+ * h = Xt^T Xt from the quantized-model activations Xt and g = X^T Xt
+ * (h_g_from_activations(x_quant=Xt, x_float=X)).
+ *
+ * w, w_orig [m, n] float32 (ld n): starting estimate and target weights.
+ * hd  [n, n] damped Hessian in permuted coordinates (gq_hessian_factor's
+ *     hd_out); u [n, n] its inverse-Cholesky factor; g [n, n] unpermuted.
+ * perm [n] int32 (NULL = identity).  Outputs as for gq_gptq_sweep.
+ */
+int64_t gq_qronos_workspace_size(int64_t m, int64_t n);
+int gq_qronos(const float* w, const float* w_orig, int64_t m, int64_t n, const float* hd,
+              const float* u, const float* g, const int32_t* perm, int w_bits, int group_size,
+              int sym, int block, float* dequant, uint8_t* codes, float* scales, float* zeros,
+              int32_t* g_idx, void* workspace, int64_t workspace_bytes, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* GQ_H_ */

@@ -1,0 +1,93 @@
+"""ctypes binding of ``libgq.so`` (the C ABI declared in ``include/gq.h``).
+
+The library must have been built in-tree (``python -m jax_gptq_b200.csrc.build``
+or ``__graft_entry__.build()``).  There is no fallback: if it is missing, or
+the process has no CUDA device, the calls raise.
+"""
+
+from __future__ import annotations
+
+import ctypes
+import os
+from ctypes import c_double, c_float, c_int, c_int64, c_void_p
+
+_HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(_HERE, "libgq.so")
+
+GQ_OK = 0
+GQ_EINVAL = 1
+GQ_ENOTPD = 2
+GQ_ETIMEOUT = 3
+GQ_ECUDA = 4
+GQ_EUNSUPPORTED = 5
+
+_P = c_void_p
+# name -> (restype, argtypes)
+SIGNATURES = {
+    "gq_version": (c_int, []),
+    "gq_last_error": (ctypes.c_char_p, []),
+    "gq_rtn": (c_int, [_P, c_int64, c_int64, c_int64, _P, c_int, c_int, c_int, _P, _P, _P, _P, _P]),
+    "gq_sgemm": (c_int, [c_int, c_int, c_int64, c_int64, c_int64, c_float, _P, c_int64, _P, c_int64,
+                         c_float, _P, c_int64, c_int, _P]),
+    "gq_syrk_bf16": (c_int, [_P, c_int64, c_int64, c_int64, _P, c_int64, c_int, _P]),
+    "gq_gemm_tn_bf16": (c_int, [_P, c_int64, _P, c_int64, c_int64, c_int64, c_int64, _P, c_int64,
+                                c_int, _P]),
+    "gq_syrk_f32": (c_int, [_P, c_int64, c_int64, c_int64, _P, c_int64, c_int, _P]),
+    "gq_gemm_tn_f32": (c_int, [_P, c_int64, _P, c_int64, c_int64, c_int64, c_int64, _P, c_int64,
+                               c_int, _P]),
+    "gq_symmetrize_upper": (c_int, [_P, c_int64, c_int64, _P]),
+    "gq_act_order_perm": (c_int, [_P, c_int64, c_int64, c_int, _P, _P]),
+    "gq_hessian_factor_workspace_size": (c_int64, [c_int64]),
+    "gq_hessian_factor": (c_int, [_P, c_int64, c_int64, _P, c_double, _P, c_int64, _P, _P, c_int64,
+                                  ctypes.POINTER(c_int), _P]),
+    "gq_gptq_sweep_workspace_size": (c_int64, [c_int64, c_int64]),
+    "gq_gptq_sweep": (c_int, [_P, c_int64, c_int64, c_int64, _P, _P, c_int64, _P, c_int, c_int, c_int,
+                              c_int, _P, _P, c_int, _P, _P, _P, _P, _P, _P, c_int64, _P]),
+    "gq_qronos_workspace_size": (c_int64, [c_int64, c_int64]),
+    "gq_qronos": (c_int, [_P, _P, c_int64, c_int64, _P, _P, _P, _P, c_int, c_int, c_int, c_int, _P,
+                          _P, _P, _P, _P, _P, c_int64, _P]),
+}
+
+
+class GQError(RuntimeError):
+    def __init__(self, status: int, message: str):
+        super().__init__(f"libgq status {status}: {message}")
+        self.status = status
+
+
+_lib = None
+
+
+def lib():
+    """Load libgq.so once and attach the declared signatures."""
+    global _lib
+    if _lib is None:
+        if not os.path.exists(LIB_PATH):
+            raise RuntimeError(
+                f"{LIB_PATH} is missing: build it with `python -m jax_gptq_b200.csrc.build`")
+        handle = ctypes.CDLL(LIB_PATH)
+        for name, (res, args) in SIGNATURES.items():
+            fn = getattr(handle, name, None)
+            if fn is None:
+                continue
+            fn.restype = res
+            fn.argtypes = args
+        _lib = handle
+    return _lib
+
+
+def exported_symbols() -> list[str]:
+    handle = lib()
+    return [n for n in SIGNATURES if getattr(handle, n, None) is not None]
+
+
+def call(name: str, *args):
+    """Call ``name``; raise ``GQError`` (``ValueError`` for GQ_EINVAL) on failure."""
+    fn = getattr(lib(), name)
+    status = fn(*args)
+    if status != GQ_OK:
+        msg = lib().gq_last_error().decode(errors="replace")
+        if status == GQ_EINVAL:
+            raise ValueError(msg)
+        raise GQError(status, msg)
+    return status

@@ -1,0 +1,73 @@
+// Library-wide plumbing: error strings, version, device properties.
+#include "gq_common.cuh"
+
+#include <cstring>
+
+namespace gq {
+
+static thread_local char g_last_error[1024] = "";
+
+void set_error(const char* fmt, ...) {
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(g_last_error, sizeof(g_last_error), fmt, ap);
+  va_end(ap);
+}
+
+const char* last_error() { return g_last_error; }
+
+int sm_count() {
+  static int cached[64] = {0};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return 148;
+  if (cached[dev] == 0) {
+    int n = 0;
+    if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0)
+      n = 148;
+    cached[dev] = n;
+  }
+  return cached[dev];
+}
+
+// Copy the upper triangle (j > i) of h into the lower triangle.  Tiled
+// through shared memory so both the read and the write are coalesced.
+__global__ void symmetrize_upper_kernel(float* __restrict__ h, int64_t d, int64_t ldh) {
+  __shared__ float tile[32][33];
+  int64_t bi = blockIdx.y, bj = blockIdx.x;  // output tile (bi, bj) in the lower triangle
+  if (bj > bi) return;
+  int tx = threadIdx.x, ty = threadIdx.y;    // 32 x 8
+  // source: tile (bj, bi) of the upper triangle
+  for (int r = ty; r < 32; r += 8) {
+    int64_t i = bj * 32 + r, j = bi * 32 + tx;
+    tile[r][tx] = (i < d && j < d) ? h[i * ldh + j] : 0.f;
+  }
+  __syncthreads();
+  for (int r = ty; r < 32; r += 8) {
+    int64_t i = bi * 32 + r, j = bj * 32 + tx;  // destination (i, j), i > j
+    if (i < d && j < d && i > j) h[i * ldh + j] = tile[tx][r];
+  }
+}
+
+int symmetrize_upper(float* h, int64_t d, int64_t ldh, cudaStream_t st) {
+  if (d <= 1) return GQ_OK;
+  int64_t nt = ceil_div(d, 32);
+  dim3 grid((unsigned)nt, (unsigned)nt);
+  symmetrize_upper_kernel<<<grid, dim3(32, 8), 0, st>>>(h, d, ldh);
+  return check_launch("symmetrize_upper");
+}
+
+}  // namespace gq
+
+extern "C" {
+
+int gq_version(void) { return 100; }
+
+const char* gq_last_error(void) { return gq::last_error(); }
+
+int gq_symmetrize_upper(float* h, int64_t d, int64_t ldh, void* stream) {
+  GQ_REQUIRE(h != nullptr && d >= 0 && ldh >= d, "gq_symmetrize_upper: bad arguments (d=%lld ldh=%lld)",
+             (long long)d, (long long)ldh);
+  return gq::symmetrize_upper(h, d, ldh, gq::as_stream(stream));
+}
+
+}  // extern "C"

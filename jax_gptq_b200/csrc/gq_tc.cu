@@ -1,0 +1,460 @@
+// Activation statistics on the tcgen05 tensor cores (stats.py:16-17):
+//   C[M, N] (+)= A^T B   with A = xa [K, M], B = xb [K, N] (bf16, row-major,
+//   K = tokens), fp32 accumulation in tensor memory.
+//
+// Both operands are read in their native [tokens, features] layout: a TMA
+// box of 64 features x 64 tokens with 128-byte swizzle is exactly one
+// MN-major SW128 canonical block for the UMMA descriptor, so no transpose
+// pass is needed.  One CTA per SM, persistent over output tiles of 128 x 256:
+//   warp 0      TMA producer (one thread), 4-stage ring of 48 KB stages;
+//   warp 1      MMA issuer (one thread): 4 x tcgen05.mma (M128 N256 K16) per
+//               stage into one of two TMEM accumulators (2 x 256 columns);
+//   warps 2-5   epilogue: tcgen05.ld 32 columns at a time, fp32 stores
+//               (optionally accumulating into C).
+// For the symmetric case (xa == xb) only tiles touching the upper triangle
+// are computed and the result is mirrored afterwards.
+//
+// Every mbarrier wait is bounded by a globaltimer deadline; a wait that
+// expires raises a shared abort flag (all roles leave their loops) and
+// records GQ_DEVERR_TIMEOUT in the device status word read by
+// gq_device_status().  No multicast loads are used, so the kernel is safe on
+// any number of GPUs.
+#include <cuda.h>
+
+#include "gq_common.cuh"
+
+namespace gq {
+
+__device__ int g_device_status = 0;
+
+namespace tc {
+
+constexpr int BM = 128, BN = 256, BK = 64, STAGES = 4;
+constexpr int A_STAGE = BM * BK * 2;       // 16 KB
+constexpr int B_STAGE = BN * BK * 2;       // 32 KB
+constexpr int STAGE_BYTES = A_STAGE + B_STAGE;
+constexpr int BOX_BYTES = 64 * BK * 2;     // one 64-feature x 64-token box: 8 KB
+constexpr int TMEM_COLS = 512;
+constexpr int THREADS = 192;
+constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024 /*align*/ + 256 /*barriers*/;
+
+// kind::f16 instruction descriptor: D f32, A/B bf16, both MN-major, N=256, M=128.
+constexpr uint32_t IDESC = (1u << 4) | (1u << 7) | (1u << 10) | (1u << 15) | (1u << 16) |
+                           ((uint32_t)(BN >> 3) << 17) | ((uint32_t)(BM >> 4) << 24);
+
+struct Params {
+  float* c;
+  int64_t ldc;
+  int64_t M, N, K;
+  int symmetric;
+  int accumulate;
+  int num_tiles;
+  int mb;  // row tiles
+  int nb;  // column tiles
+};
+
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+  return (uint32_t)__cvta_generic_to_shared(p);
+}
+
+__device__ __forceinline__ void mbar_init(uint64_t* bar, int count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count));
+}
+__device__ __forceinline__ void mbar_expect_tx(uint64_t* bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)),
+               "r"(bytes)
+               : "memory");
+}
+__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+__device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n"
+      " selp.u32 %0, 1, 0, p;\n}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+// Bounded wait; false when the deadline passed or another role aborted.
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort_flag) {
+  if (mbar_try_wait(bar, parity)) return true;
+  const uint64_t t0 = globaltimer_ns();
+  while (true) {
+    if (mbar_try_wait(bar, parity)) return true;
+    if (*abort_flag) return false;
+    if (globaltimer_ns() - t0 > kWaitLimitNs) {
+      *abort_flag = 1;
+      atomicExch(&g_device_status, GQ_DEVERR_TIMEOUT);
+      return false;
+    }
+  }
+}
+
+__device__ __forceinline__ void tma_load_2d(const CUtensorMap* map, uint64_t* bar, void* dst, int x,
+                                            int y) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%2, %3}], [%4];" ::"r"(smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(smem_u32(bar))
+      : "memory");
+}
+
+__device__ __forceinline__ void fence_before() {
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+}
+__device__ __forceinline__ void fence_after() {
+  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+}
+
+// SW128 UMMA shared-memory descriptor (sm100 format, version 1).
+__device__ __forceinline__ uint64_t make_desc(uint32_t saddr, uint32_t lbo, uint32_t sbo) {
+  uint64_t d = 0;
+  d |= (uint64_t)((saddr >> 4) & 0x3FFFu);
+  d |= (uint64_t)((lbo >> 4) & 0x3FFFu) << 16;
+  d |= (uint64_t)((sbo >> 4) & 0x3FFFu) << 32;
+  d |= 1ull << 46;  // descriptor version for tcgen05
+  d |= 2ull << 61;  // SWIZZLE_128B
+  return d;
+}
+
+__device__ __forceinline__ void umma_bf16(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc,
+                                          uint32_t accum) {
+  asm volatile(
+      "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
+      " tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n}" ::"r"(d_tmem),
+      "l"(adesc), "l"(bdesc), "r"(IDESC), "r"(accum));
+}
+__device__ __forceinline__ void umma_commit(uint64_t* bar) {
+  asm volatile(
+      "tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
+          smem_u32(bar))
+      : "memory");
+}
+
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, "
+      "%12, %13, %14, %15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, "
+      "%30, %31}, [%32];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
+        "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]),
+        "=r"(r[14]), "=r"(r[15]), "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]),
+        "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]), "=r"(r[25]),
+        "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+      : "r"(taddr));
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+}
+
+// Tile index -> (row tile, column tile).  Symmetric: column tile bn owns
+// row tiles 0 .. min(mb, 2 bn + 2) - 1 (those touching the upper triangle).
+__device__ __forceinline__ void tile_coords(const Params& p, int t, int& bm, int& bn) {
+  if (!p.symmetric) {
+    bm = t % p.mb;
+    bn = t / p.mb;
+    return;
+  }
+  int acc = 0;
+  for (int j = 0; j < p.nb; ++j) {
+    int c = min(p.mb, 2 * j + 2);
+    if (t < acc + c) {
+      bn = j;
+      bm = t - acc;
+      return;
+    }
+    acc += c;
+  }
+  bm = 0;
+  bn = 0;
+}
+
+__global__ void __launch_bounds__(THREADS, 1)
+gemm_tn_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_b,
+               Params p) {
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                             ~uintptr_t(1023));
+  uint8_t* sa = smem;
+  uint8_t* sb = smem + STAGES * A_STAGE;
+  uint64_t* full = reinterpret_cast<uint64_t*>(sb + STAGES * B_STAGE);
+  uint64_t* empty = full + STAGES;
+  uint64_t* tfull = empty + STAGES;
+  uint64_t* tempty = tfull + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tempty + 2);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(&tfull[a], 1);
+      mbar_init(&tempty[a], 128);
+    }
+    *abort_flag = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&map_a)) : "memory");
+    asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&map_b)) : "memory");
+  }
+  if (warp == 1) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                     smem_u32(tmem_slot)),
+                 "r"(TMEM_COLS));
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+  }
+  fence_before();
+  __syncthreads();
+  fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+  const int nkb = (int)((p.K + BK - 1) / BK);
+
+  if (warp == 0) {
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      for (int t = blockIdx.x; t < p.num_tiles && !*abort_flag; t += gridDim.x) {
+        int bm, bn;
+        tile_coords(p, t, bm, bn);
+        for (int kb = 0; kb < nkb; ++kb) {
+          if (!mbar_wait(&empty[stage], phase ^ 1, abort_flag)) break;
+          mbar_expect_tx(&full[stage], STAGE_BYTES);
+          const int k0 = kb * BK;
+          uint8_t* a_dst = sa + stage * A_STAGE;
+          uint8_t* b_dst = sb + stage * B_STAGE;
+          tma_load_2d(&map_a, &full[stage], a_dst, bm * BM, k0);
+          tma_load_2d(&map_a, &full[stage], a_dst + BOX_BYTES, bm * BM + 64, k0);
+#pragma unroll
+          for (int q = 0; q < 4; ++q)
+            tma_load_2d(&map_b, &full[stage], b_dst + q * BOX_BYTES, bn * BN + q * 64, k0);
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      int stage = 0, acc = 0;
+      uint32_t phase = 0, acc_phase = 0;
+      for (int t = blockIdx.x; t < p.num_tiles && !*abort_flag; t += gridDim.x) {
+        if (!mbar_wait(&tempty[acc], acc_phase ^ 1, abort_flag)) break;
+        fence_after();
+        const uint32_t d_tmem = tmem_base + (uint32_t)(acc * BN);
+        bool ok = true;
+        for (int kb = 0; kb < nkb; ++kb) {
+          if (!mbar_wait(&full[stage], phase, abort_flag)) {
+            ok = false;
+            break;
+          }
+          fence_after();
+          const uint32_t a_base = smem_u32(sa + stage * A_STAGE);
+          const uint32_t b_base = smem_u32(sb + stage * B_STAGE);
+#pragma unroll
+          for (int kk = 0; kk < BK / 16; ++kk) {
+            // 16 tokens = 16 rows of 128 B; M/N chunks of 64 features are BOX_BYTES apart,
+            // groups of 8 token rows are 1024 B apart.
+            const uint64_t ad = make_desc(a_base + kk * 2048, BOX_BYTES, 1024);
+            const uint64_t bd = make_desc(b_base + kk * 2048, BOX_BYTES, 1024);
+            umma_bf16(d_tmem, ad, bd, (kb > 0 || kk > 0) ? 1u : 0u);
+          }
+          umma_commit(&empty[stage]);
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+        if (!ok) break;
+        umma_commit(&tfull[acc]);
+        if (++acc == 2) {
+          acc = 0;
+          acc_phase ^= 1;
+        }
+      }
+    }
+  } else {
+    // epilogue warps 2..5: warp (w % 4) may access TMEM lanes 32*(w%4) .. +31
+    const int quarter = warp & 3;
+    const int row_in_tile = quarter * 32 + lane;
+    int acc = 0;
+    uint32_t acc_phase = 0;
+    for (int t = blockIdx.x; t < p.num_tiles && !*abort_flag; t += gridDim.x) {
+      int bm, bn;
+      tile_coords(p, t, bm, bn);
+      if (!mbar_wait(&tfull[acc], acc_phase, abort_flag)) break;
+      fence_after();
+      const int64_t row = (int64_t)bm * BM + row_in_tile;
+#pragma unroll 1
+      for (int cc = 0; cc < BN; cc += 32) {
+        uint32_t r[32];
+        tmem_ld32(tmem_base + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(acc * BN + cc), r);
+        const int64_t col0 = (int64_t)bn * BN + cc;
+        if (row < p.M && col0 < p.N) {
+          float* cp = p.c + row * p.ldc + col0;
+          const bool vec = (col0 + 32 <= p.N) && ((reinterpret_cast<uintptr_t>(cp) & 15) == 0);
+          if (vec) {
+#pragma unroll
+            for (int j = 0; j < 32; j += 4) {
+              float4 v = make_float4(__uint_as_float(r[j]), __uint_as_float(r[j + 1]),
+                                     __uint_as_float(r[j + 2]), __uint_as_float(r[j + 3]));
+              if (p.accumulate) {
+                float4 o = *reinterpret_cast<const float4*>(cp + j);
+                v.x += o.x; v.y += o.y; v.z += o.z; v.w += o.w;
+              }
+              *reinterpret_cast<float4*>(cp + j) = v;
+            }
+          } else {
+            for (int j = 0; j < 32 && col0 + j < p.N; ++j) {
+              float v = __uint_as_float(r[j]);
+              if (p.accumulate) v += cp[j];
+              cp[j] = v;
+            }
+          }
+        }
+      }
+      fence_before();
+      mbar_arrive(&tempty[acc]);
+      if (++acc == 2) {
+        acc = 0;
+        acc_phase ^= 1;
+      }
+    }
+  }
+
+  fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem_base),
+                 "r"(TMEM_COLS));
+  }
+}
+
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
+                                  const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
+                                  const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle,
+                                  CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+static EncodeTiledFn encode_fn() {
+  static EncodeTiledFn fn = nullptr;
+  if (!fn) {
+    void* ptr = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q) ==
+            cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiledFn>(ptr);
+  }
+  return fn;
+}
+
+// [tokens, features] bf16 map with a 64 x 64 box, 128-byte swizzle.
+static int make_map(CUtensorMap* map, const void* x, int64_t tokens, int64_t feats, int64_t ld) {
+  EncodeTiledFn fn = encode_fn();
+  if (!fn) return fail(GQ_ECUDA, "cuTensorMapEncodeTiled is unavailable");
+  cuuint64_t dims[2] = {(cuuint64_t)feats, (cuuint64_t)tokens};
+  cuuint64_t strides[1] = {(cuuint64_t)(ld * 2)};
+  cuuint32_t box[2] = {64, (cuuint32_t)BK};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(x), dims, strides,
+                  box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                  CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail(GQ_ECUDA, "cuTensorMapEncodeTiled failed (%d)", (int)r);
+  return GQ_OK;
+}
+
+static int check_operand(const char* who, const void* x, int64_t tokens, int64_t feats,
+                         int64_t ld) {
+  GQ_REQUIRE(x != nullptr, "%s: NULL activations", who);
+  GQ_REQUIRE(tokens >= 0 && feats > 0 && ld >= feats, "%s: bad shape", who);
+  GQ_REQUIRE(ld % 8 == 0, "%s: ld must be a multiple of 8 elements (16-byte TMA stride)", who);
+  GQ_REQUIRE((reinterpret_cast<uintptr_t>(x) & 15) == 0, "%s: activations must be 16-byte aligned",
+             who);
+  GQ_REQUIRE(tokens < (1ll << 31) && feats < (1ll << 31), "%s: dimension too large", who);
+  return GQ_OK;
+}
+
+int launch(const void* xa, int64_t lda, const void* xb, int64_t ldb, int64_t K, int64_t M,
+           int64_t N, float* c, int64_t ldc, int accumulate, int symmetric, cudaStream_t st) {
+  if (K == 0) {
+    if (!accumulate)
+      GQ_CHECK_CUDA(cudaMemset2DAsync(c, ldc * 4, 0, N * 4, M, st));
+    return GQ_OK;
+  }
+  CUtensorMap ma, mbm;
+  GQ_TRY(make_map(&ma, xa, K, M, lda));
+  GQ_TRY(make_map(&mbm, xb, K, N, ldb));
+  Params p;
+  p.c = c;
+  p.ldc = ldc;
+  p.M = M;
+  p.N = N;
+  p.K = K;
+  p.symmetric = symmetric;
+  p.accumulate = accumulate;
+  p.mb = (int)ceil_div(M, BM);
+  p.nb = (int)ceil_div(N, BN);
+  if (symmetric) {
+    int64_t cnt = 0;
+    for (int j = 0; j < p.nb; ++j) cnt += std::min(p.mb, 2 * j + 2);
+    p.num_tiles = (int)cnt;
+  } else {
+    p.num_tiles = p.mb * p.nb;
+  }
+  static bool attr_set = false;
+  if (!attr_set) {
+    GQ_CHECK_CUDA(cudaFuncSetAttribute(gemm_tn_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       SMEM_BYTES));
+    attr_set = true;
+  }
+  const int grid = std::min(p.num_tiles, sm_count());
+  gemm_tn_kernel<<<grid, THREADS, SMEM_BYTES, st>>>(ma, mbm, p);
+  return check_launch("tcgen05 gemm_tn");
+}
+
+}  // namespace tc
+
+int symmetrize_upper(float* h, int64_t d, int64_t ldh, cudaStream_t st);
+
+}  // namespace gq
+
+extern "C" {
+
+int gq_syrk_bf16(const uint16_t* x, int64_t tokens, int64_t d, int64_t ldx, float* h, int64_t ldh,
+                 int accumulate, void* stream) {
+  GQ_TRY(gq::tc::check_operand("gq_syrk_bf16", x, tokens, d, ldx));
+  GQ_REQUIRE(h != nullptr && ldh >= d, "gq_syrk_bf16: bad output");
+  cudaStream_t st = gq::as_stream(stream);
+  GQ_TRY(gq::tc::launch(x, ldx, x, ldx, tokens, d, d, h, ldh, accumulate, 1, st));
+  return gq::symmetrize_upper(h, d, ldh, st);
+}
+
+int gq_gemm_tn_bf16(const uint16_t* xa, int64_t lda, const uint16_t* xb, int64_t ldb,
+                    int64_t tokens, int64_t da, int64_t db, float* g, int64_t ldg, int accumulate,
+                    void* stream) {
+  GQ_TRY(gq::tc::check_operand("gq_gemm_tn_bf16", xa, tokens, da, lda));
+  GQ_TRY(gq::tc::check_operand("gq_gemm_tn_bf16", xb, tokens, db, ldb));
+  GQ_REQUIRE(g != nullptr && ldg >= db, "gq_gemm_tn_bf16: bad output");
+  return gq::tc::launch(xa, lda, xb, ldb, tokens, da, db, g, ldg, accumulate, 0,
+                        gq::as_stream(stream));
+}
+
+int gq_device_status(int* status_out, int reset, void* stream) {
+  GQ_REQUIRE(status_out != nullptr, "gq_device_status: NULL output");
+  cudaStream_t st = gq::as_stream(stream);
+  GQ_CHECK_CUDA(cudaStreamSynchronize(st));
+  int v = 0;
+  GQ_CHECK_CUDA(cudaMemcpyFromSymbol(&v, gq::g_device_status, sizeof(int)));
+  if (reset) {
+    int z = 0;
+    GQ_CHECK_CUDA(cudaMemcpyToSymbol(gq::g_device_status, &z, sizeof(int)));
+  }
+  *status_out = v;
+  return GQ_OK;
+}
+
+}  // extern "C"

@@ -1,0 +1,73 @@
+"""CPU-side checks of the C ABI: the library loads, exports every symbol that
+``include/gq.h`` declares, and rejects bad arguments before launching
+anything (no GPU needed for either)."""
+
+import ctypes
+import os
+import re
+
+import pytest
+
+from jax_gptq_b200 import _lib
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+
+
+def _declared_symbols():
+    names = set()
+    for fn in os.listdir(os.path.join(ROOT, "include")):
+        if fn.endswith(".h"):
+            text = open(os.path.join(ROOT, "include", fn)).read()
+            names |= set(re.findall(r"\b(gq_[a-z0-9_]+)\s*\(", text))
+    return names
+
+
+def test_library_exports_every_declared_symbol():
+    handle = _lib.lib()
+    declared = _declared_symbols()
+    assert "gq_rtn" in declared and "gq_gptq_sweep" in declared
+    missing = [n for n in sorted(declared) if getattr(handle, n, None) is None]
+    assert not missing, missing
+
+
+def test_every_declared_symbol_has_a_ctypes_signature():
+    declared = _declared_symbols()
+    assert declared <= set(_lib.SIGNATURES), sorted(declared - set(_lib.SIGNATURES))
+
+
+def test_version_and_error_string():
+    assert _lib.lib().gq_version() >= 100
+
+
+def test_invalid_group_size_is_rejected_without_launch():
+    lib = _lib.lib()
+    st = lib.gq_rtn(None, 4, 130, 130, None, 4, 128, 0, None, None, None, None, None)
+    assert st == _lib.GQ_EINVAL
+    assert b"group_size" in lib.gq_last_error()
+    with pytest.raises(ValueError, match="group_size"):
+        _lib.call("gq_rtn", None, 4, 130, 130, None, 4, 128, 0, None, None, None, None, None)
+
+
+def test_sweep_rejects_unsupported_block_and_group():
+    lib = _lib.lib()
+    st = lib.gq_gptq_sweep(None, 4, 256, 256, None, None, 256, None, 4, 128, 0, 64, None, None, 0,
+                           None, None, None, None, None, None, 0, None)
+    assert st == _lib.GQ_EINVAL
+    st = lib.gq_gptq_sweep(None, 4, 192, 192, None, None, 192, None, 4, 96, 0, 128, None, None, 0,
+                           None, None, None, None, None, None, 0, None)
+    assert st == _lib.GQ_EINVAL
+
+
+def test_workspace_sizes_are_positive():
+    lib = _lib.lib()
+    assert lib.gq_gptq_sweep_workspace_size(4096, 11008) >= 4096 * 11008 * 5
+    assert lib.gq_hessian_factor_workspace_size(4096) >= 4096 * 4096 * 4
+    assert lib.gq_qronos_workspace_size(64, 256) > lib.gq_gptq_sweep_workspace_size(64, 256)
+
+
+def test_hessian_factor_rejects_small_workspace():
+    lib = _lib.lib()
+    att = ctypes.c_int(0)
+    st = lib.gq_hessian_factor(ctypes.c_void_p(16), 64, 64, None, 0.01, ctypes.c_void_p(16), 64,
+                               None, ctypes.c_void_p(16), 8, ctypes.byref(att), None)
+    assert st == _lib.GQ_EINVAL

@@ -1,0 +1,180 @@
+"""GPU parity of the quantization path through the C ABI against the oracle.
+
+Bit-exact: RTN codes / dequant (reference semantics), act-order permutation,
+the sweep with U = I.  Tolerances (written per test): H within 1e-5
+relative; the inverse-Cholesky factor within 2e-3 relative Frobenius of the
+float64 oracle (float32 Cholesky of a damped Hessian); intended-semantics
+reconstruction error within 1e-3 relative of the float64 oracle's.
+"""
+
+import os
+
+import numpy as np
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+
+from jax_gptq_b200 import QuantConfig, gptq_forward_step, h_g_from_activations
+from jax_gptq_b200 import process_hessian, qronos_single_layer_update_ref, quantize_dequantize
+from jax_gptq_b200 import gptq_ref as G
+from jax_gptq_b200 import qronos_ref as Q
+from jax_gptq_b200 import quant as RQ
+from oracle import gptq as og
+from oracle import inputs
+from oracle import qronos as oqn
+from oracle import quant as oq
+from oracle import stats as ost
+
+
+def _golden(golden_dir, name):
+    return np.load(os.path.join(golden_dir, name))
+
+
+def test_rtn_bit_exact_vs_reference_vectors(golden_dir):
+    d = _golden(golden_dir, "rtn_golden.npz")
+    names = [k[:-2] for k in d.files if k.startswith("rtn_") and k.endswith("_w")]
+    for name in names:
+        bits, gs, sym = (int(v) for v in d[name + "_cfg"])
+        cfg = QuantConfig(w_bits=bits, group_size=gs, sym=bool(sym))
+        out = quantize_dequantize(d[name + "_w"], cfg)
+        assert isinstance(out, np.ndarray)
+        assert np.array_equal(out, d[name + "_out"]), name
+
+
+@pytest.mark.parametrize("shape,bits,gs,sym", [
+    ((256, 1024), 4, 128, False), ((64, 4096), 3, 128, False), ((128, 512), 4, 64, True),
+    ((33, 384), 8, 32, False), ((7, 40), 2, 4, True), ((1, 11008), 4, 128, False)])
+def test_rtn_codes_scales_zeros_match_oracle(shape, bits, gs, sym):
+    rng = np.random.default_rng(sum(shape) + bits)
+    w = (rng.standard_normal(shape) * 0.02).astype(np.float32)
+    w[0, :gs] = 0.0  # constant group -> scale floor
+    dq, q, s, z = oq.rtn(w, bits, gs, sym)
+    res = RQ.rtn(w, QuantConfig(w_bits=bits, group_size=gs, sym=sym))
+    qmin = oq.qrange(bits, sym)[0]
+    assert np.array_equal(res.dequant.cpu().numpy(), dq)
+    assert np.array_equal(res.codes.cpu().numpy().astype(np.float32) + qmin, q)
+    assert np.array_equal(res.scales.cpu().numpy(), s)
+    assert np.array_equal(res.zeros.cpu().numpy(), z)
+
+
+@pytest.mark.parametrize("case", ["none", "diag", "diag_sym3"])
+def test_gptq_reference_semantics_bit_exact(golden_dir, case):
+    d = _golden(golden_dir, "gptq_golden.npz")
+    p = f"gptq_{case}"
+    bits, gs, sym, diag = (int(v) for v in d[p + "_cfg"])
+    cfg = QuantConfig(w_bits=bits, group_size=gs, sym=bool(sym),
+                      ordering_mode="diag_h" if diag else "none")
+    x = d[p + "_x"]
+    h, g = h_g_from_activations(x)
+    hinv, perm = process_hessian(h, cfg)
+    assert np.array_equal(hinv, np.eye(x.shape[1]))
+    assert np.array_equal(perm, d[p + "_perm"])
+    out = gptq_forward_step(d[p + "_w"], hinv, perm, cfg)
+    assert np.array_equal(out, d[p + "_out"])
+    # the sweep kernel with U = I gives the same bits
+    sw = G.gptq_sweep(d[p + "_w"], hinv, perm, cfg)
+    assert np.array_equal(sw.dequant.cpu().numpy(), d[p + "_out"])
+    qr = qronos_single_layer_update_ref(d[p + "_w"], d[p + "_w"], h, g, cfg)
+    assert np.array_equal(qr, d[p + "_qronos"])
+
+
+def test_act_order_perm_matches_oracle_with_ties():
+    rng = np.random.default_rng(5)
+    for d in (7, 300, 4096):
+        diag = rng.integers(0, 5, size=d).astype(np.float32)  # many ties
+        h = np.diag(diag).astype(np.float32)
+        dev = torch.from_numpy(h).cuda()
+        perm = G.act_order_perm(dev, "diag_h").cpu().numpy()
+        assert np.array_equal(perm, og.act_order_perm(h, "diag_h"))
+
+
+def test_sgemm_matches_numpy():
+    from jax_gptq_b200 import _arrays as A
+    from jax_gptq_b200 import _lib
+    rng = np.random.default_rng(1)
+    for (M, N, K, ta, tb) in [(130, 70, 33, 0, 0), (64, 200, 129, 1, 0), (257, 129, 65, 0, 1),
+                              (5, 3, 700, 1, 1)]:
+        a = rng.standard_normal((K, M) if ta else (M, K)).astype(np.float32)
+        b = rng.standard_normal((N, K) if tb else (K, N)).astype(np.float32)
+        c = rng.standard_normal((M, N)).astype(np.float32)
+        ref = 0.5 * ((a.T if ta else a).astype(np.float64) @ (b.T if tb else b)) + 2.0 * c
+        at, bt, ct = (torch.from_numpy(v).cuda() for v in (a, b, c))
+        _lib.call("gq_sgemm", ta, tb, M, N, K, 0.5, A.ptr(at), at.shape[1], A.ptr(bt), bt.shape[1],
+                  2.0, A.ptr(ct), N, 0, A.stream())
+        assert np.allclose(ct.cpu().numpy(), ref, rtol=1e-4, atol=1e-4)
+
+
+def test_h_fp32_matches_oracle_within_1e5():
+    w, x = inputs.single_linear(0, m=64, n=1024, tokens=2048)
+    h, g = h_g_from_activations(x)
+    h64, _ = ost.h_g_from_activations(x)
+    ok, fro, worst = ost.h_tolerance_ok(h, h64, 1e-5)
+    assert ok, (fro, worst)
+    rng = np.random.default_rng(3)
+    xf = x + rng.standard_normal(x.shape).astype(np.float32)
+    h2, g2 = h_g_from_activations(x, xf)
+    _, g64 = ost.h_g_from_activations(x, xf)
+    assert np.linalg.norm(g2 - g64) / np.linalg.norm(g64) <= 1e-5
+
+
+@pytest.mark.parametrize("ordering", ["none", "diag_h"])
+def test_hessian_factor_matches_oracle(ordering):
+    w, x = inputs.single_linear(0, m=64, n=512, tokens=2048)
+    h = (x.astype(np.float64).T @ x / x.shape[0]).astype(np.float32)
+    cfg = QuantConfig(ordering_mode=ordering, semantics="intended")
+    f = G.factor_hessian(h, cfg, want_hd=True)
+    u64, perm64, att = og.process_hessian_intended(h, ordering, 0.01)
+    assert f.attempt == att == 0
+    assert np.array_equal(f.perm.cpu().numpy(), perm64)
+    u = f.u.cpu().numpy().astype(np.float64)
+    assert np.allclose(np.tril(u, -1), 0.0)
+    assert np.linalg.norm(u - u64) / np.linalg.norm(u64) < 2e-3
+    hd = f.hd.cpu().numpy().astype(np.float64)
+    ident = u @ hd @ u.T          # U Hd U^T = I  <=>  U^T U = Hd^-1
+    assert np.abs(ident - np.eye(512)).max() < 5e-3
+
+
+def test_hessian_factor_retries_damping_on_indefinite_input():
+    # a negative-definite direction that 1% damping cannot fix but 100x can
+    n = 128
+    h = np.eye(n, dtype=np.float32)
+    h[5, 5] = -0.5
+    cfg = QuantConfig(semantics="intended", damp_percent=0.01)
+    f = G.factor_hessian(h, cfg)
+    _, _, att = og.process_hessian_intended(h, "none", 0.01)
+    assert f.attempt == att and f.attempt >= 1
+
+
+def test_gptq_intended_reconstruction_matches_oracle():
+    w, x = inputs.single_linear(0, m=256, n=1024, tokens=2048)
+    h = (x.astype(np.float64).T @ x / x.shape[0])
+    cfg = QuantConfig(ordering_mode="diag_h", semantics="intended")
+    res = G.gptq_quantize(w, h.astype(np.float32), cfg)
+    u64, perm64, _ = og.process_hessian_intended(h, "diag_h", 0.01)
+    ref = og.gptq_sweep(w, u64, perm64, 4, 128, False, dtype=np.float64)
+    e_gpu = og.reconstruction_error(w, res.dequant.cpu().numpy(), h)
+    e_ref = og.reconstruction_error(w, ref["dequant"], h)
+    e_rtn = og.reconstruction_error(w, oq.quantize_dequantize(w, 4, 128), h)
+    assert abs(e_gpu - e_ref) <= 1e-3 * max(e_ref, 1e-12) + 2e-3 * e_ref, (e_gpu, e_ref)
+    assert e_gpu < e_rtn
+    codes = res.codes.cpu().numpy().astype(np.float32)
+    agree = np.mean(codes == ref["q"])
+    assert agree > 0.95, agree
+    assert np.array_equal(res.g_idx.cpu().numpy(), ref["g_idx"])
+
+
+def test_qronos_intended_matches_oracle():
+    w, x = inputs.single_linear(2, m=128, n=512, tokens=2048)
+    rng = np.random.default_rng(2)
+    xt = (x + rng.standard_normal(x.shape).astype(np.float32) * 0.05 * x.std(0)).astype(np.float32)
+    h, g = ost.h_g_from_activations(xt, x)
+    cfg = QuantConfig(w_bits=3, semantics="intended")
+    out = qronos_single_layer_update_ref(w, w, h.astype(np.float32), g.astype(np.float32), cfg)
+    ref = oqn.qronos_intended(w, w, h, g, 3, 128, False)
+
+    def err(w_hat):
+        return np.linalg.norm(x.astype(np.float64) @ w.T - xt.astype(np.float64) @ w_hat.T)
+    e_gpu, e_ref = err(out), err(ref["dequant"])
+    assert abs(e_gpu - e_ref) <= 5e-3 * e_ref, (e_gpu, e_ref)
+    assert e_gpu < err(oq.quantize_dequantize(w, 3, 128))
