@@ -67,6 +67,29 @@ int gq_sgemm(int trans_a, int trans_b, int64_t M, int64_t N, int64_t K, float al
              const float* a, int64_t lda, const float* b, int64_t ldb, float beta,
              float* c, int64_t ldc, int uplo, void* stream);
 
+/* ------------------------------------------------------------------------
+ * stats.py:4-18 h_g_from_activations, bf16 activations, fp32 accumulation
+ * on the tcgen05 tensor cores (TMEM accumulators, TMA-fed shared memory).
+ *
+ * x [tokens, d] bf16 (raw uint16 bits), row-major with ldx (elements, multiple
+ *   of 8), base 16-byte aligned.
+ * gq_syrk_bf16:    h[d, d] (+)= x^T x   (stats.py:16; full symmetric result)
+ * gq_gemm_tn_bf16: g[da, db] (+)= xa^T xb   (stats.py:17 with xa = x_float,
+ *                  xb = x_quant)
+ * accumulate = 0 overwrites, 1 adds to the existing contents (streamed
+ * calibration batches).  ldh/ldg are in elements.
+ */
+int gq_syrk_bf16(const uint16_t* x, int64_t tokens, int64_t d, int64_t ldx,
+                 float* h, int64_t ldh, int accumulate, void* stream);
+int gq_gemm_tn_bf16(const uint16_t* xa, int64_t lda, const uint16_t* xb, int64_t ldb,
+                    int64_t tokens, int64_t da, int64_t db,
+                    float* g, int64_t ldg, int accumulate, void* stream);
+
+/* Device status word written by kernels with bounded waits (0 = fine,
+ * 1 = a wait timed out, 2 = not positive definite).  BLOCKING: synchronizes
+ * the stream; reset = 1 clears the word afterwards. */
+int gq_device_status(int* status_out, int reset, void* stream);
+
 /* stats.py:4-18 for float32 activations (CUDA-core fp32 GEMM). */
 int gq_syrk_f32(const float* x, int64_t tokens, int64_t d, int64_t ldx,
                 float* h, int64_t ldh, int accumulate, void* stream);
