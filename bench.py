@@ -1,0 +1,447 @@
+"""Benchmark: quantize a Llama-2-7B-shaped decoder layer set on B200.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+One step = one layer set (q, k, v, o, gate, up, down) quantized with GPTQ
+(4-bit, group 128, act-order, damp 0.01): H = X^T X over 262,144 bf16 tokens
+for each of the four distinct layer inputs on the tcgen05 tensor cores, the
+damped inverse-Cholesky factor per input, and the seven column sweeps.
+Inputs are synthetic (seeded, generated on the device) and already resident
+in HBM when the timed region starts; they total 12.2 GB, far above the
+126 MB L2, so no flush is needed between steps.
+
+Under torchrun each rank quantizes its own layer set (layer parallelism:
+weak scaling, no data-path collective); ``value`` is seconds per layer for
+the whole job: max-over-ranks step time / layers processed by all ranks.
+
+Also reported: ``e2e`` (the same step through the host-buffer API
+``quantize_layer_gptq_host``: activations and weights copied from pinned
+host memory, codes/scales/zeros copied back, inside the timed region), the
+live roofline of the H-accumulation kernel, Qronos on the same layer set
+(3-bit), the pivoted-QR throughput, and a CPU baseline (the numpy oracle on
+a bounded sample, extrapolated).
+
+``--impl reference`` times the reference's own op sequence for this path
+(h = x^T x, the five Cholesky attempts its process_hessian makes before
+falling back, act-order, RTN) as a numpy port on the host cores, on a
+bounded sample, extrapolated to seconds per layer.
+"""
+
+from __future__ import annotations
+
+import argparse
+import datetime
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+TOKENS = 128 * 2048
+METRIC = "7B-layer-set GPTQ+Qronos s/layer; H-accum TFLOP/s; pivoted-QR GFLOP/s"
+WORKLOAD = "llama2-7b layer set (q,k,v,o 4096x4096; gate,up 11008x4096; down 4096x11008), " \
+           "GPTQ 4-bit g128 act-order damp 0.01, H over 262144 bf16 tokens"
+
+
+def _peaks():
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    try:
+        with open(path) as f:
+            p = json.load(f)
+        return p, "measured"
+    except Exception:
+        return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}, "fallback"
+
+
+class ClockSampler:
+    """nvidia-smi clock / throttle samples while the timed region runs."""
+
+    QUERY = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+             "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+             "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.gpu = gpu_index
+        self.proc = None
+        self.path = os.path.join(ROOT, "gpurun_out", f"clocks_gpu{gpu_index}.csv")
+
+    def start(self):
+        try:
+            os.makedirs(os.path.dirname(self.path), exist_ok=True)
+            self.fh = open(self.path, "w")
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.QUERY}",
+                 "--format=csv,noheader,nounits", "-lms", "200"], stdout=self.fh,
+                stderr=subprocess.DEVNULL)
+        except Exception:
+            self.proc = None
+
+    def stop(self):
+        if self.proc is None:
+            return None
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except Exception:
+            self.proc.kill()
+        self.fh.close()
+        sm, smax, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in open(self.path):
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                smax = float(parts[2])
+            except ValueError:
+                continue
+            for name, val in zip(names, parts[5:9]):
+                if val.lower() == "active":
+                    reasons.add(name)
+        if not sm:
+            return None
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": smax, "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+# ----------------------------------------------------------------------------- CPU side
+
+def _cpu_cores() -> int:
+    try:
+        return len(os.sched_getaffinity(0))
+    except Exception:
+        return os.cpu_count() or 1
+
+
+def _cpu_model() -> str:
+    try:
+        for line in open("/proc/cpuinfo"):
+            if line.startswith("model name"):
+                return line.split(":", 1)[1].strip()
+    except Exception:
+        pass
+    return "unknown"
+
+
+def reference_port_sample(shapes, sample_tokens=1024, sample_rows=512, chol_d=2048, seed=0):
+    """Time the reference's op sequence on a bounded sample; extrapolate to s/layer.
+
+    Per input group: h = x^T x (float32, stats.py:16) and the five Cholesky
+    attempts of process_hessian (gptq_ref.py:80-89; each raises after the
+    factorization, so the factorization cost is real), argsort of diag(h);
+    per linear: RTN of the permuted weights (gptq_ref.py:152-155).
+    """
+    from oracle import gptq as og
+    from oracle import quant as oq
+    rng = np.random.default_rng(seed)
+    total = 0.0
+    dims = {}
+    for _, _, n, grp in shapes:
+        dims[grp] = n
+    parts = {}
+    for grp, d in dims.items():
+        x = rng.standard_normal((sample_tokens, d)).astype(np.float32)
+        t0 = time.perf_counter()
+        h = x.T @ x
+        t_h = time.perf_counter() - t0
+        dc = min(chol_d, d)
+        hs = h[:dc, :dc] + np.float32(0.01) * np.mean(np.diag(h[:dc, :dc])) * np.eye(dc, dtype=np.float32)
+        t0 = time.perf_counter()
+        for _ in range(5):
+            np.linalg.cholesky(hs)
+        t_c = time.perf_counter() - t0
+        t0 = time.perf_counter()
+        og.act_order_perm(h, "diag_h")
+        t_p = time.perf_counter() - t0
+        est = t_h * (TOKENS / sample_tokens) + t_c * (d / dc) ** 3 + t_p
+        parts[f"stats+chol:{grp}"] = est
+        total += est
+    for name, m, n, grp in shapes:
+        rows = min(sample_rows, m)
+        w = (rng.standard_normal((rows, n)) * 0.02).astype(np.float32)
+        perm = rng.permutation(n)
+        t0 = time.perf_counter()
+        og.gptq_forward_step_reference(w, perm, 4, 128, False)
+        est = (time.perf_counter() - t0) * (m / rows)
+        parts[f"rtn:{name}"] = est
+        total += est
+    return total, parts, (f"h = x^T x on {sample_tokens} tokens per input (x{TOKENS // sample_tokens}),"
+                          f" 5 Cholesky attempts at d={chol_d} (x(d/{chol_d})^3), RTN on "
+                          f"{sample_rows} rows per linear (x m/{sample_rows})")
+
+
+def intended_port_sample(shapes, sample_tokens=2048, sample_rows=64, chol_d=1024, seed=0):
+    """The oracle's intended GPTQ (the work the GPU step does) on a bounded sample."""
+    from oracle import gptq as og
+    rng = np.random.default_rng(seed + 1)
+    total = 0.0
+    dims = {}
+    for _, _, n, grp in shapes:
+        dims[grp] = n
+    for grp, d in dims.items():
+        x = rng.standard_normal((sample_tokens, d)).astype(np.float32)
+        t0 = time.perf_counter()
+        h = x.T @ x
+        t_h = time.perf_counter() - t0
+        dc = min(chol_d, d)
+        t0 = time.perf_counter()
+        og.process_hessian_intended(h[:dc, :dc].astype(np.float64) + np.eye(dc), "diag_h", 0.01,
+                                    dtype=np.float32)
+        t_f = time.perf_counter() - t0
+        total += t_h * (TOKENS / sample_tokens) + t_f * (d / dc) ** 3
+    for name, m, n, grp in shapes:
+        rows = min(sample_rows, m)
+        w = (rng.standard_normal((rows, n)) * 0.02).astype(np.float32)
+        u = np.triu(rng.standard_normal((n, n)).astype(np.float32) * 1e-3) + np.eye(n, dtype=np.float32)
+        t0 = time.perf_counter()
+        og.gptq_sweep(w, u, np.arange(n), 4, 128, False, 128, np.float32)
+        total += (time.perf_counter() - t0) * (m / rows)
+    return total, (f"oracle intended GPTQ: H on {sample_tokens} tokens/input (x{TOKENS // sample_tokens}),"
+                   f" damped factor at d={chol_d} (x(d/{chol_d})^3), sweep on {sample_rows} rows per "
+                   f"linear (x m/{sample_rows})")
+
+
+# ----------------------------------------------------------------------------- distributed
+
+def _dist_init():
+    import torch
+    import torch.distributed as dist
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1:
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
+                                device_id=torch.device("cuda", local))
+    else:
+        torch.cuda.set_device(0)
+    return world, rank, local
+
+
+def _barrier(world):
+    import torch
+    import torch.distributed as dist
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+
+
+def _max_over_ranks(v: float, world: int) -> float:
+    if world <= 1:
+        return v
+    import torch
+    import torch.distributed as dist
+    t = torch.tensor([v], dtype=torch.float64, device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+# ----------------------------------------------------------------------------- arms
+
+def run_reference(args, world, rank):
+    if rank != 0:
+        return
+    from jax_gptq_b200.layerset import LLAMA2_7B
+    times, samples = [], None
+    for i in range(args.warmup + args.steps):
+        t, parts, samples = reference_port_sample(LLAMA2_7B, seed=i)
+        if i >= args.warmup:
+            times.append(t)
+    v = statistics.mean(times)
+    cores = _cpu_cores()
+    line = {
+        "impl": "reference", "metric": METRIC, "value": v, "unit": "s/layer", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": v * 1000.0,
+        "higher_is_better": False, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic", "config": {"workload": WORKLOAD, "tokens": TOKENS},
+        "cpu_baseline": {"value": v, "unit": "s/layer", "cores": cores, "kind": "port",
+                         "sample": samples, "cpu": _cpu_model()},
+        "e2e": {"value": v, "unit": "s/layer", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        "note": "numpy port of the reference's own CPU op sequence (JAX is not installable "
+                "offline); BLAS threads = all host cores",
+    }
+    print(json.dumps(line), flush=True)
+
+
+def run_ours(args, world, rank, local):
+    import torch
+    from jax_gptq_b200 import _lib
+    from jax_gptq_b200 import layerset as LS
+    from jax_gptq_b200 import stats
+    from jax_gptq_b200.config import QuantConfig
+
+    _lib.lib()
+    peaks, peak_kind = _peaks()
+    shapes = LS.LLAMA2_7B
+    dims = LS.group_dims(shapes)
+    seed = 1000 * rank
+    cfg = QuantConfig(w_bits=4, group_size=128, sym=False, damp_percent=0.01,
+                      ordering_mode="diag_h", semantics="intended")
+    weights = LS.synth_weights(shapes, 0.02, seed)
+    inputs, stds = {}, {}
+    for i, (grp, d) in enumerate(dims.items()):
+        inputs[grp], stds[grp] = LS.synth_activations(args.tokens, d, seed + 10 + i)
+    torch.cuda.synchronize()
+
+    # --- headline: device-resident GPTQ layer set
+    for _ in range(args.warmup):
+        LS.quantize_layer_gptq(weights, inputs, cfg, shapes)
+    sampler = ClockSampler(local)
+    _barrier(world)
+    sampler.start()
+    launches0 = _lib.lib().gq_launch_count()
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(args.steps):
+        LS.quantize_layer_gptq(weights, inputs, cfg, shapes)
+    e1.record()
+    _barrier(world)
+    launches = (_lib.lib().gq_launch_count() - launches0) // max(args.steps, 1)
+    clocks = sampler.stop()
+    ms = _max_over_ranks(e0.elapsed_time(e1) / args.steps, world)
+    s_per_layer = ms / 1000.0 / world
+
+    # --- phase breakdown (one extra timed step)
+    _, phases = LS.quantize_layer_gptq(weights, inputs, cfg, shapes, timed=True)
+
+    # --- roofline of the H-accumulation kernel (tcgen05), timed live on its stream
+    syrk_ms, syrk_flop = [], []
+    for grp, x in inputs.items():
+        d = x.shape[1]
+        h = torch.empty((d, d), dtype=torch.float32, device="cuda")
+        for _ in range(2):
+            stats.syrk_into(h, x, accumulate=False)
+        a = torch.cuda.Event(enable_timing=True)
+        b = torch.cuda.Event(enable_timing=True)
+        a.record()
+        reps = 3
+        for _ in range(reps):
+            stats.syrk_into(h, x, accumulate=False)
+        b.record()
+        torch.cuda.synchronize()
+        syrk_ms.append(a.elapsed_time(b) / reps)
+        syrk_flop.append(LS.syrk_flops(args.tokens, d))
+        del h
+    h_tflops = sum(syrk_flop) / (sum(syrk_ms) / 1e3) / 1e12
+    peak = peaks.get("bf16_tflops_sustained", peaks.get("bf16_tflops"))
+    roofline = {"bound": "tensor", "kernel": "gq_tc gemm_tn_kernel (H = X^T X, symmetric tiles)",
+                "achieved": h_tflops, "peak": peak, "unit": "TFLOP/s", "frac": h_tflops / peak,
+                "peak_kind": f"{peak_kind} bf16 sustained (kernel timed inside a long step)",
+                "algorithmic": "tokens*d*(d+1) flops per launch", "traffic": args.syrk_traffic}
+
+    # --- e2e through the host-buffer API
+    e2e = None
+    if not args.no_e2e:
+        w_host = {k: v.cpu().pin_memory() for k, v in weights.items()}
+        x_host = {k: v.cpu().pin_memory() for k, v in inputs.items()}
+        for _ in range(max(1, min(args.warmup, 2))):
+            LS.quantize_layer_gptq_host(w_host, x_host, cfg, shapes)
+        _barrier(world)
+        a = torch.cuda.Event(enable_timing=True)
+        b = torch.cuda.Event(enable_timing=True)
+        a.record()
+        for _ in range(args.steps):
+            out, nbytes = LS.quantize_layer_gptq_host(w_host, x_host, cfg, shapes)
+        b.record()
+        _barrier(world)
+        e2e_ms = _max_over_ranks(a.elapsed_time(b) / args.steps, world)
+        e2e = {"value": e2e_ms / 1000.0 / world, "unit": "s/layer",
+               "h2d_bytes_per_step": nbytes["h2d"], "d2h_bytes_per_step": nbytes["d2h"]}
+        del w_host, x_host
+
+    # --- Qronos on the same layer set (3-bit), Xt = X + N(0, (0.05 sigma_c)^2)
+    qronos = None
+    if not args.no_qronos:
+        qcfg = QuantConfig(w_bits=3, group_size=128, sym=False, damp_percent=0.01,
+                           ordering_mode="diag_h", semantics="intended")
+        xq = {g: LS.perturb_activations(inputs[g], stds[g], 0.05, seed + 50 + i)
+              for i, g in enumerate(inputs)}
+        LS.quantize_layer_qronos(weights, inputs, xq, qcfg, shapes)
+        _barrier(world)
+        a = torch.cuda.Event(enable_timing=True)
+        b = torch.cuda.Event(enable_timing=True)
+        a.record()
+        qsteps = max(1, min(args.steps, 3))
+        for _ in range(qsteps):
+            LS.quantize_layer_qronos(weights, inputs, xq, qcfg, shapes)
+        b.record()
+        _barrier(world)
+        q_ms = _max_over_ranks(a.elapsed_time(b) / qsteps, world)
+        _, qph = LS.quantize_layer_qronos(weights, inputs, xq, qcfg, shapes, timed=True)
+        qronos = {"s_per_layer": q_ms / 1000.0 / world, "steps": qsteps,
+                  "phases_ms": {"h_and_g": qph.stats_ms, "factor": qph.factor_ms,
+                                "qronos_sweeps": qph.sweep_ms}}
+        del xq
+
+    # --- blocked pivoted QR (4096 x 4096 fp32, panel 64)
+    qr = None
+    if not args.no_qr:
+        try:
+            from jax_gptq_b200.pallas import blocked_pivoted_qr as BQ
+            qr = BQ.benchmark(n=4096, panel=64, reps=2)
+        except Exception as exc:  # report, do not hide
+            qr = {"error": repr(exc)[:200]}
+
+    cpu = None
+    if rank == 0 and not args.no_cpu_baseline:
+        v, sample = intended_port_sample(shapes)
+        cpu = {"value": v, "unit": "s/layer", "cores": _cpu_cores(), "kind": "port",
+               "sample": sample, "cpu": _cpu_model()}
+
+    if rank == 0:
+        line = {
+            "metric": METRIC, "value": s_per_layer, "unit": "s/layer", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
+            "higher_is_better": False, "scaling": "weak", "vs_baseline": None,
+            "dtype": "bf16 in / f32 accumulate (H); f32 sweep", "data": "synthetic",
+            "config": {"workload": WORKLOAD, "tokens": args.tokens, "layers_per_rank": 1,
+                       "parallelism": f"layer-parallel x{world}",
+                       "l2": "inputs (12.2 GB) larger than L2; no flush"},
+            "phases_ms": {"h_accum": phases.stats_ms, "factor": phases.factor_ms,
+                          "sweeps": phases.sweep_ms, "h_by_group": phases.per_group_stats_ms},
+            "h_accum": {"tflops": h_tflops, "ms_by_group": dict(zip(dims, syrk_ms))},
+            "roofline": roofline, "e2e": e2e, "gpu_launches": int(launches), "clocks": clocks,
+            "qronos": qronos, "qr": qr, "cpu_baseline": cpu,
+        }
+        print(json.dumps(line), flush=True)
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=5)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--tokens", type=int, default=TOKENS)
+    ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-qronos", action="store_true")
+    ap.add_argument("--no-qr", action="store_true")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--syrk-traffic", type=float, default=None,
+                    help="DRAM bytes per H-accumulation launch from an ncu capture")
+    args = ap.parse_args()
+    if args.impl == "reference":
+        world = int(os.environ.get("WORLD_SIZE", "1"))
+        rank = int(os.environ.get("RANK", "0"))
+        run_reference(args, world, rank)
+        return
+    world, rank, local = _dist_init()
+    try:
+        run_ours(args, world, rank, local)
+    finally:
+        if world > 1:
+            import torch.distributed as dist
+            dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

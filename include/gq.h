@@ -37,6 +37,10 @@ int gq_version(void);
 /* Message for the most recent failing call on this host thread. */
 const char* gq_last_error(void);
 
+/* Number of kernels this library has launched since it was loaded
+ * (instrumentation; no reference counterpart). */
+long long gq_launch_count(void);
+
 /* ------------------------------------------------------------------------
  * quant.py:6-37 quantize_dequantize, and the RTN core of
  * gptq_ref.py:152-155 gptq_forward_step (permute -> RTN -> un-permute).

@@ -26,6 +26,7 @@ _P = c_void_p
 SIGNATURES = {
     "gq_version": (c_int, []),
     "gq_last_error": (ctypes.c_char_p, []),
+    "gq_launch_count": (ctypes.c_longlong, []),
     "gq_rtn": (c_int, [_P, c_int64, c_int64, c_int64, _P, c_int, c_int, c_int, _P, _P, _P, _P, _P]),
     "gq_sgemm": (c_int, [c_int, c_int, c_int64, c_int64, c_int64, c_float, _P, c_int64, _P, c_int64,
                          c_float, _P, c_int64, c_int, _P]),

@@ -1,11 +1,15 @@
 // Library-wide plumbing: error strings, version, device properties.
 #include "gq_common.cuh"
 
+#include <atomic>
 #include <cstring>
 
 namespace gq {
 
 static thread_local char g_last_error[1024] = "";
+static std::atomic<long long> g_launches{0};
+
+void note_launch() { g_launches.fetch_add(1, std::memory_order_relaxed); }
 
 void set_error(const char* fmt, ...) {
   va_list ap;
@@ -63,6 +67,8 @@ extern "C" {
 int gq_version(void) { return 100; }
 
 const char* gq_last_error(void) { return gq::last_error(); }
+
+long long gq_launch_count(void) { return gq::g_launches.load(std::memory_order_relaxed); }
 
 int gq_symmetrize_upper(float* h, int64_t d, int64_t ldh, void* stream) {
   GQ_REQUIRE(h != nullptr && d >= 0 && ldh >= d, "gq_symmetrize_upper: bad arguments (d=%lld ldh=%lld)",

@@ -25,7 +25,12 @@ inline int fail(int status, const char* fmt, ...) {
   return status;
 }
 
+// Count of kernels this library has launched (every launch site calls
+// check_launch right after the launch); read with gq_launch_count().
+void note_launch();
+
 inline int check_launch(const char* what) {
+  note_launch();
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) {
     return fail(GQ_ECUDA, "%s: %s", what, cudaGetErrorString(e));

@@ -1,0 +1,283 @@
+"""Decoder-layer-set quantization on one GPU: the whole hot path per layer.
+
+A layer set is the seven linears of a Llama-style decoder block, grouped by
+the activation that feeds them (q/k/v share the attention input, gate/up
+share the MLP input):
+
+* per input group: ``H = X^T X`` on the tcgen05 tensor cores (and for
+  Qronos ``G = X^T Xt``), act-order permutation, damped inverse-Cholesky
+  factor -- computed once and shared by the group's linears;
+* per linear: the GPTQ (or Qronos) column sweep.
+
+Shapes follow the benchmark configurations (Llama-2-7B and Llama-3-70B
+blocks).  Inputs are synthetic and generated on the device with seeded
+torch generators.
+"""
+
+from __future__ import annotations
+
+import math
+from dataclasses import dataclass, field
+
+import torch
+
+from . import stats
+from .config import QuantConfig
+from .gptq_ref import HessianFactor, SweepResult, factor_hessian, gptq_sweep
+from .qronos_ref import qronos_quantize
+
+# (name, out_features, in_features, input group)
+LLAMA2_7B = [
+    ("q_proj", 4096, 4096, "attn_in"), ("k_proj", 4096, 4096, "attn_in"),
+    ("v_proj", 4096, 4096, "attn_in"), ("o_proj", 4096, 4096, "attn_out"),
+    ("gate_proj", 11008, 4096, "mlp_in"), ("up_proj", 11008, 4096, "mlp_in"),
+    ("down_proj", 4096, 11008, "mlp_out"),
+]
+LLAMA3_70B = [
+    ("q_proj", 8192, 8192, "attn_in"), ("k_proj", 1024, 8192, "attn_in"),
+    ("v_proj", 1024, 8192, "attn_in"), ("o_proj", 8192, 8192, "attn_out"),
+    ("gate_proj", 28672, 8192, "mlp_in"), ("up_proj", 28672, 8192, "mlp_in"),
+    ("down_proj", 8192, 28672, "mlp_out"),
+]
+SHAPES = {"llama2-7b": LLAMA2_7B, "llama3-70b": LLAMA3_70B}
+
+
+def group_dims(shapes) -> dict[str, int]:
+    dims: dict[str, int] = {}
+    for _, _, n, grp in shapes:
+        dims[grp] = n
+    return dims
+
+
+def syrk_flops(tokens: int, d: int) -> float:
+    """Algorithmic flops of ``H = X^T X`` counted as a symmetric rank-k update."""
+    return float(tokens) * d * (d + 1)
+
+
+def gemm_flops(tokens: int, d: int) -> float:
+    return 2.0 * tokens * d * d
+
+
+def synth_weights(shapes, std: float, seed: int, device="cuda") -> dict[str, torch.Tensor]:
+    """bf16 N(0, std^2) weights, upcast exactly to float32."""
+    gen = torch.Generator(device=device).manual_seed(seed)
+    out = {}
+    for name, m, n, _ in shapes:
+        w = torch.randn((m, n), generator=gen, device=device, dtype=torch.float32) * std
+        out[name] = w.to(torch.bfloat16).to(torch.float32)
+    return out
+
+
+def synth_activations(tokens: int, d: int, seed: int, kind: str = "lognormal",
+                      device="cuda", chunk: int = 32768):
+    """bf16 [tokens, d] calibration activations and their per-channel std.
+
+    ``lognormal``: N(0, 1) times a per-channel log-normal(0, 1) scale;
+    ``student_t``: Student-t with 4 degrees of freedom.
+    """
+    gen = torch.Generator(device=device).manual_seed(seed)
+    x = torch.empty((tokens, d), dtype=torch.bfloat16, device=device)
+    if kind == "lognormal":
+        scale = torch.exp(torch.randn((d,), generator=gen, device=device))
+    else:
+        scale = torch.ones((d,), device=device)
+    for t0 in range(0, tokens, chunk):
+        t1 = min(tokens, t0 + chunk)
+        z = torch.randn((t1 - t0, d), generator=gen, device=device)
+        if kind == "student_t":
+            # t_4 = Z / sqrt(chi2_4 / 4), chi2_4 = sum of 4 squared normals
+            chi = torch.zeros((t1 - t0, d), device=device)
+            for _ in range(4):
+                chi += torch.randn((t1 - t0, d), generator=gen, device=device) ** 2
+            z = z / torch.sqrt(chi / 4.0)
+        x[t0:t1] = (z * scale).to(torch.bfloat16)
+    std = scale if kind == "lognormal" else torch.full((d,), math.sqrt(2.0), device=device)
+    return x, std
+
+
+def perturb_activations(x: torch.Tensor, std: torch.Tensor, rel: float, seed: int,
+                        chunk: int = 32768) -> torch.Tensor:
+    """``Xt = X + N(0, (rel * sigma_c)^2)``: stand-in for quantized-model activations."""
+    gen = torch.Generator(device=x.device).manual_seed(seed)
+    out = torch.empty_like(x)
+    for t0 in range(0, x.shape[0], chunk):
+        t1 = min(x.shape[0], t0 + chunk)
+        noise = torch.randn((t1 - t0, x.shape[1]), generator=gen, device=x.device) * (rel * std)
+        out[t0:t1] = (x[t0:t1].float() + noise).to(torch.bfloat16)
+    return out
+
+
+@dataclass
+class LayerTimes:
+    """Milliseconds per phase (CUDA events on the compute stream)."""
+    stats_ms: float = 0.0
+    factor_ms: float = 0.0
+    sweep_ms: float = 0.0
+    per_group_stats_ms: dict = field(default_factory=dict)
+
+
+class _Timer:
+    def __init__(self, enabled: bool):
+        self.enabled = enabled
+        self.marks = []
+
+    def mark(self, label: str):
+        if self.enabled:
+            ev = torch.cuda.Event(enable_timing=True)
+            ev.record()
+            self.marks.append((label, ev))
+
+    def spans(self) -> list[tuple[str, float]]:
+        if not self.enabled:
+            return []
+        torch.cuda.synchronize()
+        out = []
+        for (l0, e0), (_, e1) in zip(self.marks, self.marks[1:]):
+            out.append((l0, e0.elapsed_time(e1)))
+        return out
+
+
+def quantize_layer_gptq(weights: dict, inputs: dict, cfg: QuantConfig, shapes=LLAMA2_7B,
+                        timed: bool = False):
+    """GPTQ for every linear of a layer set.  ``inputs[group]`` = bf16 X on the device."""
+    tm = _Timer(timed)
+    factors: dict[str, HessianFactor] = {}
+    for grp, x in inputs.items():
+        tm.mark(f"stats:{grp}")
+        d = x.shape[1]
+        h = torch.empty((d, d), dtype=torch.float32, device=x.device)
+        stats.syrk_into(h, x, accumulate=False)
+        tm.mark(f"factor:{grp}")
+        factors[grp] = factor_hessian(h, cfg)
+        del h
+    results: dict[str, SweepResult] = {}
+    for name, _, _, grp in shapes:
+        tm.mark(f"sweep:{name}")
+        f = factors[grp]
+        results[name] = gptq_sweep(weights[name], f.u, f.perm, cfg)
+    tm.mark("end")
+    return results, _collect(tm)
+
+
+def quantize_layer_qronos(weights: dict, inputs_float: dict, inputs_quant: dict,
+                          cfg: QuantConfig, shapes=LLAMA2_7B, timed: bool = False):
+    """Qronos for every linear: ``h = Xt^T Xt``, ``g = X^T Xt`` per input group."""
+    tm = _Timer(timed)
+    facts = {}
+    for grp, xq in inputs_quant.items():
+        tm.mark(f"stats:{grp}")
+        d = xq.shape[1]
+        h = torch.empty((d, d), dtype=torch.float32, device=xq.device)
+        g = torch.empty((d, d), dtype=torch.float32, device=xq.device)
+        stats.syrk_into(h, xq, accumulate=False)
+        stats.gemm_tn_into(g, inputs_float[grp], xq, accumulate=False)
+        tm.mark(f"factor:{grp}")
+        facts[grp] = (factor_hessian(h, cfg, want_hd=True), g)
+        del h
+    results = {}
+    for name, _, _, grp in shapes:
+        tm.mark(f"sweep:{name}")
+        f, g = facts[grp]
+        w = weights[name]
+        results[name] = qronos_quantize(w, w, None, g, cfg, factor=f)
+    tm.mark("end")
+    return results, _collect(tm)
+
+
+_COPY_STREAMS: dict[int, tuple] = {}
+
+
+def _copy_streams():
+    dev = torch.cuda.current_device()
+    if dev not in _COPY_STREAMS:
+        _COPY_STREAMS[dev] = (torch.cuda.Stream(), torch.cuda.Stream())
+    return _COPY_STREAMS[dev]
+
+
+def quantize_layer_gptq_host(weights_host: dict, inputs_host: dict, cfg: QuantConfig,
+                             shapes=LLAMA2_7B):
+    """GPTQ layer set from host buffers to host results.
+
+    Activations (bf16) and weights (float32) are copied from (pinned) host
+    memory on a copy stream in the order the computation needs them, so the
+    transfer of the next input group overlaps the tensor-core work on the
+    current one; codes, scales and zeros stream back on a second copy stream.
+    Returns ``({name: (codes, scales, zeros, g_idx, perm)}, {"h2d": bytes,
+    "d2h": bytes})`` with host tensors.
+    """
+    compute = torch.cuda.current_stream()
+    h2d, d2h = _copy_streams()
+    start = torch.cuda.Event()
+    start.record(compute)
+    h2d.wait_event(start)
+    nbytes = {"h2d": 0, "d2h": 0}
+    dev_x, dev_w, ready_x, ready_w = {}, {}, {}, {}
+    order = []
+    for grp in inputs_host:
+        order.append(("x", grp))
+        for name, _, _, g in shapes:
+            if g == grp:
+                order.append(("w", name))
+    with torch.cuda.stream(h2d):
+        for kind, key in order:
+            src = inputs_host[key] if kind == "x" else weights_host[key]
+            dst = torch.empty(src.shape, dtype=src.dtype, device="cuda")
+            dst.copy_(src, non_blocking=True)
+            ev = torch.cuda.Event()
+            ev.record(h2d)
+            nbytes["h2d"] += src.numel() * src.element_size()
+            if kind == "x":
+                dev_x[key], ready_x[key] = dst, ev
+            else:
+                dev_w[key], ready_w[key] = dst, ev
+    factors = {}
+    results = {}
+    out = {}
+    for grp in inputs_host:
+        compute.wait_event(ready_x[grp])
+        x = dev_x[grp]
+        x.record_stream(compute)
+        d = x.shape[1]
+        h = torch.empty((d, d), dtype=torch.float32, device="cuda")
+        stats.syrk_into(h, x, accumulate=False)
+        factors[grp] = factor_hessian(h, cfg)
+        del h
+        for name, _, _, g in shapes:
+            if g != grp:
+                continue
+            compute.wait_event(ready_w[name])
+            w = dev_w[name]
+            w.record_stream(compute)
+            f = factors[grp]
+            res = gptq_sweep(w, f.u, f.perm, cfg)
+            results[name] = res
+            done = torch.cuda.Event()
+            done.record(compute)
+            d2h.wait_event(done)
+            with torch.cuda.stream(d2h):
+                host = []
+                for t in (res.codes, res.scales, res.zeros, res.g_idx, res.perm):
+                    t.record_stream(d2h)
+                    hb = torch.empty(t.shape, dtype=t.dtype, pin_memory=True)
+                    hb.copy_(t, non_blocking=True)
+                    nbytes["d2h"] += t.numel() * t.element_size()
+                    host.append(hb)
+                out[name] = tuple(host)
+    fin = torch.cuda.Event()
+    fin.record(d2h)
+    compute.wait_event(fin)
+    return out, nbytes
+
+
+def _collect(tm: _Timer) -> LayerTimes:
+    t = LayerTimes()
+    for label, ms in tm.spans():
+        kind, _, what = label.partition(":")
+        if kind == "stats":
+            t.stats_ms += ms
+            t.per_group_stats_ms[what] = ms
+        elif kind == "factor":
+            t.factor_ms += ms
+        elif kind == "sweep":
+            t.sweep_ms += ms
+    return t
