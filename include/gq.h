@@ -155,6 +155,28 @@ int gq_gptq_sweep(const float* w, int64_t m, int64_t n, int64_t ldw, const float
                   int32_t* g_idx, void* workspace, int64_t workspace_bytes, void* stream);
 
 /* ------------------------------------------------------------------------
+ * No counterpart in the reference.  gq_gptq_sweep for callers that cannot
+ * allocate device memory -- e.g. a host framework that has reserved nearly
+ * all GPU memory for its own pool, so that a cudaMalloc from a plugin fails,
+ * with no way for the plugin to borrow from that pool.  Same arguments and
+ * results as gq_gptq_sweep minus the workspace: the scratch comes from one
+ * static device buffer of GQ_SWEEP_STATIC_SCRATCH_BYTES per GPU, held until
+ * the process exits.  Sweeps needing more scratch than that
+ * (gq_gptq_sweep_workspace_size(m, n) > GQ_SWEEP_STATIC_SCRATCH_BYTES,
+ * roughly 6 million weights) return GQ_EINVAL.  All calls on a device share the
+ * buffer: calls that may overlap on the GPU race and must be ordered.  The
+ * first call on each device looks up the buffer's address; make it before any
+ * stream capture begins.
+ */
+#define GQ_SWEEP_STATIC_SCRATCH_BYTES (32ll * 1024 * 1024)
+int gq_gptq_sweep_static(const float* w, int64_t m, int64_t n, int64_t ldw, const float* start,
+                         const float* u, int64_t ldu, const int32_t* perm,
+                         int w_bits, int group_size, int sym, int block,
+                         const float* group0_scale, const float* group0_zero, int noprop_cols,
+                         float* dequant, uint8_t* codes, float* scales, float* zeros,
+                         int32_t* g_idx, void* stream);
+
+/* ------------------------------------------------------------------------
  * Qronos update (the computation qronos_ref.py:7-25 stands in for), with
  * h = Xt^T Xt from the quantized-model activations Xt and g = X^T Xt
  * (h_g_from_activations(x_quant=Xt, x_float=X)).

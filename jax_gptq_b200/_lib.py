@@ -45,6 +45,8 @@ SIGNATURES = {
     "gq_gptq_sweep": (c_int, [_P, c_int64, c_int64, c_int64, _P, _P, c_int64, _P, c_int, c_int, c_int,
                               c_int, _P, _P, c_int, _P, _P, _P, _P, _P, _P, c_int64, _P]),
     "gq_device_status": (c_int, [ctypes.POINTER(c_int), c_int, _P]),
+    "gq_gptq_sweep_static": (c_int, [_P, c_int64, c_int64, c_int64, _P, _P, c_int64, _P, c_int,
+                                     c_int, c_int, c_int, _P, _P, c_int, _P, _P, _P, _P, _P, _P]),
     "gq_qronos_workspace_size": (c_int64, [c_int64, c_int64]),
     "gq_qronos": (c_int, [_P, _P, c_int64, c_int64, _P, _P, _P, _P, c_int, c_int, c_int, c_int, _P,
                           _P, _P, _P, _P, _P, c_int64, _P]),
