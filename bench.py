@@ -271,6 +271,31 @@ def run_reference(args, world, rank):
     print(json.dumps(line), flush=True)
 
 
+def run_kernel_only(args):
+    """``--only syrk``: just the H-accumulation kernel on [tokens, dim] (profiling runs)."""
+    import torch
+    from jax_gptq_b200 import _lib
+    from jax_gptq_b200 import layerset as LS
+    from jax_gptq_b200 import stats
+    _lib.lib()
+    x, _ = LS.synth_activations(args.tokens, args.dim, 7)
+    h = torch.empty((args.dim, args.dim), dtype=torch.float32, device="cuda")
+    for _ in range(args.warmup):
+        stats.syrk_into(h, x, accumulate=False)
+    a = torch.cuda.Event(enable_timing=True)
+    b = torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize()
+    a.record()
+    for _ in range(args.steps):
+        stats.syrk_into(h, x, accumulate=False)
+    b.record()
+    torch.cuda.synchronize()
+    ms = a.elapsed_time(b) / max(args.steps, 1)
+    tf = LS.syrk_flops(args.tokens, args.dim) / (ms / 1e3) / 1e12
+    print(json.dumps({"kernel": "syrk", "tokens": args.tokens, "d": args.dim, "ms": ms,
+                      "tflops": tf}), flush=True)
+
+
 def run_ours(args, world, rank, local):
     import torch
     from jax_gptq_b200 import _lib
@@ -428,7 +453,15 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--syrk-traffic", type=float, default=None,
                     help="DRAM bytes per H-accumulation launch from an ncu capture")
+    ap.add_argument("--only", choices=["all", "syrk"], default="all",
+                    help="syrk: time only the H kernel on [--tokens, --dim] (profiling)")
+    ap.add_argument("--dim", type=int, default=4096)
     args = ap.parse_args()
+    if args.only == "syrk":
+        import torch
+        torch.cuda.set_device(0)
+        run_kernel_only(args)
+        return
     if args.impl == "reference":
         world = int(os.environ.get("WORLD_SIZE", "1"))
         rank = int(os.environ.get("RANK", "0"))
