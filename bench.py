@@ -411,7 +411,8 @@ def run_ours(args, world, rank, local):
     qr = None
     if not args.no_qr:
         try:
-            from jax_gptq_b200.pallas import blocked_pivoted_qr as BQ
+            import importlib
+            BQ = importlib.import_module("jax_gptq_b200.pallas.blocked_pivoted_qr")
             qr = BQ.benchmark(n=4096, panel=64, reps=2)
         except Exception as exc:  # report, do not hide
             qr = {"error": repr(exc)[:200]}
@@ -453,14 +454,22 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--syrk-traffic", type=float, default=None,
                     help="DRAM bytes per H-accumulation launch from an ncu capture")
-    ap.add_argument("--only", choices=["all", "syrk"], default="all",
-                    help="syrk: time only the H kernel on [--tokens, --dim] (profiling)")
+    ap.add_argument("--only", choices=["all", "syrk", "qr"], default="all",
+                    help="syrk: time only the H kernel on [--tokens, --dim]; qr: only the "
+                         "pivoted QR on a --dim x --dim matrix (profiling)")
     ap.add_argument("--dim", type=int, default=4096)
+    ap.add_argument("--panel", type=int, default=64)
     args = ap.parse_args()
-    if args.only == "syrk":
+    if args.only in ("syrk", "qr"):
         import torch
         torch.cuda.set_device(0)
-        run_kernel_only(args)
+        if args.only == "syrk":
+            run_kernel_only(args)
+        else:
+            import importlib
+            BQ = importlib.import_module("jax_gptq_b200.pallas.blocked_pivoted_qr")
+            print(json.dumps({"kernel": "qr", **BQ.benchmark(n=args.dim, panel=args.panel,
+                                                            reps=max(1, args.steps))}), flush=True)
         return
     if args.impl == "reference":
         world = int(os.environ.get("WORLD_SIZE", "1"))

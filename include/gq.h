@@ -192,6 +192,42 @@ int gq_qronos(const float* w, const float* w_orig, int64_t m, int64_t n, const f
               int sym, int block, float* dequant, uint8_t* codes, float* scales, float* zeros,
               int32_t* g_idx, void* workspace, int64_t workspace_bytes, void* stream);
 
+/* ------------------------------------------------------------------------
+ * pallas/blocked_pivoted_qr.py:1627-1722 blocked_pivoted_qr: column-pivoted
+ * Householder QR of a [m, n] float32 (lda), in place: on return a holds R in
+ * its upper triangle and explicit zeros below (like the reference's `work`),
+ * perm [n] int32 the column order.  pivot_mode 0 = "largest", 1 = "smallest".
+ * semantics 0 reproduces the reference's compiled panel path exactly (index
+ * quirks and stale mid-panel pivots included); 1 is a correct blocked QRCP
+ * (A[:, perm] = Q R, run in 64-wide panels).  panel_size <= 256 or >= min(m, n);
+ * m <= 25600.  Optional outputs: v_out [m, min(m, n)] (ldv) the Householder
+ * vectors (unit diagonal, zeros above), tau_out [min(m, n)], panel_ends and
+ * n_panels the realized panel boundaries.  BLOCKING: synchronizes the stream
+ * once per panel.
+ */
+int64_t gq_qrcp_workspace_size(int64_t m, int64_t n, int panel_size);
+int gq_qrcp(float* a, int64_t m, int64_t n, int64_t lda, int panel_size, int pivot_mode,
+            int semantics, int32_t* perm, float* v_out, int64_t ldv, float* tau_out,
+            int32_t* panel_ends, int* n_panels, void* workspace, int64_t workspace_bytes,
+            void* stream);
+
+/* pallas/blocked_pivoted_qr.py:1412-1476 factor_panel_pallas: one panel from
+ * column k, updating a, perm and norms in place; y_out [m - k, P] (ld P),
+ * tau_out [P], t_out [P, P] with P = min(panel_size, min(m, n) - k);
+ * *panel_end_out = k + accepted reflectors.  BLOCKING (one sync). */
+int gq_qr_factor_panel(float* a, int64_t m, int64_t n, int64_t lda, int32_t* perm, float* norms,
+                       int64_t k, int panel_size, int pivot_mode, int semantics, float* y_out,
+                       float* tau_out, float* t_out, int* panel_end_out, void* workspace,
+                       int64_t workspace_bytes, void* stream);
+
+/* pallas/blocked_pivoted_qr.py:818-862 apply_compact_panel_to_block (and
+ * :1592-1624 apply_panel_to_trailing_pallas on the block a[k:, panel_end:]):
+ * b [rows, cols] <- b - Y (T^T (Y^T b)) with y [rows, width] (ldy),
+ * t [width, width] (ldt).  scratch: 2 * width * cols floats. */
+int gq_qr_apply_panel(float* b, int64_t rows, int64_t cols, int64_t ldb, const float* y,
+                      int64_t ldy, const float* t, int64_t ldt, int width, float* scratch,
+                      void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -47,6 +47,13 @@ SIGNATURES = {
     "gq_device_status": (c_int, [ctypes.POINTER(c_int), c_int, _P]),
     "gq_gptq_sweep_static": (c_int, [_P, c_int64, c_int64, c_int64, _P, _P, c_int64, _P, c_int,
                                      c_int, c_int, c_int, _P, _P, c_int, _P, _P, _P, _P, _P, _P]),
+    "gq_qrcp_workspace_size": (c_int64, [c_int64, c_int64, c_int]),
+    "gq_qrcp": (c_int, [_P, c_int64, c_int64, c_int64, c_int, c_int, c_int, _P, _P, c_int64, _P, _P,
+                        ctypes.POINTER(c_int), _P, c_int64, _P]),
+    "gq_qr_factor_panel": (c_int, [_P, c_int64, c_int64, c_int64, _P, _P, c_int64, c_int, c_int, c_int,
+                                   _P, _P, _P, ctypes.POINTER(c_int), _P, c_int64, _P]),
+    "gq_qr_apply_panel": (c_int, [_P, c_int64, c_int64, c_int64, _P, c_int64, _P, c_int64, c_int, _P,
+                                  _P]),
     "gq_qronos_workspace_size": (c_int64, [c_int64, c_int64]),
     "gq_qronos": (c_int, [_P, _P, c_int64, c_int64, _P, _P, _P, _P, c_int, c_int, c_int, c_int, _P,
                           _P, _P, _P, _P, _P, c_int64, _P]),

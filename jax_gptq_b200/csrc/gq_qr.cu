@@ -1,0 +1,682 @@
+// Blocked column-pivoted Householder QR (pallas/blocked_pivoted_qr.py).
+//
+// Working copy: the matrix transposed into column-major order, at[c][r]
+// (ld = m), so pivot columns, swaps, Householder vectors and column norms are
+// contiguous.  Per panel of P columns starting at k:
+//   * one single-CTA "step" kernel per pivot: choose the pivot from the norm
+//     metadata, swap whole columns, form the reflector, append it to the
+//     compact WY pair (yt = Y^T, P x (m-k); T, P x P) and produce the vector
+//     left = (y_r T^T) Y^T that exposes row r of the transformed trailing
+//     block;
+//   * one all-SM "exposed row" kernel: e_c = B[r][c] - left . B[:, c] for the
+//     deferred (stale) trailing columns, and the norm downdate
+//     norms_c = max(norms_c - e_c^2, 0) -- the BLAS-2 pass that reads the
+//     whole trailing block every step;
+//   * at the panel end the compact-WY update B <- B - Y (T^T (Y^T B)) (three
+//     fp32 GEMMs) and an exact norm refresh from rows >= panel end.
+//
+// semantics = 0 ("reference") reproduces _factor_panel_compiled
+// (:1479-1589) and the driver (:1627-1722) exactly, including:
+//   * pivots chosen among all columns >= j, deferred trailing ones too;
+//   * panel columns updated eagerly, their norms downdated by the new row and
+//     recomputed exactly every 8 steps (:1014-1104);
+//   * the reflector built from column j - k of a[k:, :] (the panel-local
+//     index reused as a column index, :359-366);
+//   * the exposed row taken at panel-local row j (the global index reused,
+//     :1106-1112), clamped like dynamic_index_in_dim;
+//   * panels starting every P columns even after a "smallest" early stop.
+// semantics = 1 ("intended") is a correct blocked QRCP (the BLAS-3 scheme of
+// Quintana-Orti, Sun & Bischof, 1998): every column >= j is deferred, the
+// chosen pivot column is brought up to date with the panel's reflectors
+// before its Householder vector is formed, the true exposed row j downdates
+// all remaining norms, and a panel ends early when a downdated norm has lost
+// too much of its reference value to be trusted (the LAPACK xLAQPS rule),
+// after which the next panel starts from exact norms.  Its pivots and R equal
+// unblocked Householder QRCP in exact arithmetic.
+#include "gq_common.cuh"
+
+#include <algorithm>
+#include <vector>
+
+namespace gq {
+
+int sgemm(int ta, int tb, int64_t M, int64_t N, int64_t K, float alpha, const float* A, int64_t lda,
+          const float* B, int64_t ldb, float beta, float* C, int64_t ldc, int uplo, cudaStream_t st);
+
+namespace qr {
+
+constexpr float ZERO_TOL_SQ = 1e-24f;  // ZERO_TOL ** 2 (:52-53)
+constexpr int STEP_THREADS = 1024;
+constexpr int STEP_WARPS = STEP_THREADS / 32;
+constexpr int MAX_P = 256;             // widest panel (reference semantics honour panel_size)
+constexpr int INTENDED_P = 64;         // panel width used by the intended (exact) factorization
+
+// Device control block, one per factorization.
+struct Ctrl {
+  int active;     // accepted reflectors in the current panel
+  int done;       // panel stopped ("smallest" with no mass left, or early end)
+  int early_end;  // intended: a norm downdate lost precision -> end after this step
+  int row_sel;    // panel-local row exposed by the current step
+};
+
+__global__ void transpose_kernel(const float* __restrict__ src, int64_t rows, int64_t cols,
+                                 int64_t lds, float* __restrict__ dst, int64_t ldd) {
+  __shared__ float tile[32][33];
+  const int64_t r0 = (int64_t)blockIdx.y * 32, c0 = (int64_t)blockIdx.x * 32;
+  for (int i = threadIdx.y; i < 32; i += blockDim.y) {
+    int64_t r = r0 + i, c = c0 + threadIdx.x;
+    if (r < rows && c < cols) tile[i][threadIdx.x] = src[r * lds + c];
+  }
+  __syncthreads();
+  for (int i = threadIdx.y; i < 32; i += blockDim.y) {
+    int64_t c = c0 + i, r = r0 + threadIdx.x;
+    if (r < rows && c < cols) dst[c * ldd + r] = tile[threadIdx.x][i];
+  }
+}
+
+// norms[c] = sum_{r >= r0} at[c][r]^2 (warp per column); r0 >= m gives zeros.
+__global__ void col_sqnorms_kernel(const float* __restrict__ at, int64_t m, int64_t n, int64_t r0,
+                                   float* __restrict__ norms, float* __restrict__ copy) {
+  const int lane = threadIdx.x & 31;
+  const int64_t c = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  if (c >= n) return;
+  float s = 0.f;
+  for (int64_t r = r0 + lane; r < m; r += 32) {
+    float v = at[c * m + r];
+    s = fmaf(v, v, s);
+  }
+  s = warp_sum(s);
+  if (lane == 0) {
+    norms[c] = s;
+    if (copy) copy[c] = s;
+  }
+}
+
+__device__ __forceinline__ float block_sum(float v, float* red) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  v = warp_sum(v);
+  __syncthreads();
+  if (lane == 0) red[warp] = v;
+  __syncthreads();
+  float t = (lane < (int)(blockDim.x >> 5)) ? red[lane] : 0.f;
+  t = warp_sum(t);
+  return t;  // valid in every thread
+}
+
+// (value, index) best with the first-index tie rule; larger = true -> argmax.
+__device__ __forceinline__ void better(float& bv, int& bi, float v, int i, bool larger) {
+  bool take = larger ? (v > bv || (v == bv && i < bi)) : (v < bv || (v == bv && i < bi));
+  if (take) {
+    bv = v;
+    bi = i;
+  }
+}
+
+__device__ int block_arg(float v, int i, bool larger, float* redv, int* redi) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    float ov = __shfl_xor_sync(0xffffffffu, v, o);
+    int oi = __shfl_xor_sync(0xffffffffu, i, o);
+    better(v, i, ov, oi, larger);
+  }
+  __syncthreads();
+  if (lane == 0) {
+    redv[warp] = v;
+    redi[warp] = i;
+  }
+  __syncthreads();
+  if (warp == 0) {
+    float w = (lane < (int)(blockDim.x >> 5)) ? redv[lane] : (larger ? -INFINITY : INFINITY);
+    int wi = (lane < (int)(blockDim.x >> 5)) ? redi[lane] : 0x7fffffff;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      float ov = __shfl_xor_sync(0xffffffffu, w, o);
+      int oi = __shfl_xor_sync(0xffffffffu, wi, o);
+      better(w, wi, ov, oi, larger);
+    }
+    if (lane == 0) redi[0] = wi;
+  }
+  __syncthreads();
+  return redi[0];
+}
+
+struct StepArgs {
+  float* at;       // n x m column-major working copy
+  int64_t m, n;
+  int64_t k;       // panel start
+  int64_t pe;      // nominal panel end
+  int64_t j;       // global step index
+  int P;           // panel width (yt rows / T size)
+  float* yt;       // P x (m - k): reflector i in row i (panel-local rows)
+  float* t;        // P x P
+  float* tau;      // P
+  float* norms;    // n
+  float* normref;  // n: exact norms at the panel start (intended semantics)
+  int32_t* perm;   // n
+  float* left;     // m - k
+  Ctrl* ctrl;
+  int smallest;
+  int semantics;   // 0 reference, 1 intended
+};
+
+// One pivot step (single CTA).  Dynamic shared memory: v and col, (m-k) floats each.
+__global__ void __launch_bounds__(STEP_THREADS) qr_step_kernel(StepArgs a) {
+  extern __shared__ __align__(16) float sm[];
+  __shared__ float redv[STEP_WARPS];
+  __shared__ int redi[STEP_WARPS];
+  __shared__ float sw[MAX_P + 1];   // T-column work / z vectors
+  __shared__ float sw2[MAX_P + 1];
+  __shared__ int s_flag;
+
+  Ctrl* ctrl = a.ctrl;
+  if (ctrl->done) return;
+  const int64_t m = a.m, n = a.n, k = a.k, j = a.j, pe = a.pe;
+  const int64_t L = m - k;
+  const int lj = (int)(j - k);
+  const int P = a.P;
+  float* v = sm;
+  float* col = sm + L;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+
+  // 1. "smallest": stop when no remaining norm exceeds ZERO_TOL^2 (:1562-1570)
+  if (a.smallest) {
+    int any = 0;
+    for (int64_t c = j + tid; c < n; c += blockDim.x) any |= (a.norms[c] > ZERO_TOL_SQ);
+    if (tid == 0) s_flag = 0;
+    __syncthreads();
+    if (any) atomicOr(&s_flag, 1);
+    __syncthreads();
+    if (!s_flag) {
+      if (tid == 0) ctrl->done = 1;
+      return;
+    }
+  }
+  // 2. pivot (:202-219): first argmax / argmin over columns >= j
+  {
+    const bool larger = !a.smallest;
+    float bv = larger ? -INFINITY : INFINITY;
+    int bi = 0x7fffffff;
+    for (int64_t c = j + tid; c < n; c += blockDim.x) {
+      float x = a.norms[c];
+      if (a.smallest && !(x > ZERO_TOL_SQ)) x = INFINITY;
+      better(bv, bi, x, (int)c, larger);
+    }
+    int p = block_arg(bv, bi, larger, redv, redi);
+    if (p == 0x7fffffff) p = (int)j;
+    // 3. swap whole columns j and p (:264-283)
+    if (p != j) {
+      float* cj = a.at + j * m;
+      float* cp = a.at + (int64_t)p * m;
+      for (int64_t r = tid; r < m; r += blockDim.x) {
+        float x = cj[r];
+        cj[r] = cp[r];
+        cp[r] = x;
+      }
+      if (tid == 0) {
+        int32_t tp = a.perm[j];
+        a.perm[j] = a.perm[p];
+        a.perm[p] = tp;
+        float tn = a.norms[j];
+        a.norms[j] = a.norms[p];
+        a.norms[p] = tn;
+        if (a.normref) {
+          float tr = a.normref[j];
+          a.normref[j] = a.normref[p];
+          a.normref[p] = tr;
+        }
+      }
+    }
+    __syncthreads();
+  }
+
+  // 4. the column the reflector is built from
+  const int64_t src = (a.semantics == 0) ? (j - k) : j;
+  for (int64_t r = tid; r < L; r += blockDim.x) col[r] = a.at[src * m + k + r];
+  __syncthreads();
+  if (a.semantics == 1 && lj > 0) {
+    // bring the deferred pivot column up to date: col -= Y (T^T (Y^T col))
+    for (int i = warp; i < lj; i += STEP_WARPS) {
+      const float* yi = a.yt + (int64_t)i * L;
+      float s = 0.f;
+      for (int64_t r = lane; r < L; r += 32) s = fmaf(yi[r], col[r], s);
+      s = warp_sum(s);
+      if (lane == 0) sw[i] = s;
+    }
+    __syncthreads();
+    if (tid < lj) {
+      float z = 0.f;
+      for (int l = 0; l <= tid; ++l) z = fmaf(a.t[l * P + tid], sw[l], z);
+      sw2[tid] = z;
+    }
+    __syncthreads();
+    for (int64_t r = tid; r < L; r += blockDim.x) {
+      float s = 0.f;
+      for (int i = 0; i < lj; ++i) s = fmaf(a.yt[(int64_t)i * L + r], sw2[i], s);
+      col[r] = col[r] - s;
+    }
+    __syncthreads();
+  }
+  // Householder vector (:327-356): sigma over rows below lj
+  float part = 0.f;
+  for (int64_t r = lj + 1 + tid; r < L; r += blockDim.x) part = fmaf(col[r], col[r], part);
+  const float sigma = block_sum(part, redv);
+  const float x0 = col[lj];
+  float tau_j, alpha, beta = 1.f;
+  if (sigma == 0.f) {
+    tau_j = 0.f;
+    alpha = x0;
+  } else {
+    float nx = sqrtf(__fadd_rn(__fmul_rn(x0, x0), sigma));
+    alpha = (x0 <= 0.f) ? nx : -nx;
+    beta = __fsub_rn(x0, alpha);
+    tau_j = __fdiv_rn(-beta, alpha);
+  }
+  for (int64_t r = tid; r < L; r += blockDim.x) {
+    float vr;
+    if (r == lj) vr = 1.f;
+    else if (r < lj || sigma == 0.f) vr = 0.f;
+    else vr = __fdiv_rn(col[r], beta);
+    v[r] = vr;
+    a.yt[(int64_t)lj * L + r] = vr;
+  }
+  __syncthreads();
+  // 5. append to T (:674-726): T[:lj, lj] = T_prev (-tau Y_prev^T v); T[lj, lj] = tau
+  for (int i = warp; i < lj; i += STEP_WARPS) {
+    const float* yi = a.yt + (int64_t)i * L;
+    float s = 0.f;
+    for (int64_t r = lane; r < L; r += 32) s = fmaf(yi[r], v[r], s);
+    s = warp_sum(s);
+    if (lane == 0) sw[i] = -tau_j * s;
+  }
+  __syncthreads();
+  if (tid < lj) {
+    float s = 0.f;
+    for (int l = tid; l < lj; ++l) s = fmaf(a.t[tid * P + l], sw[l], s);
+    sw2[tid] = s;
+  }
+  __syncthreads();
+  if (tid < lj) a.t[tid * P + lj] = sw2[tid];
+  if (tid == 0) {
+    a.t[lj * P + lj] = tau_j;
+    a.tau[lj] = tau_j;
+  }
+  __syncthreads();
+
+  if (a.semantics == 0) {
+    // 6. eager reflector on panel columns j..pe-1 (:786-815)
+    for (int64_t c = j + warp; c < pe; c += STEP_WARPS) {
+      float* cc = a.at + c * m + k;
+      float s = 0.f;
+      for (int64_t r = lane; r < L; r += 32) s = fmaf(v[r], cc[r], s);
+      s = warp_sum(s);
+      const float wc = tau_j * s;
+      for (int64_t r = lane; r < L; r += 32) cc[r] = __fsub_rn(cc[r], __fmul_rn(v[r], wc));
+    }
+    __syncthreads();
+  }
+  // pivot column: alpha on the diagonal, zeros below; in the intended
+  // factorization rows k..j-1 take the brought-up-to-date values (its R entries)
+  for (int64_t r = tid; r < L; r += blockDim.x) {
+    if (r >= lj) a.at[j * m + k + r] = (r == lj) ? alpha : 0.f;
+    else if (a.semantics == 1) a.at[j * m + k + r] = col[r];
+  }
+  __syncthreads();
+
+  const int64_t nxt = j + 1;
+  if (a.semantics == 0 && nxt < n && nxt < pe) {
+    // 7a. panel-column norm metadata (:1048-1092)
+    const bool refresh = ((nxt - k) % 8) == 0;
+    for (int64_t c = nxt + warp; c < pe; c += STEP_WARPS) {
+      const float* cc = a.at + c * m;
+      float cur = a.norms[c];
+      if (refresh) {
+        float s = 0.f;
+        for (int64_t r = nxt + lane; r < m; r += 32) s = fmaf(cc[r], cc[r], s);
+        s = warp_sum(s);
+        cur = s;
+      } else {
+        float row = cc[j];
+        cur = fmaxf(__fsub_rn(cur, __fmul_rn(row, row)), 0.f);
+      }
+      if (lane == 0) a.norms[c] = cur;
+    }
+  }
+  // 7b. the vector exposing one row of the transformed deferred block
+  const bool exposes = (a.semantics == 0) ? (nxt < n && pe < n) : (nxt < n);
+  if (exposes) {
+    // reference: the global step index is used as the panel-local row (clamped)
+    int64_t rs = lj;
+    if (a.semantics == 0) rs = (j < 0) ? 0 : ((j > L - 1) ? L - 1 : j);
+    if (tid < P) {
+      float s = 0.f;
+      for (int l = 0; l < P; ++l) s = fmaf(a.yt[(int64_t)l * L + rs], a.t[tid * P + l], s);
+      sw[tid] = s;  // row_weights = y_r T^T
+    }
+    __syncthreads();
+    for (int64_t r = tid; r < L; r += blockDim.x) {
+      float s = 0.f;
+      for (int i = 0; i < P; ++i) s = fmaf(sw[i], a.yt[(int64_t)i * L + r], s);
+      a.left[r] = s;
+    }
+    if (tid == 0) ctrl->row_sel = (int)rs;
+  }
+  if (tid == 0) ctrl->active = ctrl->active + 1;
+}
+
+// Exposed-row downdate over deferred columns [c0, n): warp per column.
+__global__ void exposed_row_kernel(const float* __restrict__ at, int64_t m, int64_t n, int64_t k,
+                                   int64_t c0, const float* __restrict__ left,
+                                   float* __restrict__ norms, const float* __restrict__ normref,
+                                   Ctrl* ctrl, float tol) {
+  if (ctrl->done) return;
+  const int lane = threadIdx.x & 31;
+  const int64_t L = m - k;
+  const int rs = ctrl->row_sel;
+  const int64_t nw = (int64_t)gridDim.x * (blockDim.x >> 5);
+  for (int64_t c = c0 + (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); c < n;
+       c += nw) {
+    const float* b = at + c * m + k;
+    float s = 0.f;
+    int64_t r = lane * 4;
+    if ((m & 3) == 0 && (k & 3) == 0) {
+      for (; r + 3 < L; r += 128) {
+        float4 bv = *reinterpret_cast<const float4*>(b + r);
+        float4 lv = *reinterpret_cast<const float4*>(left + r);
+        s = fmaf(lv.x, bv.x, s);
+        s = fmaf(lv.y, bv.y, s);
+        s = fmaf(lv.z, bv.z, s);
+        s = fmaf(lv.w, bv.w, s);
+      }
+    } else {
+      for (int64_t q = lane; q < L; q += 32) s = fmaf(left[q], b[q], s);
+    }
+    s = warp_sum(s);
+    if (lane == 0) {
+      float e = __fsub_rn(b[rs], s);
+      float nv = fmaxf(__fsub_rn(norms[c], __fmul_rn(e, e)), 0.f);
+      norms[c] = nv;
+      if (normref && nv <= tol * normref[c] && normref[c] > 0.f) atomicExch(&ctrl->early_end, 1);
+    }
+  }
+}
+
+// After a step: intended panels stop once a downdate lost precision.
+__global__ void end_check_kernel(Ctrl* ctrl) {
+  if (ctrl->early_end) ctrl->done = 1;
+}
+
+__global__ void reset_ctrl_kernel(Ctrl* ctrl) {
+  ctrl->active = 0;
+  ctrl->done = 0;
+  ctrl->early_end = 0;
+  ctrl->row_sel = 0;
+}
+
+// V[k + r][k + i] = yt[i][r] for i < w (reflectors in global rows); columns are strided.
+__global__ void store_reflectors_kernel(const float* __restrict__ yt, int64_t m, int64_t k, int w,
+                                        float* __restrict__ V, int64_t ldv, const float* __restrict__ tau,
+                                        float* __restrict__ tau_out) {
+  const int64_t L = m - k;
+  const int i = blockIdx.y;
+  for (int64_t r = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; r < m; r += (int64_t)gridDim.x * blockDim.x) {
+    float x = (r >= k) ? yt[(int64_t)i * L + (r - k)] : 0.f;
+    V[r * ldv + k + i] = x;
+  }
+  if (blockIdx.x == 0 && threadIdx.x == 0 && tau_out) tau_out[k + i] = tau[i];
+}
+
+struct Work {
+  float* at;
+  float* yt;
+  float* t;
+  float* tau;
+  float* norms;
+  float* normref;
+  float* left;
+  float* z;
+  float* z2;
+  Ctrl* ctrl;
+};
+
+inline int64_t align256(int64_t b) { return (b + 255) & ~int64_t(255); }
+
+int64_t ws_bytes(int64_t m, int64_t n, int P) {
+  int64_t b = 0;
+  b += align256(n * m * 4);          // at
+  b += align256((int64_t)P * m * 4);  // yt
+  b += align256((int64_t)P * P * 4);  // t
+  b += align256((int64_t)P * 4);      // tau
+  b += align256(n * 4) * 2;          // norms, normref
+  b += align256(m * 4);              // left
+  b += align256(n * (int64_t)P * 4) * 2;  // z, z2
+  b += align256(sizeof(Ctrl));
+  return b;
+}
+
+Work carve(void* ws, int64_t m, int64_t n, int P) {
+  char* p = reinterpret_cast<char*>(ws);
+  Work w;
+  w.at = reinterpret_cast<float*>(p); p += align256(n * m * 4);
+  w.yt = reinterpret_cast<float*>(p); p += align256((int64_t)P * m * 4);
+  w.t = reinterpret_cast<float*>(p); p += align256((int64_t)P * P * 4);
+  w.tau = reinterpret_cast<float*>(p); p += align256((int64_t)P * 4);
+  w.norms = reinterpret_cast<float*>(p); p += align256(n * 4);
+  w.normref = reinterpret_cast<float*>(p); p += align256(n * 4);
+  w.left = reinterpret_cast<float*>(p); p += align256(m * 4);
+  w.z = reinterpret_cast<float*>(p); p += align256(n * (int64_t)P * 4);
+  w.z2 = reinterpret_cast<float*>(p); p += align256(n * (int64_t)P * 4);
+  w.ctrl = reinterpret_cast<Ctrl*>(p);
+  return w;
+}
+
+// B <- B - Y (T^T (Y^T B)) for deferred columns [c0, n), rows k..m-1 (width w).
+int apply_panel(Work& W, int64_t m, int64_t n, int64_t k, int w, int P, int64_t c0,
+                cudaStream_t st) {
+  if (c0 >= n || w <= 0) return GQ_OK;
+  const int64_t L = m - k, nc = n - c0;
+  float* bt = W.at + c0 * m + k;  // nc x L, ld m
+  // Zt = Bt Y  (Y = yt^T):  nc x w
+  GQ_TRY(sgemm(0, 1, nc, w, L, 1.f, bt, m, W.yt, L, 0.f, W.z, P, 0, st));
+  // Zt' = Zt T  (z' = T^T z)
+  GQ_TRY(sgemm(0, 0, nc, w, w, 1.f, W.z, P, W.t, P, 0.f, W.z2, P, 0, st));
+  // Bt -= Zt' yt
+  GQ_TRY(sgemm(0, 0, nc, L, w, -1.f, W.z2, P, W.yt, L, 1.f, bt, m, 0, st));
+  return GQ_OK;
+}
+
+int norms_from(Work& W, int64_t m, int64_t n, int64_t r0, bool keep_ref, cudaStream_t st) {
+  col_sqnorms_kernel<<<(unsigned)ceil_div(n, 8), 256, 0, st>>>(W.at, m, n, r0, W.norms,
+                                                               keep_ref ? W.normref : nullptr);
+  return check_launch("col_sqnorms");
+}
+
+// One panel from k; returns the realized width through *width (host-synced).
+int factor_panel(Work& W, int64_t m, int64_t n, int64_t k, int P, int smallest, int semantics,
+                 int32_t* perm, cudaStream_t st, int* width) {
+  const int64_t limit = std::min(m, n);
+  const int64_t pe = std::min(k + (int64_t)P, limit);
+  const int64_t L = m - k;
+  GQ_CHECK_CUDA(cudaMemsetAsync(W.yt, 0, (size_t)P * L * 4, st));
+  GQ_CHECK_CUDA(cudaMemsetAsync(W.t, 0, (size_t)P * P * 4, st));
+  GQ_CHECK_CUDA(cudaMemsetAsync(W.tau, 0, (size_t)P * 4, st));
+  reset_ctrl_kernel<<<1, 1, 0, st>>>(W.ctrl);
+  GQ_TRY(check_launch("reset_ctrl"));
+  const size_t smem = (size_t)L * 8;
+  const int gemv_blocks = std::max(1, sm_count() * 4);
+  const float tol3z = 0.000244140625f;  // sqrt(2^-24): LAPACK's xLAQPS recompute threshold
+  for (int64_t j = k; j < pe; ++j) {
+    StepArgs a;
+    a.at = W.at; a.m = m; a.n = n; a.k = k; a.pe = pe; a.j = j; a.P = P;
+    a.yt = W.yt; a.t = W.t; a.tau = W.tau; a.norms = W.norms; a.perm = perm; a.left = W.left;
+    a.normref = W.normref;
+    a.ctrl = W.ctrl; a.smallest = smallest; a.semantics = semantics;
+    qr_step_kernel<<<1, STEP_THREADS, smem, st>>>(a);
+    GQ_TRY(check_launch("qr_step"));
+    const int64_t c0 = (semantics == 0) ? pe : j + 1;
+    const bool exposes = (semantics == 0) ? (j + 1 < n && pe < n) : (j + 1 < n);
+    if (exposes) {
+      exposed_row_kernel<<<gemv_blocks, 256, 0, st>>>(W.at, m, n, k, c0, W.left, W.norms,
+                                                       semantics == 1 ? W.normref : nullptr,
+                                                       W.ctrl, tol3z);
+      GQ_TRY(check_launch("exposed_row"));
+    }
+    if (semantics == 1) {
+      end_check_kernel<<<1, 1, 0, st>>>(W.ctrl);
+      GQ_TRY(check_launch("end_check"));
+    }
+  }
+  Ctrl h;
+  GQ_CHECK_CUDA(cudaMemcpyAsync(&h, W.ctrl, sizeof(Ctrl), cudaMemcpyDeviceToHost, st));
+  GQ_CHECK_CUDA(cudaStreamSynchronize(st));
+  *width = h.active;
+  return GQ_OK;
+}
+
+}  // namespace qr
+}  // namespace gq
+
+extern "C" {
+
+int64_t gq_qrcp_workspace_size(int64_t m, int64_t n, int panel_size) {
+  int P = std::max(1, std::min(panel_size, gq::qr::MAX_P));
+  return gq::qr::ws_bytes(m, n, P);
+}
+
+int gq_qrcp(float* a, int64_t m, int64_t n, int64_t lda, int panel_size, int pivot_mode,
+            int semantics, int32_t* perm, float* v_out, int64_t ldv, float* tau_out,
+            int32_t* panel_ends, int* n_panels, void* workspace, int64_t workspace_bytes,
+            void* stream) {
+  using namespace gq;
+  GQ_REQUIRE(a != nullptr && perm != nullptr, "gq_qrcp: NULL a or perm");
+  GQ_REQUIRE(m > 0 && n > 0 && lda >= n, "gq_qrcp: bad shape (m=%lld n=%lld lda=%lld)",
+             (long long)m, (long long)n, (long long)lda);
+  GQ_REQUIRE(panel_size > 0, "panel_size must be positive, got %d", panel_size);
+  GQ_REQUIRE(pivot_mode == 0 || pivot_mode == 1, "gq_qrcp: pivot_mode must be 0 (largest) or 1 (smallest)");
+  GQ_REQUIRE(semantics == 0 || semantics == 1, "gq_qrcp: semantics must be 0 or 1");
+  GQ_REQUIRE(m * 8 <= 200 * 1024, "gq_qrcp: m=%lld exceeds the step kernel's shared memory", (long long)m);
+  GQ_REQUIRE(n < (1ll << 31) && m < (1ll << 31), "gq_qrcp: dimension too large");
+  const int64_t limit = std::min(m, n);
+  // A panel wider than the matrix is one panel.  The reference semantics depend
+  // on the panel width and honour it (up to MAX_P); the intended factorization
+  // is independent of it and always runs 64-wide panels.
+  int P = (int)std::min<int64_t>(panel_size, limit);
+  if (semantics == 1) P = std::min(P, qr::INTENDED_P);
+  GQ_REQUIRE(P <= qr::MAX_P, "gq_qrcp: panel_size %d > %d with min(m, n) = %lld is not supported",
+             panel_size, qr::MAX_P, (long long)limit);
+  GQ_REQUIRE(workspace_bytes >= gq_qrcp_workspace_size(m, n, P), "gq_qrcp: workspace too small");
+  GQ_REQUIRE(v_out == nullptr || ldv >= limit, "gq_qrcp: ldv too small");
+  cudaStream_t st = as_stream(stream);
+  qr::Work W = qr::carve(workspace, m, n, P);
+  static bool attr = false;
+  if (!attr) {
+    GQ_CHECK_CUDA(cudaFuncSetAttribute(qr::qr_step_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       200 * 1024));
+    attr = true;
+  }
+  dim3 tb(32, 8);
+  qr::transpose_kernel<<<dim3((unsigned)ceil_div(n, 32), (unsigned)ceil_div(m, 32)), tb, 0, st>>>(
+      a, m, n, lda, W.at, m);
+  GQ_TRY(check_launch("transpose_in"));
+  {
+    std::vector<int32_t> iota(n);
+    for (int64_t i = 0; i < n; ++i) iota[i] = (int32_t)i;
+    GQ_CHECK_CUDA(cudaMemcpyAsync(perm, iota.data(), n * 4, cudaMemcpyHostToDevice, st));
+    GQ_CHECK_CUDA(cudaStreamSynchronize(st));
+  }
+  if (v_out) GQ_CHECK_CUDA(cudaMemset2DAsync(v_out, ldv * 4, 0, limit * 4, m, st));
+  if (tau_out) GQ_CHECK_CUDA(cudaMemsetAsync(tau_out, 0, limit * 4, st));
+  GQ_TRY(qr::norms_from(W, m, n, 0, true, st));
+  int np = 0;
+  for (int64_t k = 0; k < limit;) {
+    int width = 0;
+    GQ_TRY(qr::factor_panel(W, m, n, k, P, pivot_mode, semantics, perm, st, &width));
+    const int64_t pe_real = k + width;
+    if (panel_ends) panel_ends[np] = (int32_t)pe_real;
+    ++np;
+    if (v_out && width > 0) {
+      qr::store_reflectors_kernel<<<dim3((unsigned)std::min<int64_t>(ceil_div(m, 256), 64),
+                                         (unsigned)width), 256, 0, st>>>(W.yt, m, k, width, v_out,
+                                                                          ldv, W.tau, tau_out);
+      GQ_TRY(check_launch("store_reflectors"));
+    }
+    GQ_TRY(qr::apply_panel(W, m, n, k, width, P, pe_real, st));
+    GQ_TRY(qr::norms_from(W, m, n, pe_real, true, st));
+    if (semantics == 0) {
+      k += P;  // the reference's driver steps by panel_size regardless (:1665)
+    } else {
+      if (width == 0) break;  // no mass left ("smallest")
+      k = pe_real;
+    }
+  }
+  if (n_panels) *n_panels = np;
+  qr::transpose_kernel<<<dim3((unsigned)ceil_div(m, 32), (unsigned)ceil_div(n, 32)), tb, 0, st>>>(
+      W.at, n, m, m, a, lda);
+  GQ_TRY(check_launch("transpose_out"));
+  return GQ_OK;
+}
+
+int gq_qr_factor_panel(float* a, int64_t m, int64_t n, int64_t lda, int32_t* perm, float* norms,
+                       int64_t k, int panel_size, int pivot_mode, int semantics, float* y_out,
+                       float* tau_out, float* t_out, int* panel_end_out, void* workspace,
+                       int64_t workspace_bytes, void* stream) {
+  using namespace gq;
+  GQ_REQUIRE(a && perm && norms && y_out && tau_out && t_out && panel_end_out,
+             "gq_qr_factor_panel: NULL argument");
+  GQ_REQUIRE(m > 0 && n > 0 && lda >= n, "gq_qr_factor_panel: bad shape");
+  const int64_t limit = std::min(m, n);
+  GQ_REQUIRE(panel_size > 0, "panel_size must be positive, got %d", panel_size);
+  GQ_REQUIRE(k >= 0 && k < limit, "k must be in [0, %lld), got %lld", (long long)limit, (long long)k);
+  const int P = (int)std::min<int64_t>(panel_size, limit - k);
+  GQ_REQUIRE(P <= qr::MAX_P, "gq_qr_factor_panel: panel width above %d is not supported", qr::MAX_P);
+  GQ_REQUIRE(pivot_mode == 0 || pivot_mode == 1, "gq_qr_factor_panel: bad pivot_mode");
+  GQ_REQUIRE(semantics == 0 || semantics == 1, "gq_qr_factor_panel: bad semantics");
+  GQ_REQUIRE(m * 8 <= 200 * 1024, "gq_qr_factor_panel: m too large");
+  GQ_REQUIRE(workspace_bytes >= gq_qrcp_workspace_size(m, n, P), "gq_qr_factor_panel: workspace too small");
+  cudaStream_t st = as_stream(stream);
+  qr::Work W = qr::carve(workspace, m, n, P);
+  static bool attr = false;
+  if (!attr) {
+    GQ_CHECK_CUDA(cudaFuncSetAttribute(qr::qr_step_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       200 * 1024));
+    attr = true;
+  }
+  dim3 tb(32, 8);
+  qr::transpose_kernel<<<dim3((unsigned)ceil_div(n, 32), (unsigned)ceil_div(m, 32)), tb, 0, st>>>(
+      a, m, n, lda, W.at, m);
+  GQ_TRY(check_launch("transpose_in"));
+  GQ_CHECK_CUDA(cudaMemcpyAsync(W.norms, norms, n * 4, cudaMemcpyDeviceToDevice, st));
+  GQ_CHECK_CUDA(cudaMemcpyAsync(W.normref, norms, n * 4, cudaMemcpyDeviceToDevice, st));
+  int width = 0;
+  GQ_TRY(qr::factor_panel(W, m, n, k, P, pivot_mode, semantics, perm, st, &width));
+  *panel_end_out = (int)(k + width);
+  const int64_t L = m - k;
+  // y_out [L, P] (panel-local rows), t_out [P, P], tau_out [P]
+  qr::transpose_kernel<<<dim3((unsigned)ceil_div(L, 32), (unsigned)ceil_div(P, 32)), tb, 0, st>>>(
+      W.yt, P, L, L, y_out, P);
+  GQ_TRY(check_launch("transpose_y"));
+  GQ_CHECK_CUDA(cudaMemcpyAsync(t_out, W.t, (size_t)P * P * 4, cudaMemcpyDeviceToDevice, st));
+  GQ_CHECK_CUDA(cudaMemcpyAsync(tau_out, W.tau, (size_t)P * 4, cudaMemcpyDeviceToDevice, st));
+  GQ_CHECK_CUDA(cudaMemcpyAsync(norms, W.norms, n * 4, cudaMemcpyDeviceToDevice, st));
+  qr::transpose_kernel<<<dim3((unsigned)ceil_div(m, 32), (unsigned)ceil_div(n, 32)), tb, 0, st>>>(
+      W.at, n, m, m, a, lda);
+  return check_launch("transpose_out");
+}
+
+int gq_qr_apply_panel(float* b, int64_t rows, int64_t cols, int64_t ldb, const float* y,
+                      int64_t ldy, const float* t, int64_t ldt, int width, float* scratch,
+                      void* stream) {
+  using namespace gq;
+  GQ_REQUIRE(rows >= 0 && cols >= 0 && width >= 0, "gq_qr_apply_panel: negative size");
+  GQ_REQUIRE(ldb >= cols && ldy >= width && ldt >= width, "gq_qr_apply_panel: bad leading dims");
+  if (rows == 0 || cols == 0 || width == 0) return GQ_OK;
+  GQ_REQUIRE(b && y && t && scratch, "gq_qr_apply_panel: NULL argument");
+  cudaStream_t st = as_stream(stream);
+  float* w1 = scratch;                   // width x cols
+  float* w2 = scratch + (int64_t)width * cols;
+  GQ_TRY(sgemm(1, 0, width, cols, rows, 1.f, y, ldy, b, ldb, 0.f, w1, cols, 0, st));
+  GQ_TRY(sgemm(1, 0, width, cols, width, 1.f, t, ldt, w1, cols, 0.f, w2, cols, 0, st));
+  return sgemm(0, 0, rows, cols, width, -1.f, y, ldy, w2, cols, 1.f, b, ldb, 0, st);
+}
+
+}  // extern "C"
