@@ -60,16 +60,27 @@ int gq_rtn(const float* w, int64_t m, int64_t n, int64_t ldw, const int32_t* per
            float* dequant, uint8_t* codes, float* scales, float* zeros, void* stream);
 
 /* ------------------------------------------------------------------------
- * FP32 GEMM on the CUDA cores: C = alpha * op(A) op(B) + beta * C with
- * op(A) M x K, op(B) K x N, row-major storage (trans_* = 1 means the stored
- * matrix is the transpose).  uplo = 0 computes all of C, 1 only tiles that
- * touch the lower triangle, 2 only tiles that touch the upper triangle
- * (tiles on the diagonal are computed whole).  Used for the GPTQ lazy
- * trailing update, Cholesky/inverse updates and the QR compact-WY update.
+ * Float32-accurate GEMM: C = alpha * op(A) op(B) + beta * C with op(A) M x K,
+ * op(B) K x N, row-major storage (trans_* = 1 means the stored matrix is the
+ * transpose).  uplo = 0 computes all of C, 1 only tiles that touch the lower
+ * triangle, 2 only tiles that touch the upper triangle (tiles on the diagonal
+ * are computed whole).  Used for the GPTQ lazy trailing update, Cholesky /
+ * inverse updates, Qronos and the QR compact-WY update.
+ * gq_sgemm runs the tcgen05 3xTF32 kernel (gq_gemm_f32_tc) when trans_a = 0,
+ * M, N >= 128, K >= 32, A and B are 16-byte aligned and lda, ldb are
+ * multiples of 4, and the CUDA-core kernel (gq_sgemm_simt) otherwise.
  */
 int gq_sgemm(int trans_a, int trans_b, int64_t M, int64_t N, int64_t K, float alpha,
              const float* a, int64_t lda, const float* b, int64_t ldb, float beta,
              float* c, int64_t ldc, int uplo, void* stream);
+int gq_sgemm_simt(int trans_a, int trans_b, int64_t M, int64_t N, int64_t K, float alpha,
+                  const float* a, int64_t lda, const float* b, int64_t ldb, float beta,
+                  float* c, int64_t ldc, int uplo, void* stream);
+/* tcgen05 kind::tf32 with a 3-pass hi/lo operand split (error near 2^-21 per
+ * product); A [M, K] row-major, B [K, N] (trans_b = 0) or [N, K] (1). */
+int gq_gemm_f32_tc(int trans_b, int64_t M, int64_t N, int64_t K, float alpha,
+                   const float* a, int64_t lda, const float* b, int64_t ldb, float beta,
+                   float* c, int64_t ldc, int uplo, void* stream);
 
 /* ------------------------------------------------------------------------
  * stats.py:4-18 h_g_from_activations, bf16 activations, fp32 accumulation

@@ -30,6 +30,10 @@ SIGNATURES = {
     "gq_rtn": (c_int, [_P, c_int64, c_int64, c_int64, _P, c_int, c_int, c_int, _P, _P, _P, _P, _P]),
     "gq_sgemm": (c_int, [c_int, c_int, c_int64, c_int64, c_int64, c_float, _P, c_int64, _P, c_int64,
                          c_float, _P, c_int64, c_int, _P]),
+    "gq_sgemm_simt": (c_int, [c_int, c_int, c_int64, c_int64, c_int64, c_float, _P, c_int64, _P,
+                              c_int64, c_float, _P, c_int64, c_int, _P]),
+    "gq_gemm_f32_tc": (c_int, [c_int, c_int64, c_int64, c_int64, c_float, _P, c_int64, _P, c_int64,
+                               c_float, _P, c_int64, c_int, _P]),
     "gq_syrk_bf16": (c_int, [_P, c_int64, c_int64, c_int64, _P, c_int64, c_int, _P]),
     "gq_gemm_tn_bf16": (c_int, [_P, c_int64, _P, c_int64, c_int64, c_int64, c_int64, _P, c_int64,
                                 c_int, _P]),

@@ -52,6 +52,30 @@ __global__ void symmetrize_upper_kernel(float* __restrict__ h, int64_t d, int64_
   }
 }
 
+// dst[c][r] = src[r][c] for a rows x cols block (tiled through shared memory).
+__global__ void transpose2d_kernel(const float* __restrict__ src, int64_t rows, int64_t cols,
+                                   int64_t lds, float* __restrict__ dst, int64_t ldd) {
+  __shared__ float tile[32][33];
+  const int64_t r0 = (int64_t)blockIdx.y * 32, c0 = (int64_t)blockIdx.x * 32;
+  for (int i = threadIdx.y; i < 32; i += blockDim.y) {
+    int64_t r = r0 + i, c = c0 + threadIdx.x;
+    if (r < rows && c < cols) tile[i][threadIdx.x] = src[r * lds + c];
+  }
+  __syncthreads();
+  for (int i = threadIdx.y; i < 32; i += blockDim.y) {
+    int64_t c = c0 + i, r = r0 + threadIdx.x;
+    if (r < rows && c < cols) dst[c * ldd + r] = tile[threadIdx.x][i];
+  }
+}
+
+int transpose2d(const float* src, int64_t rows, int64_t cols, int64_t lds, float* dst, int64_t ldd,
+                cudaStream_t st) {
+  if (rows == 0 || cols == 0) return GQ_OK;
+  dim3 grid((unsigned)ceil_div(cols, 32), (unsigned)ceil_div(rows, 32));
+  transpose2d_kernel<<<grid, dim3(32, 8), 0, st>>>(src, rows, cols, lds, dst, ldd);
+  return check_launch("transpose2d");
+}
+
 int symmetrize_upper(float* h, int64_t d, int64_t ldh, cudaStream_t st) {
   if (d <= 1) return GQ_OK;
   int64_t nt = ceil_div(d, 32);

@@ -8,11 +8,11 @@
 // Hd^-1 = (R^-1)^T R^-1, i.e. U = R^-1 = J L^-1 J.  Cost: one blocked
 // Cholesky (n^3/3) plus one triangular inverse, all in float32.
 //
-// Blocked right-looking Cholesky, panel width 64: a single-CTA kernel factors
+// Blocked right-looking Cholesky, panel width 128: a single-CTA kernel factors
 // the diagonal block in shared memory (flagging a non-positive or non-finite
 // pivot in a device status word instead of producing NaNs) and inverts it;
 // the panel solve and the trailing rank-64 update are fp32 GEMMs.  The
-// triangular inverse is recursive (X21 = -L22^-1 L21 L11^-1) with all 64x64
+// triangular inverse is recursive (X21 = -L22^-1 L21 L11^-1) with all 128x128
 // diagonal blocks inverted by one batched launch.
 #include "gq_common.cuh"
 
@@ -120,101 +120,180 @@ __global__ void damp_permute_kernel(const float* __restrict__ h, int64_t n, int6
 }
 
 // ---------------------------------------------------------------------------
-// Diagonal block: Cholesky of the kb x kb lower block at a (ld), in place,
-// plus its lower-triangular inverse into inv (ld 64, upper part zeroed).
-// A pivot that is not > 0 (or not finite) sets *status = GQ_DEVERR_NOTPD.
-constexpr int NB = 64;
+// Diagonal blocks of NB x NB are factored and inverted by one 1024-thread CTA
+// with the block held in registers: thread (ty, tx) of a 32 x 32 grid owns the
+// 4 x 4 tile rows 4ty..4ty+3, columns 4tx..4tx+3.  Each elimination step
+// publishes one column (and for the inverse one row) through double-buffered
+// shared memory, so a step costs one barrier, eight shared loads and sixteen
+// register FMAs per thread; warps whose tiles are finished skip the update.
+constexpr int NB = 128;
+constexpr int DIAG_THREADS = 1024;
+constexpr size_t DIAG_SMEM = 0;
 
-__global__ void __launch_bounds__(256)
-potrf_diag_kernel(float* __restrict__ a, int64_t lda, int kb, float* __restrict__ inv,
-                  int* __restrict__ status) {
-  __shared__ float s[NB][NB + 1];
-  __shared__ float sinv[NB][NB + 1];
-  __shared__ int bad;
-  const int tid = threadIdx.x;
-  if (tid == 0) bad = 0;
-  for (int e = tid; e < NB * NB; e += blockDim.x) {
-    int r = e / NB, c = e % NB;
-    s[r][c] = (r < kb && c < kb && c <= r) ? a[r * lda + c] : ((r == c) ? 1.f : 0.f);
-  }
-  __syncthreads();
-  for (int j = 0; j < kb; ++j) {
-    float djj = s[j][j];
-    if (!(djj > 0.f) || !isfinite(djj)) {
-      if (tid == 0) bad = 1;
-      djj = 1.f;  // keep going with a harmless value; the status word reports it
-    }
-    float ljj = sqrtf(djj);
-    __syncthreads();
-    if (tid == 0) s[j][j] = ljj;
-    for (int r = j + 1 + tid; r < kb; r += blockDim.x) s[r][j] = s[r][j] / ljj;
-    __syncthreads();
-    // trailing update of the lower part: s[r][c] -= s[r][j] * s[c][j] for j < c <= r
-    int rem = kb - j - 1;
-    for (int e = tid; e < rem * rem; e += blockDim.x) {
-      int r = j + 1 + e / rem, c = j + 1 + e % rem;
-      if (c <= r) s[r][c] = fmaf(-s[r][j], s[c][j], s[r][c]);
+// Lower Cholesky of v (the kb x kb block; identity beyond kb), in place.  A
+// pivot that is not > 0 (or not finite) sets *bad and continues with 1.
+__device__ void chol_regs(float (&v)[4][4], int kb, int* bad, float (*colbuf)[NB]) {
+  const int tx = threadIdx.x & 31, ty = threadIdx.x >> 5;
+  for (int j = 0; j < NB; ++j) {
+    float* col = colbuf[j & 1];
+    if (tx == (j >> 2)) {
+#pragma unroll
+      for (int i = 0; i < 4; ++i)
+#pragma unroll
+        for (int t = 0; t < 4; ++t)
+          if (t == (j & 3)) col[4 * ty + i] = v[i][t];
     }
     __syncthreads();
-  }
-  // write L back (lower part only) and zero the strict upper part
-  for (int e = tid; e < kb * kb; e += blockDim.x) {
-    int r = e / kb, c = e % kb;
-    a[r * lda + c] = (c <= r) ? s[r][c] : 0.f;
-  }
-  // inverse by forward substitution, one column per thread
-  if (tid < NB) {
-    int c = tid;
-    for (int r = 0; r < NB; ++r) {
-      float v;
-      if (r < c) v = 0.f;
-      else {
-        float acc = (r == c) ? 1.f : 0.f;
-        for (int k = c; k < r; ++k) acc = fmaf(-s[r][k], sinv[k][c], acc);
-        v = acc / s[r][r];
+    float djj = col[j];
+    if (j < kb && (!(djj > 0.f) || !isfinite(djj))) {
+      if (threadIdx.x == 0) *bad = 1;
+      djj = 1.f;
+    }
+    if (j >= kb) djj = 1.f;
+    const float ljj = sqrtf(djj);
+    const float rinv = 1.f / djj;
+    if (4 * ty + 3 > j && 4 * tx + 3 > j && 4 * tx <= 4 * ty + 3) {
+      // trailing update s[r][c] -= s[r][j] s[c][j] / s[j][j] for j < c <= r
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const int r = 4 * ty + i;
+        const float srj = col[r] * rinv;
+#pragma unroll
+        for (int t = 0; t < 4; ++t) {
+          const int c = 4 * tx + t;
+          if (c > j && c <= r) v[i][t] = fmaf(-srj, col[c], v[i][t]);
+        }
       }
-      sinv[r][c] = v;
+    }
+    if (tx == (j >> 2)) {
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const int r = 4 * ty + i;
+        const float lv = (r == j) ? ljj : col[r] / ljj;
+#pragma unroll
+        for (int t = 0; t < 4; ++t)
+          if (t == (j & 3) && r >= j) v[i][t] = lv;
+      }
     }
   }
-  __syncthreads();
-  for (int e = tid; e < NB * NB; e += blockDim.x) {
-    int r = e / NB, c = e % NB;
-    inv[r * NB + c] = (r < kb && c < kb) ? sinv[r][c] : 0.f;
-  }
-  if (tid == 0 && bad) atomicExch(status, GQ_DEVERR_NOTPD);
 }
 
-// Batched lower-triangular inverse of the 64x64 diagonal blocks of a (in place).
-__global__ void __launch_bounds__(256) trinv_diag_blocks_kernel(float* __restrict__ a, int64_t n,
-                                                                int64_t lda) {
-  __shared__ float s[NB][NB + 1];
-  __shared__ float sinv[NB][NB + 1];
-  const int64_t b0 = (int64_t)blockIdx.x * NB;
-  const int kb = (int)min((int64_t)NB, n - b0);
-  const int tid = threadIdx.x;
-  for (int e = tid; e < NB * NB; e += blockDim.x) {
-    int r = e / NB, c = e % NB;
-    s[r][c] = (r < kb && c < kb && c <= r) ? a[(b0 + r) * lda + b0 + c] : ((r == c) ? 1.f : 0.f);
-  }
-  __syncthreads();
-  if (tid < NB) {
-    int c = tid;
-    for (int r = 0; r < NB; ++r) {
-      float v;
-      if (r < c) v = 0.f;
-      else {
-        float acc = (r == c) ? 1.f : 0.f;
-        for (int k = c; k < r; ++k) acc = fmaf(-s[r][k], sinv[k][c], acc);
-        v = acc / s[r][r];
+// x = L^-1 for the lower L in v (right-looking substitution on x = I): step k
+// scales row k by 1 / L[k][k] and removes it from the rows below.
+__device__ void trinv_regs(const float (&v)[4][4], float (&x)[4][4], float (*colbuf)[NB],
+                           float (*rowbuf)[NB]) {
+  const int tx = threadIdx.x & 31, ty = threadIdx.x >> 5;
+#pragma unroll
+  for (int i = 0; i < 4; ++i)
+#pragma unroll
+    for (int t = 0; t < 4; ++t) x[i][t] = (4 * ty + i == 4 * tx + t) ? 1.f : 0.f;
+  for (int k = 0; k < NB; ++k) {
+    float* col = colbuf[k & 1];
+    float* row = rowbuf[k & 1];
+    if (tx == (k >> 2)) {
+#pragma unroll
+      for (int i = 0; i < 4; ++i)
+#pragma unroll
+        for (int t = 0; t < 4; ++t)
+          if (t == (k & 3)) col[4 * ty + i] = v[i][t];
+    }
+    if (ty == (k >> 2)) {
+#pragma unroll
+      for (int i = 0; i < 4; ++i)
+#pragma unroll
+        for (int t = 0; t < 4; ++t)
+          if (i == (k & 3)) row[4 * tx + t] = x[i][t];
+    }
+    __syncthreads();
+    const float rk = 1.f / col[k];
+    if (4 * ty + 3 > k && 4 * tx <= k) {
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const int r = 4 * ty + i;
+        const float lrk = col[r];
+#pragma unroll
+        for (int t = 0; t < 4; ++t) {
+          const int c = 4 * tx + t;
+          if (r > k && c <= k) x[i][t] = fmaf(-lrk, row[c] * rk, x[i][t]);
+        }
       }
-      sinv[r][c] = v;
+    }
+    if (ty == (k >> 2)) {
+#pragma unroll
+      for (int i = 0; i < 4; ++i)
+#pragma unroll
+        for (int t = 0; t < 4; ++t)
+          if (i == (k & 3)) x[i][t] *= rk;
     }
   }
+}
+
+// Cholesky of the kb x kb lower block at a (ld lda) in place (strict upper
+// part zeroed) and its inverse into inv (NB x NB, ld NB, zero padded).
+__global__ void __launch_bounds__(DIAG_THREADS)
+potrf_diag_kernel(float* __restrict__ a, int64_t lda, int kb, float* __restrict__ inv,
+                  int* __restrict__ status) {
+  __shared__ float colbuf[2][NB];
+  __shared__ float rowbuf[2][NB];
+  __shared__ int bad;
+  const int tx = threadIdx.x & 31, ty = threadIdx.x >> 5;
+  if (threadIdx.x == 0) bad = 0;
+  float v[4][4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i)
+#pragma unroll
+    for (int t = 0; t < 4; ++t) {
+      const int r = 4 * ty + i, c = 4 * tx + t;
+      v[i][t] = (r < kb && c < kb) ? ((c <= r) ? a[r * lda + c] : 0.f) : ((r == c) ? 1.f : 0.f);
+    }
   __syncthreads();
-  for (int e = tid; e < kb * kb; e += blockDim.x) {
-    int r = e / kb, c = e % kb;
-    a[(b0 + r) * lda + b0 + c] = sinv[r][c];
-  }
+  chol_regs(v, kb, &bad, colbuf);
+#pragma unroll
+  for (int i = 0; i < 4; ++i)
+#pragma unroll
+    for (int t = 0; t < 4; ++t) {
+      const int r = 4 * ty + i, c = 4 * tx + t;
+      if (r < kb && c < kb) a[r * lda + c] = (c <= r) ? v[i][t] : 0.f;
+    }
+  float x[4][4];
+  __syncthreads();
+  trinv_regs(v, x, colbuf, rowbuf);
+#pragma unroll
+  for (int i = 0; i < 4; ++i)
+#pragma unroll
+    for (int t = 0; t < 4; ++t) {
+      const int r = 4 * ty + i, c = 4 * tx + t;
+      inv[r * NB + c] = (r < kb && c < kb && c <= r) ? x[i][t] : 0.f;
+    }
+  __syncthreads();
+  if (threadIdx.x == 0 && bad) atomicExch(status, GQ_DEVERR_NOTPD);
+}
+
+// Batched in-place inverse of the NB x NB lower-triangular diagonal blocks of a.
+__global__ void __launch_bounds__(DIAG_THREADS)
+trinv_diag_blocks_kernel(float* __restrict__ a, int64_t n, int64_t lda) {
+  __shared__ float colbuf[2][NB];
+  __shared__ float rowbuf[2][NB];
+  const int tx = threadIdx.x & 31, ty = threadIdx.x >> 5;
+  const int64_t b0 = (int64_t)blockIdx.x * NB;
+  const int kb = (int)min((int64_t)NB, n - b0);
+  float v[4][4], x[4][4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i)
+#pragma unroll
+    for (int t = 0; t < 4; ++t) {
+      const int r = 4 * ty + i, c = 4 * tx + t;
+      v[i][t] = (r < kb && c < kb) ? ((c <= r) ? a[(b0 + r) * lda + b0 + c] : 0.f)
+                                   : ((r == c) ? 1.f : 0.f);
+    }
+  trinv_regs(v, x, colbuf, rowbuf);
+#pragma unroll
+  for (int i = 0; i < 4; ++i)
+#pragma unroll
+    for (int t = 0; t < 4; ++t) {
+      const int r = 4 * ty + i, c = 4 * tx + t;
+      if (r < kb && c < kb) a[(b0 + r) * lda + b0 + c] = (c <= r) ? x[i][t] : 0.f;
+    }
 }
 
 // Zero the strict upper triangle of an n x n matrix (ld).
@@ -234,13 +313,21 @@ __global__ void reverse_copy_kernel(const float* __restrict__ linv, int64_t n, i
     u[i * ldu + j] = linv[(n - 1 - i) * ldl + (n - 1 - j)];
 }
 
-// Blocked lower Cholesky of a (n x n, ld n) in place; panel scratch p (n x 64),
-// diagonal-inverse scratch dinv (64 x 64).
+// Blocked lower Cholesky of a (n x n, ld n) in place; panel scratch p (n x NB),
+// diagonal-inverse scratch dinv (NB x NB).
 int cholesky_lower(float* a, int64_t n, float* p, float* dinv, int* status, cudaStream_t st) {
+  static bool attr = false;
+  if (!attr) {
+    GQ_CHECK_CUDA(cudaFuncSetAttribute(potrf_diag_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       (int)DIAG_SMEM));
+    GQ_CHECK_CUDA(cudaFuncSetAttribute(trinv_diag_blocks_kernel,
+                                       cudaFuncAttributeMaxDynamicSharedMemorySize, (int)DIAG_SMEM));
+    attr = true;
+  }
   for (int64_t k0 = 0; k0 < n; k0 += NB) {
     int kb = (int)std::min<int64_t>(NB, n - k0);
     float* akk = a + k0 * n + k0;
-    potrf_diag_kernel<<<1, 256, 0, st>>>(akk, n, kb, dinv, status);
+    potrf_diag_kernel<<<1, DIAG_THREADS, DIAG_SMEM, st>>>(akk, n, kb, dinv, status);
     GQ_TRY(check_launch("potrf_diag"));
     int64_t rem = n - k0 - kb;
     if (rem <= 0) break;
@@ -256,9 +343,15 @@ int cholesky_lower(float* a, int64_t n, float* p, float* dinv, int* status, cuda
   return GQ_OK;
 }
 
+int transpose2d(const float* src, int64_t rows, int64_t cols, int64_t lds, float* dst, int64_t ldd,
+                cudaStream_t st);
+
 // Recursive lower-triangular inverse of a[0:n, 0:n] (ld lda) in place.  The
-// 64x64 diagonal blocks must already be inverted; the strict upper triangle
-// must be zero.  scratch: at least (n/2 + 64) * (n/2 + 64) floats.
+// NB x NB diagonal blocks must already be inverted; the strict upper triangle
+// must be zero.  With [[L11, 0], [L21, L22]]^-1 = [[X11, 0], [X21, X22]],
+// X21 = -X22 L21 X11, evaluated as two products whose operands are both
+// K-major (tensor-core GEMM path):  Tt = X11^T L21^T,  X21 = -X22 Tt^T.
+// scratch: at least (n/2 + 64) * (n + 64) floats.
 int trinv_rec(float* a, int64_t n, int64_t lda, float* scratch, cudaStream_t st) {
   if (n <= NB) return GQ_OK;
   int64_t n1 = ((n / 2 + NB - 1) / NB) * NB;
@@ -269,16 +362,17 @@ int trinv_rec(float* a, int64_t n, int64_t lda, float* scratch, cudaStream_t st)
   float* a22 = a + n1 * lda + n1;
   GQ_TRY(trinv_rec(a11, n1, lda, scratch, st));
   GQ_TRY(trinv_rec(a22, n2, lda, scratch, st));
-  // T = L21 * L11^-1  (n2 x n1)
-  GQ_TRY(sgemm(0, 0, n2, n1, n1, 1.f, a21, lda, a11, lda, 0.f, scratch, n1, 0, st));
-  // X21 = -L22^-1 * T
-  GQ_TRY(sgemm(0, 0, n2, n1, n2, -1.f, a22, lda, scratch, n1, 0.f, a21, lda, 0, st));
+  float* s1 = scratch;            // X11^T, n1 x n1
+  float* tt = scratch + n1 * n1;  // Tt = (L21 X11)^T, n1 x n2
+  GQ_TRY(transpose2d(a11, n1, n1, lda, s1, n1, st));
+  GQ_TRY(sgemm(0, 1, n1, n2, n1, 1.f, s1, n1, a21, lda, 0.f, tt, n2, 0, st));
+  GQ_TRY(sgemm(0, 1, n2, n1, n2, -1.f, a22, lda, tt, n2, 0.f, a21, lda, 0, st));
   return GQ_OK;
 }
 
 int64_t hessian_ws_floats(int64_t d) {
   int64_t half = d / 2 + NB;
-  return d * d + d * NB + NB * NB + half * half + 64;
+  return d * d + d * NB + NB * NB + half * (d + NB) + 64;
 }
 
 }  // namespace gq
@@ -311,9 +405,9 @@ int gq_hessian_factor(const float* h, int64_t d, int64_t ldh, const int32_t* per
   float* ht = ws;                                  // d*d
   float* p = ht + d * d;                           // d*64
   float* dinv = p + d * gq::NB;                    // 64*64
-  float* scratch = dinv + gq::NB * gq::NB;         // (d/2+64)^2
+  float* scratch = dinv + gq::NB * gq::NB;         // (d/2+64) x (d+64)
   int64_t half = d / 2 + gq::NB;
-  float* mean = scratch + half * half;             // 1 float
+  float* mean = scratch + half * (d + gq::NB);     // 1 float
   int* status = reinterpret_cast<int*>(mean + 16);  // 1 int
 
   gq::diag_mean_kernel<<<1, 1024, 0, st>>>(h, d, ldh, mean);
@@ -333,7 +427,8 @@ int gq_hessian_factor(const float* h, int64_t d, int64_t ldh, const int32_t* per
     dim3 gz((unsigned)std::min<int64_t>(gq::ceil_div(d, 256), 64), (unsigned)d);
     gq::zero_upper_kernel<<<gz, 256, 0, st>>>(ht, d, d);
     GQ_TRY(gq::check_launch("zero_upper"));
-    gq::trinv_diag_blocks_kernel<<<(unsigned)gq::ceil_div(d, gq::NB), 256, 0, st>>>(ht, d, d);
+    gq::trinv_diag_blocks_kernel<<<(unsigned)gq::ceil_div(d, gq::NB), gq::DIAG_THREADS,
+                                   gq::DIAG_SMEM, st>>>(ht, d, d);
     GQ_TRY(gq::check_launch("trinv_diag_blocks"));
     GQ_TRY(gq::trinv_rec(ht, d, d, scratch, st));
     dim3 g2((unsigned)std::min<int64_t>(gq::ceil_div(d, 256), 64), (unsigned)d);

@@ -128,8 +128,31 @@ sgemm_kernel(int64_t M, int64_t N, int64_t K, float alpha, const float* __restri
   }
 }
 
+namespace tc32 {
+bool eligible(int ta, int tb, int64_t M, int64_t N, int64_t K, const float* A, int64_t lda,
+              const float* B, int64_t ldb, const float* C, int64_t ldc);
+int launch(int tb, int64_t M, int64_t N, int64_t K, float alpha, const float* A, int64_t lda,
+           const float* B, int64_t ldb, float beta, float* C, int64_t ldc, int uplo,
+           cudaStream_t st);
+}  // namespace tc32
+
+int sgemm_simt(int ta, int tb, int64_t M, int64_t N, int64_t K, float alpha, const float* A,
+               int64_t lda, const float* B, int64_t ldb, float beta, float* C, int64_t ldc,
+               int uplo, cudaStream_t st);
+
+// fp32 GEMM used throughout the library: the tcgen05 3xTF32 kernel when the
+// shape and alignment allow it, the CUDA-core kernel otherwise.
 int sgemm(int ta, int tb, int64_t M, int64_t N, int64_t K, float alpha, const float* A, int64_t lda,
           const float* B, int64_t ldb, float beta, float* C, int64_t ldc, int uplo, cudaStream_t st) {
+  if (M == 0 || N == 0) return GQ_OK;
+  if (tc32::eligible(ta, tb, M, N, K, A, lda, B, ldb, C, ldc))
+    return tc32::launch(tb, M, N, K, alpha, A, lda, B, ldb, beta, C, ldc, uplo, st);
+  return sgemm_simt(ta, tb, M, N, K, alpha, A, lda, B, ldb, beta, C, ldc, uplo, st);
+}
+
+int sgemm_simt(int ta, int tb, int64_t M, int64_t N, int64_t K, float alpha, const float* A,
+               int64_t lda, const float* B, int64_t ldb, float beta, float* C, int64_t ldc,
+               int uplo, cudaStream_t st) {
   if (M == 0 || N == 0) return GQ_OK;
   dim3 grid((unsigned)ceil_div(N, SG_BN), (unsigned)ceil_div(M, SG_BM));
   if (grid.y > 65535) return fail(GQ_EUNSUPPORTED, "gq_sgemm: M=%lld too large", (long long)M);
@@ -158,6 +181,17 @@ int gq_sgemm(int trans_a, int trans_b, int64_t M, int64_t N, int64_t K, float al
   GQ_REQUIRE(ldb >= (trans_b ? K : N), "gq_sgemm: ldb too small");
   return gq::sgemm(trans_a ? 1 : 0, trans_b ? 1 : 0, M, N, K, alpha, a, lda, b, ldb, beta, c, ldc,
                    uplo, gq::as_stream(stream));
+}
+
+int gq_sgemm_simt(int trans_a, int trans_b, int64_t M, int64_t N, int64_t K, float alpha,
+                  const float* a, int64_t lda, const float* b, int64_t ldb, float beta, float* c,
+                  int64_t ldc, int uplo, void* stream) {
+  GQ_REQUIRE(M >= 0 && N >= 0 && K >= 0, "gq_sgemm_simt: negative size");
+  GQ_REQUIRE(uplo >= 0 && uplo <= 2, "gq_sgemm_simt: uplo must be 0, 1 or 2");
+  GQ_REQUIRE(ldc >= N && lda >= (trans_a ? M : K) && ldb >= (trans_b ? K : N),
+             "gq_sgemm_simt: leading dimension too small");
+  return gq::sgemm_simt(trans_a ? 1 : 0, trans_b ? 1 : 0, M, N, K, alpha, a, lda, b, ldb, beta, c,
+                        ldc, uplo, gq::as_stream(stream));
 }
 
 int gq_syrk_f32(const float* x, int64_t tokens, int64_t d, int64_t ldx, float* h, int64_t ldh,

@@ -8,11 +8,11 @@
 // err [m, 128] float32 -- the scaled errors of the current block.
 //
 // Per 128-column block:
-//   1. sweep_block_kernel: a warp owns ROWS rows; lane l holds columns
-//      4l..4l+3 of each in registers; the block of U lives in shared memory.
-//      For each column i the current value is broadcast from its owner lane,
-//      every lane quantizes it redundantly (no divergence), and the error
-//      (w - dq) / U_ii is applied to the lane's columns > i.
+//   1. sweep_block_kernel: a warp owns 4 rows; lane l holds columns 4l..4l+3
+//      of each in registers; the block of U lives in shared memory.  For each
+//      column i, lane r < 4 gathers row r's current value, quantizes it once,
+//      writes the code / dequantized value / error and broadcasts the error
+//      (w - dq) / U_ii, which every lane applies to its columns > i.
 //   2. wp[:, b1:] -= err @ U[b0:b1, b1:]  (fp32 GEMM).
 // Finally codes/dequant are scattered back to original column order.
 #include "gq_common.cuh"
@@ -25,8 +25,8 @@ int sgemm(int ta, int tb, int64_t M, int64_t N, int64_t K, float alpha, const fl
 int check_quant_args(const char* who, int64_t m, int64_t n, int w_bits, int group_size, int sym);
 
 constexpr int SW_BLOCK = 128;
-constexpr int SW_ROWS = 2;        // rows per warp
-constexpr int SW_WARPS = 8;       // warps per CTA
+constexpr int SW_ROWS = 4;        // rows per warp (lane r < 4 quantizes row r)
+constexpr int SW_WARPS = 4;       // warps per CTA
 constexpr int SW_ROWS_CTA = SW_ROWS * SW_WARPS;
 
 inline int64_t round4(int64_t n) { return (n + 3) & ~int64_t(3); }
@@ -110,30 +110,30 @@ sweep_block_kernel(SweepArgs a) {
   for (int i = threadIdx.x; i < SW_BLOCK; i += blockDim.x) udinv[i] = (i < bw) ? 1.f / us[i][i] : 0.f;
   __syncthreads();
 
+  // Lane l holds columns 4l..4l+3 of the warp's SW_ROWS rows; lane r < SW_ROWS
+  // additionally "owns" row r: it quantizes that row's current column and
+  // writes its outputs, so every quantization is computed exactly once.
   const int64_t row_base = (int64_t)blockIdx.x * SW_ROWS_CTA + warp * SW_ROWS;
+  const bool row_lane = lane < SW_ROWS;
+  const int64_t my_row = row_base + lane;
+  const bool my_valid = row_lane && my_row < a.m;
   float w[SW_ROWS][4];
-  float e[SW_ROWS][4];
-  uint32_t codes[SW_ROWS];
-  float scale[SW_ROWS], zero[SW_ROWS];
-  bool valid[SW_ROWS];
 #pragma unroll
   for (int r = 0; r < SW_ROWS; ++r) {
     const int64_t row = row_base + r;
-    valid[r] = row < a.m;
-    codes[r] = 0;
-    scale[r] = 1.f;
-    zero[r] = 0.f;
-#pragma unroll
-    for (int t = 0; t < 4; ++t) e[r][t] = 0.f;
     float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
-    if (valid[r] && 4 * lane < bw)
+    if (row < a.m && 4 * lane < bw)
       v = *reinterpret_cast<const float4*>(a.wp + row * a.ldp + a.b0 + 4 * lane);
     w[r][0] = v.x; w[r][1] = v.y; w[r][2] = v.z; w[r][3] = v.w;
-    if (a.g > SW_BLOCK && valid[r]) {
-      scale[r] = a.big_scale[row];
-      zero[r] = a.big_zero[row];
-    }
   }
+  float my_scale = 1.f, my_zero = 0.f;
+  if (a.g > SW_BLOCK && my_valid) {
+    my_scale = a.big_scale[my_row];
+    my_zero = a.big_zero[my_row];
+  }
+  float* wrow = my_valid ? a.wp + my_row * a.ldp + a.b0 : nullptr;
+  uint8_t* crow = my_valid ? a.cp + my_row * a.ldp + a.b0 : nullptr;
+  float* erow = my_valid ? a.err + my_row * SW_BLOCK : nullptr;
   const int seg = (a.g <= SW_BLOCK) ? (a.g >> 2) : 32;  // lanes per group inside a block
 
   for (int i4 = 0; i4 < bw; i4 += 4) {
@@ -142,10 +142,11 @@ sweep_block_kernel(SweepArgs a) {
     for (int sub = 0; sub < 4; ++sub) {
       const int i = i4 + sub;
       if (i >= bw) break;
-      const int64_t col = a.b0 + i;
       // group parameters at the group's first column, from the current values
-      if (a.g <= SW_BLOCK && (col % a.g) == 0) {
-        const int64_t gi = col / a.g;
+      // (g divides 128 here and blocks start on group boundaries, so the test
+      // on the block-local index is a mask)
+      if (a.g <= SW_BLOCK && (i & (a.g - 1)) == 0) {
+        const int64_t gi = (a.b0 + i) / a.g;
 #pragma unroll
         for (int r = 0; r < SW_ROWS; ++r) {
           float mn = INFINITY, mx = -INFINITY, ma = 0.f;
@@ -165,55 +166,52 @@ sweep_block_kernel(SweepArgs a) {
           mn = __shfl_sync(0xffffffffu, mn, owner);
           mx = __shfl_sync(0xffffffffu, mx, owner);
           ma = __shfl_sync(0xffffffffu, ma, owner);
-          float s, z;
-          if (gi == 0 && a.group0_scale != nullptr) {
-            s = valid[r] ? a.group0_scale[row_base + r] : 1.f;
-            z = valid[r] ? a.group0_zero[row_base + r] : 0.f;
-          } else if (a.sym) {
-            group_scale_zero(-ma, ma, a.qp, a.sym, s, z);
-          } else {
-            group_scale_zero(mn, mx, a.qp, a.sym, s, z);
-          }
-          scale[r] = s;
-          zero[r] = z;
-          if (lane == 0 && valid[r] && a.scales) {
-            a.scales[(row_base + r) * a.n_groups + gi] = s;
-            a.zeros[(row_base + r) * a.n_groups + gi] = z;
+          if (lane == r) {
+            float s, z;
+            if (gi == 0 && a.group0_scale != nullptr) {
+              s = my_valid ? a.group0_scale[my_row] : 1.f;
+              z = my_valid ? a.group0_zero[my_row] : 0.f;
+            } else if (a.sym) {
+              group_scale_zero(-ma, ma, a.qp, a.sym, s, z);
+            } else {
+              group_scale_zero(mn, mx, a.qp, a.sym, s, z);
+            }
+            my_scale = s;
+            my_zero = z;
+            if (my_valid && a.scales) {
+              a.scales[my_row * a.n_groups + gi] = s;
+              a.zeros[my_row * a.n_groups + gi] = z;
+            }
           }
         }
       }
-      const float dinv = udinv[i];
-      const bool prop = col >= a.noprop_cols;
-      float4 urow = *reinterpret_cast<const float4*>(&us[i][4 * lane]);
-      float uv[4] = {urow.x, urow.y, urow.z, urow.w};
+      // gather column i of each row into its row lane
+      float mine = 0.f;
 #pragma unroll
       for (int r = 0; r < SW_ROWS; ++r) {
-        float wi = __shfl_sync(0xffffffffu, w[r][sub], owner);
-        float dq;
-        float q = quantize_one(wi, scale[r], zero[r], a.qp, dq);
-        float err = prop ? __fmul_rn(__fsub_rn(wi, dq), dinv) : 0.f;
-        if (lane == owner) {
-          w[r][sub] = dq;
-          e[r][sub] = err;
-          codes[r] |= ((uint32_t)(int)(q - a.qp.qmin) & 0xffu) << (8 * sub);
-        }
+        const float v = __shfl_sync(0xffffffffu, w[r][sub], owner);
+        if (lane == r) mine = v;
+      }
+      const bool prop = a.b0 + i >= a.noprop_cols;
+      float dq;
+      const float q = quantize_one(mine, my_scale, my_zero, a.qp, dq);
+      const float my_err = prop ? __fmul_rn(__fsub_rn(mine, dq), udinv[i]) : 0.f;
+      if (my_valid) {
+        wrow[i] = dq;
+        crow[i] = (uint8_t)(int)(q - a.qp.qmin);
+        erow[i] = my_err;
+      }
+      const float4 urow = *reinterpret_cast<const float4*>(&us[i][4 * lane]);
+      const float uv[4] = {urow.x, urow.y, urow.z, urow.w};
+#pragma unroll
+      for (int r = 0; r < SW_ROWS; ++r) {
+        const float err = __shfl_sync(0xffffffffu, my_err, r);
 #pragma unroll
         for (int t = 0; t < 4; ++t) {
           if (4 * lane + t > i) w[r][t] = fmaf(-err, uv[t], w[r][t]);
         }
       }
     }
-  }
-
-#pragma unroll
-  for (int r = 0; r < SW_ROWS; ++r) {
-    const int64_t row = row_base + r;
-    if (!valid[r] || 4 * lane >= bw) continue;
-    *reinterpret_cast<float4*>(a.wp + row * a.ldp + a.b0 + 4 * lane) =
-        make_float4(w[r][0], w[r][1], w[r][2], w[r][3]);
-    *reinterpret_cast<uint32_t*>(a.cp + row * a.ldp + a.b0 + 4 * lane) = codes[r];
-    *reinterpret_cast<float4*>(a.err + row * SW_BLOCK + 4 * lane) =
-        make_float4(e[r][0], e[r][1], e[r][2], e[r][3]);
   }
 }
 
@@ -242,10 +240,19 @@ __global__ void g_idx_kernel(const int32_t* __restrict__ perm, int64_t n, int g,
   if (j < n) g_idx[perm ? perm[j] : j] = (int32_t)(j / g);
 }
 
-int64_t sweep_ws_bytes(int64_t m, int64_t n) {
+// Byte offset of the transposed U band (after wp, cp, err, bscale, bzero).
+inline int64_t sweep_ubt_offset(int64_t m, int64_t n) {
   int64_t ldp = round4(n);
-  return m * ldp * 4 + m * ldp + m * SW_BLOCK * 4 + 2 * m * 4 + 256;
+  int64_t off = m * ldp * 4 + ((m * ldp + 15) & ~int64_t(15)) + m * SW_BLOCK * 4 + 2 * m * 4;
+  return (off + 255) & ~int64_t(255);
 }
+
+int64_t sweep_ws_bytes(int64_t m, int64_t n) {
+  return sweep_ubt_offset(m, n) + n * SW_BLOCK * 4 + 256;
+}
+
+int transpose2d(const float* src, int64_t rows, int64_t cols, int64_t lds, float* dst, int64_t ldd,
+                cudaStream_t st);
 
 }  // namespace gq
 
@@ -284,6 +291,7 @@ int gq_gptq_sweep(const float* w, int64_t m, int64_t n, int64_t ldw, const float
   float* err = reinterpret_cast<float*>(ws + m * ldp * 4 + ((m * ldp + 15) & ~int64_t(15)));
   float* bscale = err + m * SW_BLOCK;
   float* bzero = bscale + m;
+  float* ubt = reinterpret_cast<float*>(ws + sweep_ubt_offset(m, n));  // [n, 128]
 
   if (start) {
     GQ_CHECK_CUDA(cudaMemcpy2DAsync(wp, ldp * 4, start, n * 4, n * 4, m, cudaMemcpyDeviceToDevice, st));
@@ -333,8 +341,11 @@ int gq_gptq_sweep(const float* w, int64_t m, int64_t n, int64_t ldw, const float
     GQ_TRY(check_launch("sweep_block"));
     const int64_t b1 = b0 + bw;
     if (b1 < n) {
-      GQ_TRY(sgemm(0, 0, m, n - b1, bw, -1.f, err, SW_BLOCK, u + b0 * ldu + b1, ldu, 1.f, wp + b1,
-                   ldp, 0, st));
+      // wp[:, b1:] -= err @ U[b0:b1, b1:], with the U band transposed so that
+      // both GEMM operands are K-major (tensor-core path)
+      GQ_TRY(transpose2d(u + b0 * ldu + b1, bw, n - b1, ldu, ubt, SW_BLOCK, st));
+      GQ_TRY(sgemm(0, 1, m, n - b1, bw, -1.f, err, SW_BLOCK, ubt, SW_BLOCK, 1.f, wp + b1, ldp, 0,
+                   st));
     }
   }
   if (dequant || codes) {

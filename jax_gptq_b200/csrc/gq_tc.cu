@@ -454,6 +454,10 @@ int launch(const void* xa, int64_t lda, const void* xb, int64_t ldb, int64_t K, 
 
 int symmetrize_upper(float* h, int64_t d, int64_t ldh, cudaStream_t st);
 
+namespace tc32 {
+int read_status(int reset, int* out);
+}
+
 }  // namespace gq
 
 extern "C" {
@@ -487,7 +491,9 @@ int gq_device_status(int* status_out, int reset, void* stream) {
     int z = 0;
     GQ_CHECK_CUDA(cudaMemcpyToSymbol(gq::g_device_status, &z, sizeof(int)));
   }
-  *status_out = v;
+  int v32 = 0;
+  GQ_TRY(gq::tc32::read_status(reset, &v32));
+  *status_out = v ? v : v32;
   return GQ_OK;
 }
 

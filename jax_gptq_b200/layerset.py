@@ -137,9 +137,28 @@ class _Timer:
         return out
 
 
+def _members(shapes, grp):
+    return [(name, m) for name, m, _, g in shapes if g == grp]
+
+
+def _split_rows(res: SweepResult, members) -> dict:
+    """Per-linear views of a sweep run on row-stacked weights."""
+    out, r0 = {}, 0
+    for name, m in members:
+        out[name] = SweepResult(res.dequant[r0:r0 + m], res.codes[r0:r0 + m],
+                                res.scales[r0:r0 + m], res.zeros[r0:r0 + m], res.g_idx, res.perm)
+        r0 += m
+    return out
+
+
 def quantize_layer_gptq(weights: dict, inputs: dict, cfg: QuantConfig, shapes=LLAMA2_7B,
                         timed: bool = False):
-    """GPTQ for every linear of a layer set.  ``inputs[group]`` = bf16 X on the device."""
+    """GPTQ for every linear of a layer set.  ``inputs[group]`` = bf16 X on the device.
+
+    Linears that share an input also share the Hessian factor, and their rows
+    are independent, so they are swept together as one row-stacked matrix
+    (more rows in flight per column step).
+    """
     tm = _Timer(timed)
     factors: dict[str, HessianFactor] = {}
     for grp, x in inputs.items():
@@ -151,17 +170,21 @@ def quantize_layer_gptq(weights: dict, inputs: dict, cfg: QuantConfig, shapes=LL
         factors[grp] = factor_hessian(h, cfg)
         del h
     results: dict[str, SweepResult] = {}
-    for name, _, _, grp in shapes:
-        tm.mark(f"sweep:{name}")
+    for grp in inputs:
+        members = _members(shapes, grp)
+        tm.mark(f"sweep:{grp}")
         f = factors[grp]
-        results[name] = gptq_sweep(weights[name], f.u, f.perm, cfg)
+        w = weights[members[0][0]] if len(members) == 1 else \
+            torch.cat([weights[name] for name, _ in members], dim=0)
+        results.update(_split_rows(gptq_sweep(w, f.u, f.perm, cfg), members))
     tm.mark("end")
     return results, _collect(tm)
 
 
 def quantize_layer_qronos(weights: dict, inputs_float: dict, inputs_quant: dict,
                           cfg: QuantConfig, shapes=LLAMA2_7B, timed: bool = False):
-    """Qronos for every linear: ``h = Xt^T Xt``, ``g = X^T Xt`` per input group."""
+    """Qronos for every linear: ``h = Xt^T Xt``, ``g = X^T Xt`` per input group;
+    linears sharing an input are updated together as one row-stacked matrix."""
     tm = _Timer(timed)
     facts = {}
     for grp, xq in inputs_quant.items():
@@ -175,11 +198,13 @@ def quantize_layer_qronos(weights: dict, inputs_float: dict, inputs_quant: dict,
         facts[grp] = (factor_hessian(h, cfg, want_hd=True), g)
         del h
     results = {}
-    for name, _, _, grp in shapes:
-        tm.mark(f"sweep:{name}")
+    for grp in inputs_quant:
+        members = _members(shapes, grp)
+        tm.mark(f"sweep:{grp}")
         f, g = facts[grp]
-        w = weights[name]
-        results[name] = qronos_quantize(w, w, None, g, cfg, factor=f)
+        w = weights[members[0][0]] if len(members) == 1 else \
+            torch.cat([weights[name] for name, _ in members], dim=0)
+        results.update(_split_rows(qronos_quantize(w, w, None, g, cfg, factor=f), members))
     tm.mark("end")
     return results, _collect(tm)
 
@@ -199,11 +224,12 @@ def quantize_layer_gptq_host(weights_host: dict, inputs_host: dict, cfg: QuantCo
     """GPTQ layer set from host buffers to host results.
 
     Activations (bf16) and weights (float32) are copied from (pinned) host
-    memory on a copy stream in the order the computation needs them, so the
-    transfer of the next input group overlaps the tensor-core work on the
-    current one; codes, scales and zeros stream back on a second copy stream.
-    Returns ``({name: (codes, scales, zeros, g_idx, perm)}, {"h2d": bytes,
-    "d2h": bytes})`` with host tensors.
+    memory on a copy stream in the order the computation needs them -- the
+    weights of linears sharing an input straight into one row-stacked device
+    buffer -- so the transfer of the next input group overlaps the tensor-core
+    work on the current one; codes, scales and zeros stream back on a second
+    copy stream.  Returns ``({name: (codes, scales, zeros, g_idx, perm)},
+    {"h2d": bytes, "d2h": bytes})`` with host tensors.
     """
     compute = torch.cuda.current_stream()
     h2d, d2h = _copy_streams()
@@ -212,26 +238,26 @@ def quantize_layer_gptq_host(weights_host: dict, inputs_host: dict, cfg: QuantCo
     h2d.wait_event(start)
     nbytes = {"h2d": 0, "d2h": 0}
     dev_x, dev_w, ready_x, ready_w = {}, {}, {}, {}
-    order = []
-    for grp in inputs_host:
-        order.append(("x", grp))
-        for name, _, _, g in shapes:
-            if g == grp:
-                order.append(("w", name))
     with torch.cuda.stream(h2d):
-        for kind, key in order:
-            src = inputs_host[key] if kind == "x" else weights_host[key]
+        for grp, src in inputs_host.items():
             dst = torch.empty(src.shape, dtype=src.dtype, device="cuda")
             dst.copy_(src, non_blocking=True)
             ev = torch.cuda.Event()
             ev.record(h2d)
             nbytes["h2d"] += src.numel() * src.element_size()
-            if kind == "x":
-                dev_x[key], ready_x[key] = dst, ev
-            else:
-                dev_w[key], ready_w[key] = dst, ev
-    factors = {}
-    results = {}
+            dev_x[grp], ready_x[grp] = dst, ev
+            members = _members(shapes, grp)
+            n = weights_host[members[0][0]].shape[1]
+            wdev = torch.empty((sum(m for _, m in members), n), dtype=torch.float32, device="cuda")
+            r0 = 0
+            for name, m in members:
+                wsrc = weights_host[name]
+                wdev[r0:r0 + m].copy_(wsrc, non_blocking=True)
+                nbytes["h2d"] += wsrc.numel() * wsrc.element_size()
+                r0 += m
+            ev = torch.cuda.Event()
+            ev.record(h2d)
+            dev_w[grp], ready_w[grp] = wdev, ev
     out = {}
     for grp in inputs_host:
         compute.wait_event(ready_x[grp])
@@ -240,29 +266,28 @@ def quantize_layer_gptq_host(weights_host: dict, inputs_host: dict, cfg: QuantCo
         d = x.shape[1]
         h = torch.empty((d, d), dtype=torch.float32, device="cuda")
         stats.syrk_into(h, x, accumulate=False)
-        factors[grp] = factor_hessian(h, cfg)
+        f = factor_hessian(h, cfg)
         del h
-        for name, _, _, g in shapes:
-            if g != grp:
-                continue
-            compute.wait_event(ready_w[name])
-            w = dev_w[name]
-            w.record_stream(compute)
-            f = factors[grp]
-            res = gptq_sweep(w, f.u, f.perm, cfg)
-            results[name] = res
-            done = torch.cuda.Event()
-            done.record(compute)
-            d2h.wait_event(done)
-            with torch.cuda.stream(d2h):
-                host = []
-                for t in (res.codes, res.scales, res.zeros, res.g_idx, res.perm):
-                    t.record_stream(d2h)
-                    hb = torch.empty(t.shape, dtype=t.dtype, pin_memory=True)
-                    hb.copy_(t, non_blocking=True)
-                    nbytes["d2h"] += t.numel() * t.element_size()
-                    host.append(hb)
-                out[name] = tuple(host)
+        compute.wait_event(ready_w[grp])
+        w = dev_w[grp]
+        w.record_stream(compute)
+        res = gptq_sweep(w, f.u, f.perm, cfg)
+        done = torch.cuda.Event()
+        done.record(compute)
+        d2h.wait_event(done)
+        with torch.cuda.stream(d2h):
+            host = []
+            for t in (res.codes, res.scales, res.zeros, res.g_idx, res.perm):
+                t.record_stream(d2h)
+                hb = torch.empty(t.shape, dtype=t.dtype, pin_memory=True)
+                hb.copy_(t, non_blocking=True)
+                nbytes["d2h"] += t.numel() * t.element_size()
+                host.append(hb)
+        r0 = 0
+        for name, m in _members(shapes, grp):
+            out[name] = (host[0][r0:r0 + m], host[1][r0:r0 + m], host[2][r0:r0 + m], host[3],
+                         host[4])
+            r0 += m
     fin = torch.cuda.Event()
     fin.record(d2h)
     compute.wait_event(fin)
