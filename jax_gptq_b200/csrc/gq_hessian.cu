@@ -5,15 +5,14 @@
 //
 // U is computed without forming Hd^-1: with J the exchange matrix, factor
 // J Hd J = L L^T (lower Cholesky), so Hd = R R^T with R = J L J upper, and
-// Hd^-1 = (R^-1)^T R^-1, i.e. U = R^-1 = J L^-1 J.  Cost: one blocked
-// Cholesky (n^3/3) plus one triangular inverse, all in float32.
+// Hd^-1 = (R^-1)^T R^-1, i.e. U = R^-1 = J L^-1 J.  Cost: n^3/3 for the
+// Cholesky plus n^3/3 for the triangular inverse, all in float32.
 //
-// Blocked right-looking Cholesky, panel width 128: a single-CTA kernel factors
-// the diagonal block in shared memory (flagging a non-positive or non-finite
-// pivot in a device status word instead of producing NaNs) and inverts it;
-// the panel solve and the trailing rank-64 update are fp32 GEMMs.  The
-// triangular inverse is recursive (X21 = -L22^-1 L21 L11^-1) with all 128x128
-// diagonal blocks inverted by one batched launch.
+// L^-1 is computed by one recursion that interleaves both (inv_chol_rec):
+// its leaves are 128 x 128 diagonal blocks, factored and inverted by a
+// single-CTA kernel in shared memory (a non-positive or non-finite pivot sets
+// a device status word instead of producing NaNs); everything else is fp32
+// tensor-core GEMMs whose K is half the current size.
 #include "gq_common.cuh"
 
 #include <algorithm>
@@ -23,6 +22,9 @@ namespace gq {
 
 int sgemm(int ta, int tb, int64_t M, int64_t N, int64_t K, float alpha, const float* A, int64_t lda,
           const float* B, int64_t ldb, float beta, float* C, int64_t ldc, int uplo, cudaStream_t st);
+int sgemm_tri(int ta, int tb, int64_t M, int64_t N, int64_t K, float alpha, const float* A,
+              int64_t lda, const float* B, int64_t ldb, float beta, float* C, int64_t ldc, int tri,
+              cudaStream_t st);
 
 // ---------------------------------------------------------------------------
 // Act-order permutation by ranking: element i goes to position
@@ -120,180 +122,167 @@ __global__ void damp_permute_kernel(const float* __restrict__ h, int64_t n, int6
 }
 
 // ---------------------------------------------------------------------------
-// Diagonal blocks of NB x NB are factored and inverted by one 1024-thread CTA
-// with the block held in registers: thread (ty, tx) of a 32 x 32 grid owns the
-// 4 x 4 tile rows 4ty..4ty+3, columns 4tx..4tx+3.  Each elimination step
-// publishes one column (and for the inverse one row) through double-buffered
-// shared memory, so a step costs one barrier, eight shared loads and sixteen
-// register FMAs per thread; warps whose tiles are finished skip the update.
+// Diagonal blocks of NB x NB are factored and inverted by one 512-thread CTA
+// in shared memory, in four sub-panels of 32 columns (right-looking):
+//   1. warp 0 factors the 32 x 32 diagonal sub-block with lane i holding row i
+//      in registers (columns published by warp shuffles, no block barrier),
+//      then inverts it with lane c solving L x = e_c;
+//   2. all warps form the panel below, L21 = A21 X11^T (X11 = L11^-1);
+//   3. all warps apply the rank-32 trailing update A22 -= L21 L21^T.
+// The 128 x 128 inverse is then completed block row by block row,
+// X_ij = -X_ii sum_k L_ik X_kj.  The block's inverse (not L) is written back:
+// the panel solve below and the triangular inverse of the whole factor only
+// need L^-1 on the diagonal.
 constexpr int NB = 128;
-constexpr int DIAG_THREADS = 1024;
-constexpr size_t DIAG_SMEM = 0;
+constexpr int SUB = 32;
+constexpr int DIAG_THREADS = 512;
+constexpr int DP = NB + 1;  // shared-memory pitch: row-strided lane reads hit distinct banks
+constexpr size_t DIAG_SMEM = (size_t)(2 * NB + SUB) * DP * sizeof(float) + SUB * sizeof(float);
 
-// Lower Cholesky of v (the kb x kb block; identity beyond kb), in place.  A
-// pivot that is not > 0 (or not finite) sets *bad and continues with 1.
-__device__ void chol_regs(float (&v)[4][4], int kb, int* bad, float (*colbuf)[NB]) {
-  const int tx = threadIdx.x & 31, ty = threadIdx.x >> 5;
-  for (int j = 0; j < NB; ++j) {
-    float* col = colbuf[j & 1];
-    if (tx == (j >> 2)) {
+// acc[q][s] = sum_{k < K} A[(w + 16q) DP + k] * B(k, lane + 32s) for q < nq, s < ns, where
+// w is the warp, B(k, c) = B[c DP + k] (NT) or B[k DP + c] (NN).  Row reads are warp
+// broadcasts; column reads are lane-contiguous (NN) or lane-strided by the odd pitch (NT).
+template <bool NT>
+__device__ __forceinline__ void smem_mm(const float* A, const float* B, int nq, int ns, int K,
+                                        float (&acc)[6][3]) {
+  const int w = threadIdx.x >> 5, lane = threadIdx.x & 31;
 #pragma unroll
-      for (int i = 0; i < 4; ++i)
+  for (int q = 0; q < 6; ++q)
 #pragma unroll
-        for (int t = 0; t < 4; ++t)
-          if (t == (j & 3)) col[4 * ty + i] = v[i][t];
+    for (int s = 0; s < 3; ++s) acc[q][s] = 0.f;
+#pragma unroll 4
+  for (int k = 0; k < K; ++k) {
+    float b[3];
+#pragma unroll
+    for (int s = 0; s < 3; ++s) {
+      const int c = lane + 32 * s;
+      b[s] = (s < ns) ? (NT ? B[c * DP + k] : B[k * DP + c]) : 0.f;
     }
-    __syncthreads();
-    float djj = col[j];
-    if (j < kb && (!(djj > 0.f) || !isfinite(djj))) {
-      if (threadIdx.x == 0) *bad = 1;
+#pragma unroll
+    for (int q = 0; q < 6; ++q) {
+      if (q < nq) {
+        const float av = A[(w + 16 * q) * DP + k];
+#pragma unroll
+        for (int s = 0; s < 3; ++s) acc[q][s] = fmaf(av, b[s], acc[q][s]);
+      }
+    }
+  }
+}
+
+// Warp-level Cholesky + inverse of the 32 x 32 sub-block at S[c0][c0]: L goes
+// back to S, L^-1 to X.  rdiag: 32 floats of scratch.  Returns true (uniform)
+// if a pivot was not > 0 or not finite; that pivot is replaced by 1.
+__device__ bool sub_factor(float* S, float* X, float* rdiag, int c0) {
+  const unsigned FULL = 0xffffffffu;
+  const int lane = threadIdx.x & 31;
+  float r[SUB];
+#pragma unroll
+  for (int k = 0; k < SUB; ++k) r[k] = S[(c0 + lane) * DP + c0 + k];
+  bool bad = false;
+  float my_rinv = 1.f;
+#pragma unroll
+  for (int j = 0; j < SUB; ++j) {
+    float djj = __shfl_sync(FULL, r[j], j);
+    if (!(djj > 0.f) || !isfinite(djj)) {
+      bad = true;
       djj = 1.f;
     }
-    if (j >= kb) djj = 1.f;
-    const float ljj = sqrtf(djj);
-    const float rinv = 1.f / djj;
-    if (4 * ty + 3 > j && 4 * tx + 3 > j && 4 * tx <= 4 * ty + 3) {
-      // trailing update s[r][c] -= s[r][j] s[c][j] / s[j][j] for j < c <= r
+    // rsqrtf (2 ulp) keeps the serial pivot chain short; the factor's own
+    // float32 rounding error is orders of magnitude larger
+    const float rl = rsqrtf(djj);
+    const float ljj = djj * rl;
+    if (lane == j) my_rinv = rl;
+    const float lij = (lane < j) ? 0.f : ((lane == j) ? ljj : r[j] * rl);
+    r[j] = lij;
 #pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        const int r = 4 * ty + i;
-        const float srj = col[r] * rinv;
-#pragma unroll
-        for (int t = 0; t < 4; ++t) {
-          const int c = 4 * tx + t;
-          if (c > j && c <= r) v[i][t] = fmaf(-srj, col[c], v[i][t]);
-        }
-      }
-    }
-    if (tx == (j >> 2)) {
-#pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        const int r = 4 * ty + i;
-        const float lv = (r == j) ? ljj : col[r] / ljj;
-#pragma unroll
-        for (int t = 0; t < 4; ++t)
-          if (t == (j & 3) && r >= j) v[i][t] = lv;
-      }
-    }
+    for (int k = j + 1; k < SUB; ++k) r[k] = fmaf(-lij, __shfl_sync(FULL, lij, k), r[k]);
   }
+#pragma unroll
+  for (int k = 0; k < SUB; ++k) S[(c0 + lane) * DP + c0 + k] = r[k];
+  rdiag[lane] = my_rinv;
+  __syncwarp();
+  // column `lane` of L^-1 by forward substitution (L rows read as broadcasts)
+  float x[SUB];
+#pragma unroll
+  for (int i = 0; i < SUB; ++i) {
+    float s = (i == lane) ? 1.f : 0.f;
+#pragma unroll
+    for (int k = 0; k < i; ++k) s = fmaf(-S[(c0 + i) * DP + c0 + k], x[k], s);
+    x[i] = s * rdiag[i];
+  }
+#pragma unroll
+  for (int i = 0; i < SUB; ++i) X[(c0 + i) * DP + c0 + lane] = x[i];
+  return bad;
 }
 
-// x = L^-1 for the lower L in v (right-looking substitution on x = I): step k
-// scales row k by 1 / L[k][k] and removes it from the rows below.
-__device__ void trinv_regs(const float (&v)[4][4], float (&x)[4][4], float (*colbuf)[NB],
-                           float (*rowbuf)[NB]) {
-  const int tx = threadIdx.x & 31, ty = threadIdx.x >> 5;
-#pragma unroll
-  for (int i = 0; i < 4; ++i)
-#pragma unroll
-    for (int t = 0; t < 4; ++t) x[i][t] = (4 * ty + i == 4 * tx + t) ? 1.f : 0.f;
-  for (int k = 0; k < NB; ++k) {
-    float* col = colbuf[k & 1];
-    float* row = rowbuf[k & 1];
-    if (tx == (k >> 2)) {
-#pragma unroll
-      for (int i = 0; i < 4; ++i)
-#pragma unroll
-        for (int t = 0; t < 4; ++t)
-          if (t == (k & 3)) col[4 * ty + i] = v[i][t];
-    }
-    if (ty == (k >> 2)) {
-#pragma unroll
-      for (int i = 0; i < 4; ++i)
-#pragma unroll
-        for (int t = 0; t < 4; ++t)
-          if (i == (k & 3)) row[4 * tx + t] = x[i][t];
+// Cholesky of the kb x kb lower block at a (ld lda); a receives L^-1 (strict
+// upper part zeroed).  Rows/columns beyond kb are treated as identity.
+__global__ void __launch_bounds__(DIAG_THREADS)
+potrf_diag_kernel(float* __restrict__ a, int64_t lda, int kb, int* __restrict__ status) {
+  extern __shared__ float smem[];
+  float* S = smem;               // NB x DP: the block, becoming L
+  float* X = S + NB * DP;        // NB x DP: L^-1
+  float* W = X + NB * DP;        // SUB x DP: block-row products of the inverse
+  float* rdiag = W + SUB * DP;   // SUB
+  __shared__ int bad;
+  const int w = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (threadIdx.x == 0) bad = 0;
+  for (int e = threadIdx.x; e < NB * NB; e += DIAG_THREADS) {
+    const int r = e / NB, c = e % NB;
+    S[r * DP + c] = (r < kb && c < kb) ? ((c <= r) ? a[r * lda + c] : 0.f) : ((r == c) ? 1.f : 0.f);
+    X[r * DP + c] = 0.f;
+  }
+  __syncthreads();
+  float acc[6][3];
+  for (int c0 = 0; c0 < NB; c0 += SUB) {
+    if (w == 0) {
+      if (sub_factor(S, X, rdiag, c0) && lane == 0) bad = 1;
     }
     __syncthreads();
-    const float rk = 1.f / col[k];
-    if (4 * ty + 3 > k && 4 * tx <= k) {
+    const int m = NB - c0 - SUB;
+    if (m == 0) break;
+    float* panel = S + (c0 + SUB) * DP + c0;
+    // L21 = A21 X11^T
+    smem_mm<true>(panel, X + c0 * DP + c0, m / 16, 1, SUB, acc);
+    __syncthreads();
 #pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        const int r = 4 * ty + i;
-        const float lrk = col[r];
+    for (int q = 0; q < 6; ++q)
+      if (q < m / 16) panel[(w + 16 * q) * DP + lane] = acc[q][0];
+    __syncthreads();
+    // A22 -= L21 L21^T (lower part)
+    smem_mm<true>(panel, panel, m / 16, m / 32, SUB, acc);
+    float* a22 = panel + SUB;
 #pragma unroll
-        for (int t = 0; t < 4; ++t) {
-          const int c = 4 * tx + t;
-          if (r > k && c <= k) x[i][t] = fmaf(-lrk, row[c] * rk, x[i][t]);
-        }
+    for (int q = 0; q < 6; ++q)
+#pragma unroll
+      for (int s = 0; s < 3; ++s) {
+        const int r = w + 16 * q, c = lane + 32 * s;
+        if (q < m / 16 && s < m / 32 && c <= r) a22[r * DP + c] -= acc[q][s];
       }
-    }
-    if (ty == (k >> 2)) {
-#pragma unroll
-      for (int i = 0; i < 4; ++i)
-#pragma unroll
-        for (int t = 0; t < 4; ++t)
-          if (i == (k & 3)) x[i][t] *= rk;
-    }
+    __syncthreads();
   }
-}
-
-// Cholesky of the kb x kb lower block at a (ld lda) in place (strict upper
-// part zeroed) and its inverse into inv (NB x NB, ld NB, zero padded).
-__global__ void __launch_bounds__(DIAG_THREADS)
-potrf_diag_kernel(float* __restrict__ a, int64_t lda, int kb, float* __restrict__ inv,
-                  int* __restrict__ status) {
-  __shared__ float colbuf[2][NB];
-  __shared__ float rowbuf[2][NB];
-  __shared__ int bad;
-  const int tx = threadIdx.x & 31, ty = threadIdx.x >> 5;
-  if (threadIdx.x == 0) bad = 0;
-  float v[4][4];
+  // off-diagonal blocks of L^-1, block row by block row
+  for (int i = 1; i < NB / SUB; ++i) {
+    smem_mm<false>(S + SUB * i * DP, X, 2, i, SUB * i, acc);  // W = L[i, :i] X[:i, :i]
 #pragma unroll
-  for (int i = 0; i < 4; ++i)
+    for (int q = 0; q < 2; ++q)
 #pragma unroll
-    for (int t = 0; t < 4; ++t) {
-      const int r = 4 * ty + i, c = 4 * tx + t;
-      v[i][t] = (r < kb && c < kb) ? ((c <= r) ? a[r * lda + c] : 0.f) : ((r == c) ? 1.f : 0.f);
-    }
-  __syncthreads();
-  chol_regs(v, kb, &bad, colbuf);
+      for (int s = 0; s < 3; ++s)
+        if (s < i) W[(w + 16 * q) * DP + lane + 32 * s] = acc[q][s];
+    __syncthreads();
+    smem_mm<false>(X + SUB * i * DP + SUB * i, W, 2, i, SUB, acc);  // X[i, :i] = -X_ii W
 #pragma unroll
-  for (int i = 0; i < 4; ++i)
+    for (int q = 0; q < 2; ++q)
 #pragma unroll
-    for (int t = 0; t < 4; ++t) {
-      const int r = 4 * ty + i, c = 4 * tx + t;
-      if (r < kb && c < kb) a[r * lda + c] = (c <= r) ? v[i][t] : 0.f;
-    }
-  float x[4][4];
-  __syncthreads();
-  trinv_regs(v, x, colbuf, rowbuf);
-#pragma unroll
-  for (int i = 0; i < 4; ++i)
-#pragma unroll
-    for (int t = 0; t < 4; ++t) {
-      const int r = 4 * ty + i, c = 4 * tx + t;
-      inv[r * NB + c] = (r < kb && c < kb && c <= r) ? x[i][t] : 0.f;
-    }
-  __syncthreads();
+      for (int s = 0; s < 3; ++s)
+        if (s < i) X[(SUB * i + w + 16 * q) * DP + lane + 32 * s] = -acc[q][s];
+    __syncthreads();
+  }
+  for (int e = threadIdx.x; e < NB * NB; e += DIAG_THREADS) {
+    const int r = e / NB, c = e % NB;
+    if (r < kb && c < kb) a[r * lda + c] = (c <= r) ? X[r * DP + c] : 0.f;
+  }
   if (threadIdx.x == 0 && bad) atomicExch(status, GQ_DEVERR_NOTPD);
-}
-
-// Batched in-place inverse of the NB x NB lower-triangular diagonal blocks of a.
-__global__ void __launch_bounds__(DIAG_THREADS)
-trinv_diag_blocks_kernel(float* __restrict__ a, int64_t n, int64_t lda) {
-  __shared__ float colbuf[2][NB];
-  __shared__ float rowbuf[2][NB];
-  const int tx = threadIdx.x & 31, ty = threadIdx.x >> 5;
-  const int64_t b0 = (int64_t)blockIdx.x * NB;
-  const int kb = (int)min((int64_t)NB, n - b0);
-  float v[4][4], x[4][4];
-#pragma unroll
-  for (int i = 0; i < 4; ++i)
-#pragma unroll
-    for (int t = 0; t < 4; ++t) {
-      const int r = 4 * ty + i, c = 4 * tx + t;
-      v[i][t] = (r < kb && c < kb) ? ((c <= r) ? a[(b0 + r) * lda + b0 + c] : 0.f)
-                                   : ((r == c) ? 1.f : 0.f);
-    }
-  trinv_regs(v, x, colbuf, rowbuf);
-#pragma unroll
-  for (int i = 0; i < 4; ++i)
-#pragma unroll
-    for (int t = 0; t < 4; ++t) {
-      const int r = 4 * ty + i, c = 4 * tx + t;
-      if (r < kb && c < kb) a[(b0 + r) * lda + b0 + c] = (c <= r) ? x[i][t] : 0.f;
-    }
 }
 
 // Zero the strict upper triangle of an n x n matrix (ld).
@@ -313,66 +302,61 @@ __global__ void reverse_copy_kernel(const float* __restrict__ linv, int64_t n, i
     u[i * ldu + j] = linv[(n - 1 - i) * ldl + (n - 1 - j)];
 }
 
-// Blocked lower Cholesky of a (n x n, ld n) in place; panel scratch p (n x NB),
-// diagonal-inverse scratch dinv (NB x NB).
-int cholesky_lower(float* a, int64_t n, float* p, float* dinv, int* status, cudaStream_t st) {
-  static bool attr = false;
-  if (!attr) {
+int transpose2d(const float* src, int64_t rows, int64_t cols, int64_t lds, float* dst, int64_t ldd,
+                cudaStream_t st);
+
+// In-place inverse Cholesky of the n x n lower triangle of a (ld lda): on
+// return the lower triangle holds X = L^-1, where A = L L^T.  The strict upper
+// triangle must be zero on entry (the leaves keep their own diagonal blocks'
+// upper parts zero).  Recursive on a split n = n1 + n2 (n1 a multiple of NB):
+//   X11 = rec(A11);  L21 = A21 X11^T;  A22 -= L21 L21^T;  X22 = rec(A22);
+//   X21 = -X22 L21 X11,
+// i.e. Cholesky (n^3/3) and triangular inverse (n^3/3) interleaved, with the
+// product operands' zero triangles skipped tile by tile.  Every GEMM has both
+// operands K-major (tensor-core path): X11^T is formed by a transpose and the
+// last product is taken as X21 = -X22 Tt^T with Tt = X11^T L21^T.
+// scratch: n1 * n floats suffice (n1 <= n / 2 + NB).
+int diag_kernel_setup() {
+  static int attr_device = -1;
+  int dev = 0;
+  GQ_CHECK_CUDA(cudaGetDevice(&dev));
+  if (attr_device != dev) {
     GQ_CHECK_CUDA(cudaFuncSetAttribute(potrf_diag_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                        (int)DIAG_SMEM));
-    GQ_CHECK_CUDA(cudaFuncSetAttribute(trinv_diag_blocks_kernel,
-                                       cudaFuncAttributeMaxDynamicSharedMemorySize, (int)DIAG_SMEM));
-    attr = true;
-  }
-  for (int64_t k0 = 0; k0 < n; k0 += NB) {
-    int kb = (int)std::min<int64_t>(NB, n - k0);
-    float* akk = a + k0 * n + k0;
-    potrf_diag_kernel<<<1, DIAG_THREADS, DIAG_SMEM, st>>>(akk, n, kb, dinv, status);
-    GQ_TRY(check_launch("potrf_diag"));
-    int64_t rem = n - k0 - kb;
-    if (rem <= 0) break;
-    float* a21 = a + (k0 + kb) * n + k0;
-    // P = A21 * L11^-T   (rem x kb)
-    GQ_TRY(sgemm(0, 1, rem, kb, kb, 1.f, a21, n, dinv, NB, 0.f, p, NB, 0, st));
-    // A22 -= P P^T (lower tiles)
-    float* a22 = a + (k0 + kb) * n + (k0 + kb);
-    GQ_TRY(sgemm(0, 1, rem, rem, kb, -1.f, p, NB, p, NB, 1.f, a22, n, 1, st));
-    GQ_CHECK_CUDA(cudaMemcpy2DAsync(a21, n * sizeof(float), p, NB * sizeof(float),
-                                    kb * sizeof(float), rem, cudaMemcpyDeviceToDevice, st));
+    attr_device = dev;
   }
   return GQ_OK;
 }
 
-int transpose2d(const float* src, int64_t rows, int64_t cols, int64_t lds, float* dst, int64_t ldd,
-                cudaStream_t st);
-
-// Recursive lower-triangular inverse of a[0:n, 0:n] (ld lda) in place.  The
-// NB x NB diagonal blocks must already be inverted; the strict upper triangle
-// must be zero.  With [[L11, 0], [L21, L22]]^-1 = [[X11, 0], [X21, X22]],
-// X21 = -X22 L21 X11, evaluated as two products whose operands are both
-// K-major (tensor-core GEMM path):  Tt = X11^T L21^T,  X21 = -X22 Tt^T.
-// scratch: at least (n/2 + 64) * (n + 64) floats.
-int trinv_rec(float* a, int64_t n, int64_t lda, float* scratch, cudaStream_t st) {
-  if (n <= NB) return GQ_OK;
+int inv_chol_rec(float* a, int64_t n, int64_t lda, float* scratch, int* status, cudaStream_t st) {
+  if (n <= NB) {
+    potrf_diag_kernel<<<1, DIAG_THREADS, DIAG_SMEM, st>>>(a, lda, (int)n, status);
+    return check_launch("potrf_diag");
+  }
   int64_t n1 = ((n / 2 + NB - 1) / NB) * NB;
   if (n1 >= n) n1 = n - NB;
-  int64_t n2 = n - n1;
+  const int64_t n2 = n - n1;
   float* a11 = a;
   float* a21 = a + n1 * lda;
-  float* a22 = a + n1 * lda + n1;
-  GQ_TRY(trinv_rec(a11, n1, lda, scratch, st));
-  GQ_TRY(trinv_rec(a22, n2, lda, scratch, st));
-  float* s1 = scratch;            // X11^T, n1 x n1
-  float* tt = scratch + n1 * n1;  // Tt = (L21 X11)^T, n1 x n2
-  GQ_TRY(transpose2d(a11, n1, n1, lda, s1, n1, st));
-  GQ_TRY(sgemm(0, 1, n1, n2, n1, 1.f, s1, n1, a21, lda, 0.f, tt, n2, 0, st));
-  GQ_TRY(sgemm(0, 1, n2, n1, n2, -1.f, a22, lda, tt, n2, 0.f, a21, lda, 0, st));
+  float* a22 = a21 + n1;
+  GQ_TRY(inv_chol_rec(a11, n1, lda, scratch, status, st));
+  float* l21 = scratch;  // n2 x n1
+  GQ_TRY(sgemm_tri(0, 1, n2, n1, n1, 1.f, a21, lda, a11, lda, 0.f, l21, n1, 3, st));
+  GQ_TRY(sgemm(0, 1, n2, n2, n1, -1.f, l21, n1, l21, n1, 1.f, a22, lda, 1, st));
+  GQ_CHECK_CUDA(cudaMemcpy2DAsync(a21, lda * sizeof(float), l21, n1 * sizeof(float),
+                                  n1 * sizeof(float), n2, cudaMemcpyDeviceToDevice, st));
+  float* tt = scratch;            // n1 x n2: Tt = X11^T L21^T
+  float* xt = scratch + n1 * n2;  // n1 x n1: X11^T
+  GQ_TRY(transpose2d(a11, n1, n1, lda, xt, n1, st));
+  GQ_TRY(sgemm_tri(0, 1, n1, n2, n1, 1.f, xt, n1, a21, lda, 0.f, tt, n2, 1, st));
+  GQ_TRY(inv_chol_rec(a22, n2, lda, scratch + n1 * n2, status, st));
+  GQ_TRY(sgemm_tri(0, 1, n2, n1, n2, -1.f, a22, lda, tt, n2, 0.f, a21, lda, 2, st));
   return GQ_OK;
 }
 
 int64_t hessian_ws_floats(int64_t d) {
   int64_t half = d / 2 + NB;
-  return d * d + d * NB + NB * NB + half * (d + NB) + 64;
+  return d * d + half * (d + NB) + 64;
 }
 
 }  // namespace gq
@@ -403,13 +387,12 @@ int gq_hessian_factor(const float* h, int64_t d, int64_t ldh, const int32_t* per
   cudaStream_t st = gq::as_stream(stream);
   float* ws = reinterpret_cast<float*>(workspace);
   float* ht = ws;                                  // d*d
-  float* p = ht + d * d;                           // d*64
-  float* dinv = p + d * gq::NB;                    // 64*64
-  float* scratch = dinv + gq::NB * gq::NB;         // (d/2+64) x (d+64)
+  float* scratch = ht + d * d;                     // (d/2+NB) x (d+NB)
   int64_t half = d / 2 + gq::NB;
   float* mean = scratch + half * (d + gq::NB);     // 1 float
   int* status = reinterpret_cast<int*>(mean + 16);  // 1 int
 
+  GQ_TRY(gq::diag_kernel_setup());
   gq::diag_mean_kernel<<<1, 1024, 0, st>>>(h, d, ldh, mean);
   GQ_TRY(gq::check_launch("diag_mean"));
   for (int attempt = 0; attempt < 5; ++attempt) {
@@ -418,19 +401,15 @@ int gq_hessian_factor(const float* h, int64_t d, int64_t ldh, const int32_t* per
     dim3 grid((unsigned)std::min<int64_t>(gq::ceil_div(d, 256), 64), (unsigned)d);
     gq::damp_permute_kernel<<<grid, 256, 0, st>>>(h, d, ldh, perm, mean, (float)damp, ht, hd_out);
     GQ_TRY(gq::check_launch("damp_permute"));
-    GQ_TRY(gq::cholesky_lower(ht, d, p, dinv, status, st));
+    dim3 gz((unsigned)std::min<int64_t>(gq::ceil_div(d, 256), 64), (unsigned)d);
+    gq::zero_upper_kernel<<<gz, 256, 0, st>>>(ht, d, d);
+    GQ_TRY(gq::check_launch("zero_upper"));
+    // L^-1 in place, then U = J L^-1 J
+    GQ_TRY(gq::inv_chol_rec(ht, d, d, scratch, status, st));
     int host_status = 0;
     GQ_CHECK_CUDA(cudaMemcpyAsync(&host_status, status, sizeof(int), cudaMemcpyDeviceToHost, st));
     GQ_CHECK_CUDA(cudaStreamSynchronize(st));
     if (host_status != gq::GQ_DEVERR_NONE) continue;
-    // L^-1 in place, then U = J L^-1 J
-    dim3 gz((unsigned)std::min<int64_t>(gq::ceil_div(d, 256), 64), (unsigned)d);
-    gq::zero_upper_kernel<<<gz, 256, 0, st>>>(ht, d, d);
-    GQ_TRY(gq::check_launch("zero_upper"));
-    gq::trinv_diag_blocks_kernel<<<(unsigned)gq::ceil_div(d, gq::NB), gq::DIAG_THREADS,
-                                   gq::DIAG_SMEM, st>>>(ht, d, d);
-    GQ_TRY(gq::check_launch("trinv_diag_blocks"));
-    GQ_TRY(gq::trinv_rec(ht, d, d, scratch, st));
     dim3 g2((unsigned)std::min<int64_t>(gq::ceil_div(d, 256), 64), (unsigned)d);
     gq::reverse_copy_kernel<<<g2, 256, 0, st>>>(ht, d, d, u, ldu);
     GQ_TRY(gq::check_launch("reverse_copy"));

@@ -132,7 +132,7 @@ namespace tc32 {
 bool eligible(int ta, int tb, int64_t M, int64_t N, int64_t K, const float* A, int64_t lda,
               const float* B, int64_t ldb, const float* C, int64_t ldc);
 int launch(int tb, int64_t M, int64_t N, int64_t K, float alpha, const float* A, int64_t lda,
-           const float* B, int64_t ldb, float beta, float* C, int64_t ldc, int uplo,
+           const float* B, int64_t ldb, float beta, float* C, int64_t ldc, int uplo, int tri,
            cudaStream_t st);
 }  // namespace tc32
 
@@ -146,8 +146,21 @@ int sgemm(int ta, int tb, int64_t M, int64_t N, int64_t K, float alpha, const fl
           const float* B, int64_t ldb, float beta, float* C, int64_t ldc, int uplo, cudaStream_t st) {
   if (M == 0 || N == 0) return GQ_OK;
   if (tc32::eligible(ta, tb, M, N, K, A, lda, B, ldb, C, ldc))
-    return tc32::launch(tb, M, N, K, alpha, A, lda, B, ldb, beta, C, ldc, uplo, st);
+    return tc32::launch(tb, M, N, K, alpha, A, lda, B, ldb, beta, C, ldc, uplo, 0, st);
   return sgemm_simt(ta, tb, M, N, K, alpha, A, lda, B, ldb, beta, C, ldc, uplo, st);
+}
+
+// sgemm with a triangular operand whose zero triangle is stored as zeros and
+// starts on 128 boundaries (tri: 1 A upper, 2 A lower, 3 B lower): the
+// tensor-core path skips the all-zero k-slices of each tile; the result is the
+// same as the full product.
+int sgemm_tri(int ta, int tb, int64_t M, int64_t N, int64_t K, float alpha, const float* A,
+              int64_t lda, const float* B, int64_t ldb, float beta, float* C, int64_t ldc, int tri,
+              cudaStream_t st) {
+  if (M == 0 || N == 0) return GQ_OK;
+  if (tc32::eligible(ta, tb, M, N, K, A, lda, B, ldb, C, ldc))
+    return tc32::launch(tb, M, N, K, alpha, A, lda, B, ldb, beta, C, ldc, 0, tri, st);
+  return sgemm_simt(ta, tb, M, N, K, alpha, A, lda, B, ldb, beta, C, ldc, 0, st);
 }
 
 int sgemm_simt(int ta, int tb, int64_t M, int64_t N, int64_t K, float alpha, const float* A,

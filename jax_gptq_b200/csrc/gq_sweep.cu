@@ -7,13 +7,14 @@
 // with the dequantized values; cp [m, ldp] uint8 -- codes in permuted order;
 // err [m, 128] float32 -- the scaled errors of the current block.
 //
-// Per 128-column block:
-//   1. sweep_block_kernel: a warp owns 4 rows; lane l holds columns 4l..4l+3
-//      of each in registers; the block of U lives in shared memory.  For each
-//      column i, lane r < 4 gathers row r's current value, quantizes it once,
-//      writes the code / dequantized value / error and broadcasts the error
-//      (w - dq) / U_ii, which every lane applies to its columns > i.
-//   2. wp[:, b1:] -= err @ U[b0:b1, b1:]  (fp32 GEMM).
+// Per 128-column block [b0, b1):
+//   1. the band U[b0:b1, b0:] is transposed into ubt (column j of the band is
+//      a contiguous 128-float row);
+//   2. sweep_rows_kernel: one lane per weight row, one warp per CTA; the
+//      lane quantizes its row's columns one by one (32-column sub-blocks in
+//      registers, the rest of the block in a shared-memory row buffer) and
+//      writes codes, dequantized values and scaled errors (w - dq) / U_ii;
+//   3. wp[:, b1:] -= err @ U[b0:b1, b1:]  (fp32 GEMM).
 // Finally codes/dequant are scattered back to original column order.
 #include "gq_common.cuh"
 #include "gq_quant.cuh"
@@ -25,9 +26,9 @@ int sgemm(int ta, int tb, int64_t M, int64_t N, int64_t K, float alpha, const fl
 int check_quant_args(const char* who, int64_t m, int64_t n, int w_bits, int group_size, int sym);
 
 constexpr int SW_BLOCK = 128;
-constexpr int SW_ROWS = 4;        // rows per warp (lane r < 4 quantizes row r)
-constexpr int SW_WARPS = 4;       // warps per CTA
-constexpr int SW_ROWS_CTA = SW_ROWS * SW_WARPS;
+constexpr int SW_SUB = 32;   // columns of a register-resident sub-block
+constexpr int SW_WP = 33;    // pitch of the row buffer (lane-private columns, conflict-free)
+constexpr int SW_TP = 36;    // pitch of the sub-block U tile (16-byte rows for broadcast reads)
 
 inline int64_t round4(int64_t n) { return (n + 3) & ~int64_t(3); }
 
@@ -77,11 +78,10 @@ struct SweepArgs {
   float* wp;            // [m, ldp]
   uint8_t* cp;          // [m, ldp]
   float* err;           // [m, 128]
-  const float* u;       // [n, ldu]
-  int64_t m, n, ldp, ldu;
+  const float* ubt;     // [n - b0, 128]: ubt[j][i] = U[b0 + i][b0 + j]
+  int64_t m, n, ldp;
   int64_t b0;           // first column of this block
   int bw;               // block width (<= 128)
-  int g;                // group size
   int n_groups;
   QParams qp;
   int sym;
@@ -94,124 +94,188 @@ struct SweepArgs {
   float* zeros;
 };
 
-__global__ void __launch_bounds__(SW_WARPS * 32)
-sweep_block_kernel(SweepArgs a) {
-  extern __shared__ __align__(16) float sweep_smem[];
-  float (*us)[SW_BLOCK] = reinterpret_cast<float (*)[SW_BLOCK]>(sweep_smem);
-  float* udinv = sweep_smem + SW_BLOCK * SW_BLOCK;
-  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+// Scale / zero of lane's row from its running min, max and max |w|; group 0
+// may take caller-supplied parameters.
+__device__ __forceinline__ void sweep_group_params(const SweepArgs& a, int64_t row, bool valid,
+                                                   int64_t gi, float mn, float mx, float ma,
+                                                   float& scale, float& zero) {
+  if (gi == 0 && a.group0_scale != nullptr) {
+    scale = valid ? a.group0_scale[row] : 1.f;
+    zero = valid ? a.group0_zero[row] : 0.f;
+  } else if (a.sym) {
+    group_scale_zero(-ma, ma, a.qp, a.sym, scale, zero);
+  } else {
+    group_scale_zero(mn, mx, a.qp, a.sym, scale, zero);
+  }
+  if (valid && a.scales) {
+    a.scales[row * a.n_groups + gi] = scale;
+    a.zeros[row * a.n_groups + gi] = zero;
+  }
+}
+
+// One 128-column block of the sweep for 32 rows: lane l owns row 32 * blockIdx.x + l.
+// Columns are taken in sub-blocks of 32 held in registers; inside a sub-block
+// each column's scaled error is applied at once to the later columns
+// (right-looking, U tile broadcast from shared memory), and after the
+// sub-block its 32 errors are applied to the block's remaining columns, which
+// live in a lane-private shared-memory row buffer.  Every column therefore
+// receives the updates of all earlier columns in increasing order, one fmaf
+// each.  G: group size when it divides 128 (4..128), 0 when groups span blocks.
+template <int G>
+__global__ void __launch_bounds__(32) sweep_rows_kernel(SweepArgs a) {
+  constexpr int GD = (G > 0) ? G : 1;  // divisor-safe group size for the G = 0 instance
+  __shared__ float ws[SW_BLOCK * SW_WP];
+  __shared__ __align__(16) float tile[SW_SUB * SW_TP];
+  __shared__ float rinv[SW_BLOCK];
+  const int lane = threadIdx.x;
   const int bw = a.bw;
-  // U block into shared memory (zero beyond the block width)
-  for (int e = threadIdx.x; e < SW_BLOCK * SW_BLOCK; e += blockDim.x) {
-    int r = e >> 7, c = e & 127;
-    us[r][c] = (r < bw && c < bw) ? a.u[(a.b0 + r) * a.ldu + a.b0 + c] : 0.f;
+  const float* __restrict__ ubt = a.ubt;
+  for (int i = lane; i < SW_BLOCK; i += 32)
+    rinv[i] = (i < bw) ? 1.f / ubt[(int64_t)i * SW_BLOCK + i] : 0.f;
+  const int64_t row = (int64_t)blockIdx.x * 32 + lane;
+  const bool valid = row < a.m;
+  float* wrow = valid ? a.wp + row * a.ldp + a.b0 : nullptr;
+  if (valid) {
+    for (int j = 0; j < bw; j += 4) {
+      const float4 v = *reinterpret_cast<const float4*>(wrow + j);
+      ws[(j + 0) * SW_WP + lane] = v.x;
+      ws[(j + 1) * SW_WP + lane] = v.y;
+      ws[(j + 2) * SW_WP + lane] = v.z;
+      ws[(j + 3) * SW_WP + lane] = v.w;
+    }
   }
-  __syncthreads();
-  for (int i = threadIdx.x; i < SW_BLOCK; i += blockDim.x) udinv[i] = (i < bw) ? 1.f / us[i][i] : 0.f;
-  __syncthreads();
+  float scale = 1.f, zero = 0.f;
+  if (G == 0 && valid) {
+    scale = a.big_scale[row];
+    zero = a.big_zero[row];
+  }
+  __syncwarp();
 
-  // Lane l holds columns 4l..4l+3 of the warp's SW_ROWS rows; lane r < SW_ROWS
-  // additionally "owns" row r: it quantizes that row's current column and
-  // writes its outputs, so every quantization is computed exactly once.
-  const int64_t row_base = (int64_t)blockIdx.x * SW_ROWS_CTA + warp * SW_ROWS;
-  const bool row_lane = lane < SW_ROWS;
-  const int64_t my_row = row_base + lane;
-  const bool my_valid = row_lane && my_row < a.m;
-  float w[SW_ROWS][4];
+  for (int c0 = 0; c0 < bw; c0 += SW_SUB) {
+    // tile[k][t] = U[b0 + c0 + k][b0 + c0 + t]  (lane t copies its row of the band)
+    if (c0 + lane < bw) {
+      const float4* src = reinterpret_cast<const float4*>(ubt + (int64_t)(c0 + lane) * SW_BLOCK + c0);
 #pragma unroll
-  for (int r = 0; r < SW_ROWS; ++r) {
-    const int64_t row = row_base + r;
-    float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
-    if (row < a.m && 4 * lane < bw)
-      v = *reinterpret_cast<const float4*>(a.wp + row * a.ldp + a.b0 + 4 * lane);
-    w[r][0] = v.x; w[r][1] = v.y; w[r][2] = v.z; w[r][3] = v.w;
-  }
-  float my_scale = 1.f, my_zero = 0.f;
-  if (a.g > SW_BLOCK && my_valid) {
-    my_scale = a.big_scale[my_row];
-    my_zero = a.big_zero[my_row];
-  }
-  float* wrow = my_valid ? a.wp + my_row * a.ldp + a.b0 : nullptr;
-  uint8_t* crow = my_valid ? a.cp + my_row * a.ldp + a.b0 : nullptr;
-  float* erow = my_valid ? a.err + my_row * SW_BLOCK : nullptr;
-  const int seg = (a.g <= SW_BLOCK) ? (a.g >> 2) : 32;  // lanes per group inside a block
+      for (int q = 0; q < SW_SUB / 4; ++q) {
+        const float4 v = __ldg(src + q);
+        tile[(4 * q + 0) * SW_TP + lane] = v.x;
+        tile[(4 * q + 1) * SW_TP + lane] = v.y;
+        tile[(4 * q + 2) * SW_TP + lane] = v.z;
+        tile[(4 * q + 3) * SW_TP + lane] = v.w;
+      }
+    } else {
+#pragma unroll
+      for (int k = 0; k < SW_SUB; ++k) tile[k * SW_TP + lane] = 0.f;
+    }
+    __syncwarp();
+    float w[SW_SUB], e[SW_SUB];
+    uint32_t cw[SW_SUB / 4];
+#pragma unroll
+    for (int k = 0; k < SW_SUB; ++k) w[k] = (c0 + k < bw) ? ws[(c0 + k) * SW_WP + lane] : 0.f;
+#pragma unroll
+    for (int q = 0; q < SW_SUB / 4; ++q) cw[q] = 0u;
 
-  for (int i4 = 0; i4 < bw; i4 += 4) {
-    const int owner = i4 >> 2;
 #pragma unroll
-    for (int sub = 0; sub < 4; ++sub) {
-      const int i = i4 + sub;
-      if (i >= bw) break;
+    for (int k = 0; k < SW_SUB; ++k) {
+      const int i = c0 + k;
+      if (i >= bw) {
+        e[k] = 0.f;
+        continue;
+      }
       // group parameters at the group's first column, from the current values
-      // (g divides 128 here and blocks start on group boundaries, so the test
-      // on the block-local index is a mask)
-      if (a.g <= SW_BLOCK && (i & (a.g - 1)) == 0) {
-        const int64_t gi = (a.b0 + i) / a.g;
+      if (G > 0 && G <= SW_SUB && (k % GD) == 0) {
+        float mn = INFINITY, mx = -INFINITY, ma = 0.f;
 #pragma unroll
-        for (int r = 0; r < SW_ROWS; ++r) {
-          float mn = INFINITY, mx = -INFINITY, ma = 0.f;
-#pragma unroll
-          for (int t = 0; t < 4; ++t) {
-            if (4 * lane + t < bw) {
-              mn = fminf(mn, w[r][t]);
-              mx = fmaxf(mx, w[r][t]);
-              ma = fmaxf(ma, fabsf(w[r][t]));
-            }
-          }
-          for (int o = 1; o < seg; o <<= 1) {
-            mn = fminf(mn, __shfl_xor_sync(0xffffffffu, mn, o));
-            mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
-            ma = fmaxf(ma, __shfl_xor_sync(0xffffffffu, ma, o));
-          }
-          mn = __shfl_sync(0xffffffffu, mn, owner);
-          mx = __shfl_sync(0xffffffffu, mx, owner);
-          ma = __shfl_sync(0xffffffffu, ma, owner);
-          if (lane == r) {
-            float s, z;
-            if (gi == 0 && a.group0_scale != nullptr) {
-              s = my_valid ? a.group0_scale[my_row] : 1.f;
-              z = my_valid ? a.group0_zero[my_row] : 0.f;
-            } else if (a.sym) {
-              group_scale_zero(-ma, ma, a.qp, a.sym, s, z);
-            } else {
-              group_scale_zero(mn, mx, a.qp, a.sym, s, z);
-            }
-            my_scale = s;
-            my_zero = z;
-            if (my_valid && a.scales) {
-              a.scales[my_row * a.n_groups + gi] = s;
-              a.zeros[my_row * a.n_groups + gi] = z;
-            }
-          }
+        for (int t = k; t < k + GD && t < SW_SUB; ++t) {
+          mn = fminf(mn, w[t]);
+          mx = fmaxf(mx, w[t]);
+          ma = fmaxf(ma, fabsf(w[t]));
         }
+        sweep_group_params(a, row, valid, (a.b0 + i) / GD, mn, mx, ma, scale, zero);
       }
-      // gather column i of each row into its row lane
-      float mine = 0.f;
+      if (G > SW_SUB && k == 0 && (c0 % GD) == 0) {
+        float mn = INFINITY, mx = -INFINITY, ma = 0.f;
 #pragma unroll
-      for (int r = 0; r < SW_ROWS; ++r) {
-        const float v = __shfl_sync(0xffffffffu, w[r][sub], owner);
-        if (lane == r) mine = v;
+        for (int t = 0; t < SW_SUB; ++t) {
+          mn = fminf(mn, w[t]);
+          mx = fmaxf(mx, w[t]);
+          ma = fmaxf(ma, fabsf(w[t]));
+        }
+        for (int j = c0 + SW_SUB; j < c0 + G; ++j) {
+          const float v = ws[j * SW_WP + lane];
+          mn = fminf(mn, v);
+          mx = fmaxf(mx, v);
+          ma = fmaxf(ma, fabsf(v));
+        }
+        sweep_group_params(a, row, valid, (a.b0 + i) / GD, mn, mx, ma, scale, zero);
       }
-      const bool prop = a.b0 + i >= a.noprop_cols;
       float dq;
-      const float q = quantize_one(mine, my_scale, my_zero, a.qp, dq);
-      const float my_err = prop ? __fmul_rn(__fsub_rn(mine, dq), udinv[i]) : 0.f;
-      if (my_valid) {
-        wrow[i] = dq;
-        crow[i] = (uint8_t)(int)(q - a.qp.qmin);
-        erow[i] = my_err;
-      }
-      const float4 urow = *reinterpret_cast<const float4*>(&us[i][4 * lane]);
-      const float uv[4] = {urow.x, urow.y, urow.z, urow.w};
+      const float q = quantize_one(w[k], scale, zero, a.qp, dq);
+      const bool prop = a.b0 + i >= a.noprop_cols;
+      e[k] = prop ? __fmul_rn(__fsub_rn(w[k], dq), rinv[i]) : 0.f;
+      w[k] = dq;
+      cw[k >> 2] |= ((uint32_t)(int)(q - a.qp.qmin) & 0xffu) << (8 * (k & 3));
 #pragma unroll
-      for (int r = 0; r < SW_ROWS; ++r) {
-        const float err = __shfl_sync(0xffffffffu, my_err, r);
+      for (int q4 = 0; q4 < SW_SUB / 4; ++q4) {
+        if (4 * q4 + 3 > k) {
+          const float4 u4 = *reinterpret_cast<const float4*>(&tile[k * SW_TP + 4 * q4]);
+          const float uu[4] = {u4.x, u4.y, u4.z, u4.w};
 #pragma unroll
-        for (int t = 0; t < 4; ++t) {
-          if (4 * lane + t > i) w[r][t] = fmaf(-err, uv[t], w[r][t]);
+          for (int t = 0; t < 4; ++t)
+            if (4 * q4 + t > k) w[4 * q4 + t] = fmaf(-e[k], uu[t], w[4 * q4 + t]);
         }
       }
     }
+
+    if (valid) {
+      float* erow = a.err + row * SW_BLOCK + c0;
+      uint8_t* crow = a.cp + row * a.ldp + a.b0 + c0;
+      if (c0 + SW_SUB <= bw) {
+#pragma unroll
+        for (int q = 0; q < SW_SUB / 4; ++q) {
+          *reinterpret_cast<float4*>(wrow + c0 + 4 * q) =
+              make_float4(w[4 * q], w[4 * q + 1], w[4 * q + 2], w[4 * q + 3]);
+          *reinterpret_cast<float4*>(erow + 4 * q) =
+              make_float4(e[4 * q], e[4 * q + 1], e[4 * q + 2], e[4 * q + 3]);
+          *reinterpret_cast<uint32_t*>(crow + 4 * q) = cw[q];
+        }
+      } else {
+#pragma unroll
+        for (int k = 0; k < SW_SUB; ++k) {
+          if (c0 + k < bw) {
+            wrow[c0 + k] = w[k];
+            erow[k] = e[k];
+            crow[k] = (uint8_t)(cw[k >> 2] >> (8 * (k & 3)));
+          }
+        }
+      }
+    }
+
+    // the block's later columns: ws[j] -= sum_k e[k] U[c0 + k][j], k increasing
+    const float4* ub4 = reinterpret_cast<const float4*>(ubt);
+    for (int j0 = c0 + SW_SUB; j0 < bw; j0 += 4) {
+      float v[4];
+#pragma unroll
+      for (int jj = 0; jj < 4; ++jj) v[jj] = ws[(j0 + jj) * SW_WP + lane];
+#pragma unroll
+      for (int kc = 0; kc < SW_SUB / 4; ++kc) {
+        float4 u4[4];
+#pragma unroll
+        for (int jj = 0; jj < 4; ++jj)
+          u4[jj] = (j0 + jj < bw) ? __ldg(ub4 + (int64_t)(j0 + jj) * (SW_BLOCK / 4) + c0 / 4 + kc)
+                                  : make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+        for (int jj = 0; jj < 4; ++jj) {
+          v[jj] = fmaf(-e[4 * kc + 0], u4[jj].x, v[jj]);
+          v[jj] = fmaf(-e[4 * kc + 1], u4[jj].y, v[jj]);
+          v[jj] = fmaf(-e[4 * kc + 2], u4[jj].z, v[jj]);
+          v[jj] = fmaf(-e[4 * kc + 3], u4[jj].w, v[jj]);
+        }
+      }
+#pragma unroll
+      for (int jj = 0; jj < 4; ++jj) ws[(j0 + jj) * SW_WP + lane] = v[jj];
+    }
+    __syncwarp();
   }
 }
 
@@ -304,18 +368,15 @@ int gq_gptq_sweep(const float* w, int64_t m, int64_t n, int64_t ldw, const float
   }
 
   SweepArgs a;
-  a.wp = wp; a.cp = cp; a.err = err; a.u = u;
-  a.m = m; a.n = n; a.ldp = ldp; a.ldu = ldu;
-  a.g = group_size; a.n_groups = (int)(n / group_size);
+  a.wp = wp; a.cp = cp; a.err = err; a.ubt = ubt;
+  a.m = m; a.n = n; a.ldp = ldp;
+  a.n_groups = (int)(n / group_size);
   a.qp = make_qparams(w_bits, sym); a.sym = sym;
   a.noprop_cols = noprop_cols;
   a.group0_scale = group0_scale; a.group0_zero = group0_zero;
   a.big_scale = bscale; a.big_zero = bzero;
   a.scales = scales; a.zeros = zeros;
-  const unsigned grid = (unsigned)ceil_div(m, SW_ROWS_CTA);
-  const size_t sweep_smem_bytes = (SW_BLOCK * SW_BLOCK + SW_BLOCK) * sizeof(float);
-  GQ_CHECK_CUDA(cudaFuncSetAttribute(sweep_block_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                     (int)sweep_smem_bytes));
+  const unsigned grid = (unsigned)ceil_div(m, 32);
   for (int64_t b0 = 0; b0 < n; b0 += SW_BLOCK) {
     const int bw = (int)std::min<int64_t>(SW_BLOCK, n - b0);
     if (group_size > SW_BLOCK && b0 % group_size == 0) {
@@ -337,15 +398,25 @@ int gq_gptq_sweep(const float* w, int64_t m, int64_t n, int64_t ldw, const float
     }
     a.b0 = b0;
     a.bw = bw;
-    sweep_block_kernel<<<grid, SW_WARPS * 32, sweep_smem_bytes, st>>>(a);
-    GQ_TRY(check_launch("sweep_block"));
+    // U[b0:b1, b0:] transposed: the sweep reads the block's rows of U as
+    // contiguous runs, and the trailing GEMM gets both operands K-major
+    // (tensor-core path)
+    GQ_TRY(transpose2d(u + b0 * ldu + b0, bw, n - b0, ldu, ubt, SW_BLOCK, st));
+    switch (group_size) {
+      case 4: sweep_rows_kernel<4><<<grid, 32, 0, st>>>(a); break;
+      case 8: sweep_rows_kernel<8><<<grid, 32, 0, st>>>(a); break;
+      case 16: sweep_rows_kernel<16><<<grid, 32, 0, st>>>(a); break;
+      case 32: sweep_rows_kernel<32><<<grid, 32, 0, st>>>(a); break;
+      case 64: sweep_rows_kernel<64><<<grid, 32, 0, st>>>(a); break;
+      case 128: sweep_rows_kernel<128><<<grid, 32, 0, st>>>(a); break;
+      default: sweep_rows_kernel<0><<<grid, 32, 0, st>>>(a); break;
+    }
+    GQ_TRY(check_launch("sweep_rows"));
     const int64_t b1 = b0 + bw;
     if (b1 < n) {
-      // wp[:, b1:] -= err @ U[b0:b1, b1:], with the U band transposed so that
-      // both GEMM operands are K-major (tensor-core path)
-      GQ_TRY(transpose2d(u + b0 * ldu + b1, bw, n - b1, ldu, ubt, SW_BLOCK, st));
-      GQ_TRY(sgemm(0, 1, m, n - b1, bw, -1.f, err, SW_BLOCK, ubt, SW_BLOCK, 1.f, wp + b1, ldp, 0,
-                   st));
+      // wp[:, b1:] -= err @ U[b0:b1, b1:]
+      GQ_TRY(sgemm(0, 1, m, n - b1, bw, -1.f, err, SW_BLOCK, ubt + (int64_t)bw * SW_BLOCK,
+                   SW_BLOCK, 1.f, wp + b1, ldp, 0, st));
     }
   }
   if (dequant || codes) {

@@ -56,6 +56,7 @@ struct Params {
   int64_t M, N, K;
   float alpha, beta;
   int uplo;
+  int tri;  // 0 none, 1 A upper (k >= row0), 2 A lower (k < row0 + BM), 3 B lower (k < col0 + BN)
   int num_tiles;
   int mb, nb;
   int b_kmajor;
@@ -160,6 +161,17 @@ __device__ __forceinline__ bool tile_skipped(const Params& p, int bm, int bn) {
   return false;
 }
 
+// k-slices [kb0, kb1) of tile (bm, bn): a triangular operand whose zero
+// triangle starts on a 128 boundary contributes nothing outside this range.
+__device__ __forceinline__ void k_range(const Params& p, int bm, int bn, int nkb, int& kb0,
+                                        int& kb1) {
+  kb0 = 0;
+  kb1 = nkb;
+  if (p.tri == 1) kb0 = min(nkb, bm * (BM / BK));
+  else if (p.tri == 2) kb1 = min(nkb, (bm + 1) * (BM / BK));
+  else if (p.tri == 3) kb1 = min(nkb, (bn + 1) * (BN / BK));
+}
+
 __global__ void __launch_bounds__(THREADS, 1)
 tf32x3_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_b,
               Params p) {
@@ -214,7 +226,9 @@ tf32x3_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__
       for (int t = blockIdx.x; t < p.num_tiles && !*abort_flag; t += gridDim.x) {
         const int bm = t % p.mb, bn = t / p.mb;
         if (tile_skipped(p, bm, bn)) continue;
-        for (int kb = 0; kb < nkb; ++kb) {
+        int kb0, kb1;
+        k_range(p, bm, bn, nkb, kb0, kb1);
+        for (int kb = kb0; kb < kb1; ++kb) {
           if (!mbar_wait(&empty[stage], phase ^ 1, abort_flag)) break;
           mbar_expect_tx(&full[stage], A_BYTES + B_BYTES);
           const int k0 = kb * BK;
@@ -242,15 +256,17 @@ tf32x3_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__
       for (int t = blockIdx.x; ok && t < p.num_tiles && !*abort_flag; t += gridDim.x) {
         const int bm = t % p.mb, bn = t / p.mb;
         if (tile_skipped(p, bm, bn)) continue;
+        int kb0, kb1;
+        k_range(p, bm, bn, nkb, kb0, kb1);
         // one TMEM accumulation per CHUNK_KB k-slices (CHUNK_KB * 32 of K)
-        for (int kc = 0; kc < nkb && ok; kc += CHUNK_KB) {
+        for (int kc = kb0; kc < kb1 && ok; kc += CHUNK_KB) {
           if (!mbar_wait(&tempty[acc], acc_phase ^ 1, abort_flag)) {
             ok = false;
             break;
           }
           fence_after();
           const uint32_t d_tmem = tmem_base + (uint32_t)(acc * BN);
-          const int kend = min(nkb, kc + CHUNK_KB);
+          const int kend = min(kb1, kc + CHUNK_KB);
           for (int kb = kc; kb < kend; ++kb) {
             if (!mbar_wait(&conv[stage], phase, abort_flag)) {
               ok = false;
@@ -294,8 +310,10 @@ tf32x3_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__
     for (int t = blockIdx.x; t < p.num_tiles && !*abort_flag; t += gridDim.x) {
       const int bm = t % p.mb, bn = t / p.mb;
       if (tile_skipped(p, bm, bn)) continue;
+      int kb0, kb1;
+      k_range(p, bm, bn, nkb, kb0, kb1);
       bool ok = true;
-      for (int kb = 0; kb < nkb; ++kb) {
+      for (int kb = kb0; kb < kb1; ++kb) {
         if (!mbar_wait(&full[stage], phase, abort_flag)) {
           ok = false;
           break;
@@ -354,7 +372,9 @@ tf32x3_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__
       float sum[BN];
 #pragma unroll
       for (int j = 0; j < BN; ++j) sum[j] = 0.f;
-      for (int kc = 0; kc < nkb; kc += CHUNK_KB) {
+      int kb0, kb1;
+      k_range(p, bm, bn, nkb, kb0, kb1);
+      for (int kc = kb0; kc < kb1; kc += CHUNK_KB) {
         if (!mbar_wait(&tfull[acc], acc_phase, abort_flag)) {
           ok = false;
           break;
@@ -469,7 +489,7 @@ bool eligible(int ta, int tb, int64_t M, int64_t N, int64_t K, const float* A, i
 }
 
 int launch(int tb, int64_t M, int64_t N, int64_t K, float alpha, const float* A, int64_t lda,
-           const float* B, int64_t ldb, float beta, float* C, int64_t ldc, int uplo,
+           const float* B, int64_t ldb, float beta, float* C, int64_t ldc, int uplo, int tri,
            cudaStream_t st) {
   CUtensorMap ma, mbm;
   GQ_TRY(make_map(&ma, A, M, K, lda, BM));
@@ -484,15 +504,18 @@ int launch(int tb, int64_t M, int64_t N, int64_t K, float alpha, const float* A,
   p.alpha = alpha;
   p.beta = beta;
   p.uplo = uplo;
+  p.tri = tri;
   p.mb = (int)ceil_div(M, BM);
   p.nb = (int)ceil_div(N, BN);
   p.num_tiles = p.mb * p.nb;
   p.b_kmajor = tb;
-  static bool attr = false;
-  if (!attr) {
+  static int attr_device = -1;
+  int dev = 0;
+  GQ_CHECK_CUDA(cudaGetDevice(&dev));
+  if (attr_device != dev) {
     GQ_CHECK_CUDA(cudaFuncSetAttribute(tf32x3_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                        SMEM_BYTES));
-    attr = true;
+    attr_device = dev;
   }
   const int grid = std::min(p.num_tiles, sm_count());
   tf32x3_kernel<<<grid, THREADS, SMEM_BYTES, st>>>(ma, mbm, p);
@@ -509,6 +532,6 @@ extern "C" int gq_gemm_f32_tc(int trans_b, int64_t M, int64_t N, int64_t K, floa
              "gq_gemm_f32_tc: needs M, N >= 128, K >= 32, 16-byte aligned operands and leading "
              "dimensions that are multiples of 4");
   GQ_REQUIRE(uplo >= 0 && uplo <= 2, "gq_gemm_f32_tc: bad uplo");
-  return gq::tc32::launch(trans_b ? 1 : 0, M, N, K, alpha, a, lda, b, ldb, beta, c, ldc, uplo,
+  return gq::tc32::launch(trans_b ? 1 : 0, M, N, K, alpha, a, lda, b, ldb, beta, c, ldc, uplo, 0,
                           gq::as_stream(stream));
 }

@@ -135,6 +135,24 @@ def test_hessian_factor_matches_oracle(ordering):
     assert np.abs(ident - np.eye(512)).max() < 5e-3
 
 
+@pytest.mark.parametrize("d", [128, 200, 384, 1000, 1030])
+def test_hessian_factor_sizes(d):
+    """Recursive inverse Cholesky: partial last leaf (200, 1000, 1030) and a
+    leading dimension that is not a multiple of 4 (1030: CUDA-core GEMMs)."""
+    rng = np.random.default_rng(d)
+    x = rng.standard_normal((2 * d, d)).astype(np.float32) * rng.uniform(0.2, 3.0, d).astype(np.float32)
+    h = (x.astype(np.float64).T @ x / x.shape[0]).astype(np.float32)
+    cfg = QuantConfig(ordering_mode="diag_h", semantics="intended")
+    f = G.factor_hessian(h, cfg, want_hd=True)
+    u64, perm64, att = og.process_hessian_intended(h, "diag_h", 0.01)
+    assert f.attempt == att == 0
+    u = f.u.cpu().numpy().astype(np.float64)
+    assert np.array_equal(np.tril(u, -1), np.zeros_like(u))
+    assert np.linalg.norm(u - u64) / np.linalg.norm(u64) < 2e-3
+    hd = f.hd.cpu().numpy().astype(np.float64)
+    assert np.abs(u @ hd @ u.T - np.eye(d)).max() < 5e-3
+
+
 def test_hessian_factor_retries_damping_on_indefinite_input():
     # a negative-definite direction that 1% damping cannot fix but 100x can
     n = 128
