@@ -441,6 +441,52 @@ def run_ours(args, world, rank, local):
         print(json.dumps(line), flush=True)
 
 
+def run_sharded(args, world, rank, local):
+    """One layer set spread over all ranks (strong scaling): each rank holds a
+    1/N token shard of every input, H is summed by NCCL all-reduce, every rank
+    factors it, and each sweeps its 1/N of the rows (outputs gathered)."""
+    import torch
+    from jax_gptq_b200 import _lib
+    from jax_gptq_b200 import distributed as D
+    from jax_gptq_b200 import layerset as LS
+    from jax_gptq_b200.config import QuantConfig
+
+    _lib.lib()
+    shapes = LS.LLAMA2_7B
+    dims = LS.group_dims(shapes)
+    cfg = QuantConfig(w_bits=4, group_size=128, sym=False, damp_percent=0.01,
+                      ordering_mode="diag_h", semantics="intended")
+    weights = LS.synth_weights(shapes, 0.02, 0)
+    t0, t1 = D.shard_range(args.tokens, rank, world)
+    inputs = {grp: LS.synth_activations(t1 - t0, d, 10 + i + 100 * rank)[0]
+              for i, (grp, d) in enumerate(dims.items())}
+    torch.cuda.synchronize()
+    for _ in range(args.warmup):
+        D.quantize_layer_gptq_sharded(weights, inputs, cfg, shapes)
+    sampler = ClockSampler(local)
+    _barrier(world)
+    sampler.start()
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(args.steps):
+        D.quantize_layer_gptq_sharded(weights, inputs, cfg, shapes)
+    e1.record()
+    _barrier(world)
+    clocks = sampler.stop()
+    ms = _max_over_ranks(e0.elapsed_time(e1) / args.steps, world)
+    if rank == 0:
+        print(json.dumps({
+            "metric": METRIC, "value": ms / 1000.0, "unit": "s/layer", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
+            "higher_is_better": False, "scaling": "strong", "vs_baseline": None, "dtype": "f32",
+            "data": "synthetic (seeded, on device)",
+            "config": {"workload": WORKLOAD, "tokens": args.tokens,
+                       "parallelism": f"token-sharded H (NCCL all-reduce) + row-sharded sweep x{world}",
+                       "l2_flush": "inputs larger than L2"},
+            "clocks": clocks}), flush=True)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -459,6 +505,9 @@ def main():
                          "pivoted QR on a --dim x --dim matrix (profiling)")
     ap.add_argument("--dim", type=int, default=4096)
     ap.add_argument("--panel", type=int, default=64)
+    ap.add_argument("--strategy", choices=["layer", "sharded"], default="layer",
+                    help="layer: each rank quantizes its own layer set (weak scaling, no "
+                         "collective); sharded: one layer set over all ranks (strong scaling)")
     args = ap.parse_args()
     if args.only in ("syrk", "qr"):
         import torch
@@ -478,7 +527,10 @@ def main():
         return
     world, rank, local = _dist_init()
     try:
-        run_ours(args, world, rank, local)
+        if args.strategy == "sharded":
+            run_sharded(args, world, rank, local)
+        else:
+            run_ours(args, world, rank, local)
     finally:
         if world > 1:
             import torch.distributed as dist

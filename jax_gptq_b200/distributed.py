@@ -1,0 +1,229 @@
+"""Multi-GPU partitioning of the quantization path (one process per GPU).
+
+The reference runs on a single device; these are the ways its path splits
+across GPUs, each tied to an independence in the computation:
+
+* token-sharded statistics -- ``H = sum_r X_r^T X_r`` (``stats.py:4-18`` is a
+  sum over tokens): every rank forms the Gram matrix of its own tokens on its
+  tensor cores, then one in-place float32 all-reduce per input group (NCCL
+  over NVLink; the reduction of one group overlaps the next group's SYRK);
+* replicated factor -- every rank factors the identical reduced H
+  (``gptq_ref.py:44-93``); the factorization is deterministic, so the ranks'
+  ``U`` agree bit for bit and nothing is broadcast;
+* row-sharded sweep -- rows of ``W`` are independent once ``U`` and the
+  permutation are fixed (``gptq_ref.py:136-155`` quantizes row-wise), so each
+  rank sweeps a contiguous block of rows with no communication, and one
+  all-gather assembles the outputs when the caller wants them whole;
+* layer parallelism -- whole layer sets are independent units and go to ranks
+  by a longest-processing-time-first schedule on their cost, no collective.
+
+Pivoted QR does not shard (a global argmax per pivot step); it runs as
+independent replicas.
+
+Process groups are the caller's (``torch.distributed`` with the NCCL backend
+on GPUs); every function takes an optional ``group``.  The collective helpers
+also accept CPU tensors under gloo.
+"""
+
+from __future__ import annotations
+
+from typing import Hashable
+
+import torch
+
+from . import _arrays as A
+from . import stats
+from .config import QuantConfig
+from .gptq_ref import SweepResult, factor_hessian, gptq_sweep
+
+SWEEP_ROW_ALIGN = 32  # the sweep kernel runs one warp per 32 rows
+
+
+def _dist():
+    import torch.distributed as dist
+    return dist
+
+
+def rank_world(group=None) -> tuple[int, int]:
+    """(rank, world size) in ``group``; (0, 1) without an initialized process group."""
+    dist = _dist()
+    if not (dist.is_available() and dist.is_initialized()):
+        return 0, 1
+    return dist.get_rank(group), dist.get_world_size(group)
+
+
+def shard_range(n: int, rank: int, world: int, align: int = 1) -> tuple[int, int]:
+    """Contiguous block ``[start, stop)`` of ``n`` items owned by ``rank``.
+
+    Items are dealt in blocks of ``align`` (only the last block may be short);
+    the first ``n_blocks % world`` ranks get one block more.  Ranges of all
+    ranks tile ``[0, n)`` in rank order; a rank may get an empty range.
+    """
+    if world < 1 or not 0 <= rank < world:
+        raise ValueError(f"bad rank {rank} for world size {world}")
+    if n < 0 or align < 1:
+        raise ValueError(f"bad n={n} or align={align}")
+    nb = -(-n // align)
+    base, extra = divmod(nb, world)
+    b0 = rank * base + min(rank, extra)
+    b1 = b0 + base + (1 if rank < extra else 0)
+    return min(n, b0 * align), min(n, b1 * align)
+
+
+def lpt_assign(costs: dict[Hashable, float], world: int) -> list[list[Hashable]]:
+    """Longest-processing-time-first schedule: units in decreasing cost (ties
+    by key order), each to the currently least-loaded rank (ties to the lower
+    rank).  Deterministic, so every rank computes the same assignment."""
+    if world < 1:
+        raise ValueError("world must be >= 1")
+    loads = [0.0] * world
+    out: list[list[Hashable]] = [[] for _ in range(world)]
+    for key, cost in sorted(costs.items(), key=lambda kv: (-float(kv[1]), str(kv[0]))):
+        r = min(range(world), key=lambda i: (loads[i], i))
+        out[r].append(key)
+        loads[r] += float(cost)
+    return out
+
+
+# Relative throughputs used by the layer-set cost model (only compared with
+# each other): bf16 tensor-core SYRK, fp32 (3xTF32) tensor-core factor and
+# sweep GEMMs.
+_BF16_RATE = 1.0e15
+_F32_RATE = 1.7e14
+
+
+def layer_set_cost(shapes, tokens: int) -> float:
+    """Modelled seconds for one GPTQ layer set: SYRK per input group
+    (tokens * d^2), inverse-Cholesky factor (2 d^3 / 3) and sweep GEMMs
+    (m * n^2 per group of row-stacked linears)."""
+    dims: dict[str, int] = {}
+    rows: dict[str, int] = {}
+    for _name, m, n, grp in shapes:
+        dims[grp] = n
+        rows[grp] = rows.get(grp, 0) + m
+    t = 0.0
+    for grp, d in dims.items():
+        t += tokens * d * d / _BF16_RATE
+        t += (2.0 * d ** 3 / 3.0) / _F32_RATE
+        t += rows[grp] * d * d / _F32_RATE
+    return t
+
+
+def allreduce_sum_(t: torch.Tensor, group=None, async_op: bool = False):
+    """In-place sum over the ranks of ``group``; returns the work handle when
+    ``async_op`` (None for a single rank)."""
+    dist = _dist()
+    if not (dist.is_available() and dist.is_initialized()) or dist.get_world_size(group) == 1:
+        return None
+    return dist.all_reduce(t, op=dist.ReduceOp.SUM, group=group, async_op=async_op)
+
+
+def gather_rows(local: torch.Tensor, n_rows: int, group=None,
+                align: int = SWEEP_ROW_ALIGN) -> torch.Tensor:
+    """Inverse of row sharding: every rank passes its ``shard_range(n_rows,
+    rank, world, align)`` block of rows; every rank gets the whole
+    ``[n_rows, ...]`` tensor (one all-gather of equal-size padded blocks)."""
+    rank, world = rank_world(group)
+    r0, r1 = shard_range(n_rows, rank, world, align)
+    if local.shape[0] != r1 - r0:
+        raise ValueError(f"rank {rank}: expected {r1 - r0} rows, got {local.shape[0]}")
+    if world == 1:
+        return local
+    spans = [shard_range(n_rows, r, world, align) for r in range(world)]
+    rows_max = max(b - a for a, b in spans)
+    tail = tuple(local.shape[1:])
+    pad = torch.zeros((rows_max,) + tail, dtype=local.dtype, device=local.device)
+    pad[: r1 - r0] = local
+    blocks = [torch.empty_like(pad) for _ in range(world)]
+    _dist().all_gather(blocks, pad, group=group)
+    return torch.cat([blocks[r][: b - a] for r, (a, b) in enumerate(spans)], dim=0)
+
+
+def hessians_token_sharded(inputs_local: dict[str, torch.Tensor], group=None,
+                           inputs_float_local: dict[str, torch.Tensor] | None = None):
+    """``{group: H}`` (and ``{group: G}`` when float inputs are given) summed
+    over the ranks' token shards, identical on every rank.
+
+    ``inputs_local[grp]`` is this rank's ``[tokens_r, d]`` activations on the
+    device (bf16 runs the tcgen05 SYRK).  Each group's all-reduce is issued
+    asynchronously, so NCCL moves one group's H while the next SYRK runs."""
+    A.require_cuda()
+    hs: dict[str, torch.Tensor] = {}
+    gs: dict[str, torch.Tensor] = {}
+    pending = []
+    for grp, x in inputs_local.items():
+        d = x.shape[1]
+        h = torch.empty((d, d), dtype=torch.float32, device=x.device)
+        stats.syrk_into(h, x, accumulate=False)
+        pending.append(allreduce_sum_(h, group, async_op=True))
+        hs[grp] = h
+        if inputs_float_local is not None:
+            g = torch.empty((d, d), dtype=torch.float32, device=x.device)
+            stats.gemm_tn_into(g, inputs_float_local[grp], x, accumulate=False)
+            pending.append(allreduce_sum_(g, group, async_op=True))
+            gs[grp] = g
+    for w in pending:
+        if w is not None:
+            w.wait()
+    return (hs, gs) if inputs_float_local is not None else hs
+
+
+def _members(shapes, grp):
+    return [(name, m) for name, m, _, g in shapes if g == grp]
+
+
+def quantize_layer_gptq_sharded(weights: dict, inputs_local: dict, cfg: QuantConfig, shapes,
+                                group=None, gather: bool = True) -> dict[str, SweepResult]:
+    """GPTQ for one layer set spread over the ranks of ``group``.
+
+    ``inputs_local[grp]``: this rank's token shard of the group's activations.
+    ``weights[name]``: the whole weight (every rank holds it; each sweeps only
+    its ``shard_range`` rows of the group's row-stacked linears).  With
+    ``gather`` every rank returns whole results keyed by linear name;
+    otherwise results are keyed by input group and hold this rank's rows of
+    the group's row-stacked matrix."""
+    rank, world = rank_world(group)
+    hs = hessians_token_sharded(inputs_local, group)
+    out: dict[str, SweepResult] = {}
+    for grp, h in hs.items():
+        f = factor_hessian(h, cfg)
+        members = _members(shapes, grp)
+        w = weights[members[0][0]] if len(members) == 1 else \
+            torch.cat([weights[name] for name, _ in members], dim=0)
+        m = w.shape[0]
+        r0, r1 = shard_range(m, rank, world, SWEEP_ROW_ALIGN)
+        res = gptq_sweep(w[r0:r1], f.u, f.perm, cfg)
+        if not gather:
+            out[grp] = res
+            continue
+        deq = gather_rows(res.dequant, m, group)
+        codes = gather_rows(res.codes, m, group)
+        scales = gather_rows(res.scales, m, group)
+        zeros = gather_rows(res.zeros, m, group)
+        i0 = 0
+        for name, mi in members:
+            out[name] = SweepResult(deq[i0:i0 + mi], codes[i0:i0 + mi], scales[i0:i0 + mi],
+                                    zeros[i0:i0 + mi], res.g_idx, res.perm)
+            i0 += mi
+    return out
+
+
+def layer_sets_for_rank(n_layers: int, shapes, tokens: int, group=None) -> list[int]:
+    """Layer-parallel schedule: the layer indices this rank quantizes (LPT on
+    :func:`layer_set_cost`; equal-cost layers are dealt round-robin)."""
+    rank, world = rank_world(group)
+    cost = layer_set_cost(shapes, tokens)
+    return sorted(lpt_assign({i: cost for i in range(n_layers)}, world)[rank])
+
+
+def tokens_for_rank(n_tokens: int, group=None) -> tuple[int, int]:
+    """This rank's token shard ``[start, stop)`` for token-sharded statistics."""
+    rank, world = rank_world(group)
+    return shard_range(n_tokens, rank, world)
+
+
+__all__ = [
+    "SWEEP_ROW_ALIGN", "rank_world", "shard_range", "lpt_assign", "layer_set_cost",
+    "allreduce_sum_", "gather_rows", "hessians_token_sharded", "quantize_layer_gptq_sharded",
+    "layer_sets_for_rank", "tokens_for_rank",
+]
