@@ -67,8 +67,10 @@ int gq_rtn(const float* w, int64_t m, int64_t n, int64_t ldw, const int32_t* per
  * are computed whole).  Used for the GPTQ lazy trailing update, Cholesky /
  * inverse updates, Qronos and the QR compact-WY update.
  * gq_sgemm runs the tcgen05 3xTF32 kernel (gq_gemm_f32_tc) when trans_a = 0,
- * M, N >= 128, K >= 32, A and B are 16-byte aligned and lda, ldb are
- * multiples of 4, and the CUDA-core kernel (gq_sgemm_simt) otherwise.
+ * trans_b = 1, N >= 128, K >= 32, A and B are 16-byte aligned and lda, ldb
+ * are multiples of 4 (any M >= 1, so a row's result does not depend on how
+ * many rows share the call), and the CUDA-core kernel (gq_sgemm_simt)
+ * otherwise.
  */
 int gq_sgemm(int trans_a, int trans_b, int64_t M, int64_t N, int64_t K, float alpha,
              const float* a, int64_t lda, const float* b, int64_t ldb, float beta,
@@ -77,7 +79,8 @@ int gq_sgemm_simt(int trans_a, int trans_b, int64_t M, int64_t N, int64_t K, flo
                   const float* a, int64_t lda, const float* b, int64_t ldb, float beta,
                   float* c, int64_t ldc, int uplo, void* stream);
 /* tcgen05 kind::tf32 with a 3-pass hi/lo operand split (error near 2^-21 per
- * product); A [M, K] row-major, B [K, N] (trans_b = 0) or [N, K] (1). */
+ * product); A [M, K] and B [N, K] row-major (trans_b must be 1: both operands
+ * K-major); GQ_EINVAL for any other layout or for N < 128 or K < 32. */
 int gq_gemm_f32_tc(int trans_b, int64_t M, int64_t N, int64_t K, float alpha,
                    const float* a, int64_t lda, const float* b, int64_t ldb, float beta,
                    float* c, int64_t ldc, int uplo, void* stream);

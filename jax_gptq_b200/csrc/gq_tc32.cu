@@ -481,7 +481,10 @@ bool eligible(int ta, int tb, int64_t M, int64_t N, int64_t K, const float* A, i
   // Both operands K-major only: for 32-bit MN-major operands the UMMA wants the
   // 32-byte-atom 128B swizzle, which this kernel's TMA loads do not produce.
   if (ta != 0 || tb != 1) return false;
-  if (M < 128 || N < 128 || K < 32) return false;
+  // M may be anything >= 1 (rows past M are zero-filled by TMA and not
+  // stored), so the arithmetic a row gets does not depend on how many rows
+  // share the call; N and K are fixed by the operands' shapes.
+  if (M < 1 || N < 128 || K < 32) return false;
   if (!aligned16(A) || !aligned16(B)) return false;
   if ((lda & 3) || (ldb & 3)) return false;
   if (M >= (1ll << 31) || N >= (1ll << 31) || K >= (1ll << 31)) return false;
@@ -529,7 +532,7 @@ extern "C" int gq_gemm_f32_tc(int trans_b, int64_t M, int64_t N, int64_t K, floa
                               const float* a, int64_t lda, const float* b, int64_t ldb, float beta,
                               float* c, int64_t ldc, int uplo, void* stream) {
   GQ_REQUIRE(gq::tc32::eligible(0, trans_b, M, N, K, a, lda, b, ldb, c, ldc),
-             "gq_gemm_f32_tc: needs M, N >= 128, K >= 32, 16-byte aligned operands and leading "
+             "gq_gemm_f32_tc: needs M >= 1, N >= 128, K >= 32, 16-byte aligned operands and leading "
              "dimensions that are multiples of 4");
   GQ_REQUIRE(uplo >= 0 && uplo <= 2, "gq_gemm_f32_tc: bad uplo");
   return gq::tc32::launch(trans_b ? 1 : 0, M, N, K, alpha, a, lda, b, ldb, beta, c, ldc, uplo, 0,

@@ -26,7 +26,8 @@ def _status():
 @pytest.mark.parametrize("M,N,K,tb,alpha,beta", [
     (128, 128, 32, 1, 1.0, 0.0), (256, 384, 128, 1, -1.0, 1.0), (300, 200, 76, 1, 0.5, 2.0),
     (1000, 520, 640, 1, 1.0, 0.0), (129, 1024, 36, 1, -1.0, 1.0), (4096, 256, 128, 1, -1.0, 1.0),
-    (512, 512, 4096, 1, 1.0, 0.0)])
+    (512, 512, 4096, 1, 1.0, 0.0), (96, 256, 128, 1, -1.0, 1.0), (1, 384, 64, 1, 1.0, 0.0),
+    (33, 130, 96, 1, 2.0, -1.0)])
 def test_tf32x3_matches_float64(M, N, K, tb, alpha, beta):
     rng = np.random.default_rng(M + N + K)
     a = rng.standard_normal((M, K)).astype(np.float32)
