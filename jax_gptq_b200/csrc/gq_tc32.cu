@@ -16,7 +16,9 @@
 //   warp 0     TMA producer (one thread)
 //   warp 1     MMA issuer (one thread), 2 TMEM accumulators of 128 columns
 //   warps 2-5  hi/lo converters (in place: raw -> hi; lo to its own buffer)
-//   warps 6-9  epilogue: tcgen05.ld, alpha/beta, fp32 stores
+//   warps 6-9  epilogue: tcgen05.ld, then for beta 0 / 1 swizzled 32 x 32
+//              chunks written by TMA tensor stores / fp32 reduce-adds (no
+//              read of C by the SM), for other beta per-row loads and stores
 // All waits are bounded (timeout -> device status word, no hang); no
 // multicast loads.
 #include <cuda.h>
@@ -48,7 +50,11 @@ constexpr int B_BYTES = BN * BK * 4;   // 16 KB
 constexpr int STAGE_BYTES = 2 * (A_BYTES + B_BYTES);  // raw/hi + lo for A and B
 constexpr int THREADS = 320;
 constexpr int TMEM_COLS = 256;
-constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024 + 256;
+// epilogue staging: per epilogue warp two 32 x 32 fp32 chunks (4 KB each,
+// 128-byte swizzled rows, the layout a SWIZZLE_128B tensor store reads)
+constexpr int C_CHUNK_BYTES = 32 * 32 * 4;
+constexpr int C_STAGE_BYTES = 4 * 2 * C_CHUNK_BYTES;
+constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + C_STAGE_BYTES + 1024 + 256;
 
 struct Params {
   float* c;
@@ -60,6 +66,7 @@ struct Params {
   int num_tiles;
   int mb, nb;
   int b_kmajor;
+  int c_mode;  // 0: stores from registers (any beta); 1: TMA store (beta 0); 2: TMA add (beta 1)
 };
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
@@ -174,7 +181,7 @@ __device__ __forceinline__ void k_range(const Params& p, int bm, int bn, int nkb
 
 __global__ void __launch_bounds__(THREADS, 1)
 tf32x3_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_b,
-              Params p) {
+              const __grid_constant__ CUtensorMap map_c, Params p) {
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~uintptr_t(1023));
@@ -183,7 +190,8 @@ tf32x3_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__
   auto b_hi = [&](int s) { return smem + s * STAGE_BYTES + A_BYTES; };
   auto a_lo = [&](int s) { return smem + s * STAGE_BYTES + A_BYTES + B_BYTES; };
   auto b_lo = [&](int s) { return smem + s * STAGE_BYTES + 2 * A_BYTES + B_BYTES; };
-  uint64_t* full = reinterpret_cast<uint64_t*>(smem + STAGES * STAGE_BYTES);
+  uint8_t* c_stage = smem + STAGES * STAGE_BYTES;
+  uint64_t* full = reinterpret_cast<uint64_t*>(c_stage + C_STAGE_BYTES);
   uint64_t* conv = full + STAGES;
   uint64_t* empty = conv + STAGES;
   uint64_t* tfull = empty + STAGES;
@@ -397,7 +405,43 @@ tf32x3_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__
       if (!ok) break;
       const int64_t row = (int64_t)bm * BM + row_in_tile;
       const int64_t col0 = (int64_t)bn * BN;
-      if (row < p.M) {
+      if (p.c_mode != 0) {
+        // 32-column chunks staged in shared memory and written by the tensor
+        // engine: a plain store (beta 0) or an fp32 add into C at L2 (beta 1,
+        // C + alpha * sum rounded once, as fmaf(1, C, alpha * sum) would be).
+        // Rows and columns past M, N are clipped by the tensor map.
+#pragma unroll
+        for (int cc = 0; cc < BN / 32; ++cc) {
+          uint8_t* buf = c_stage + (quarter * 2 + (cc & 1)) * C_CHUNK_BYTES;
+          if (lane == 0) asm volatile("cp.async.bulk.wait_group.read 1;" ::: "memory");
+          __syncwarp();
+#pragma unroll
+          for (int j4 = 0; j4 < 8; ++j4) {
+            const float4 v = make_float4(p.alpha * sum[cc * 32 + 4 * j4], p.alpha * sum[cc * 32 + 4 * j4 + 1],
+                                         p.alpha * sum[cc * 32 + 4 * j4 + 2],
+                                         p.alpha * sum[cc * 32 + 4 * j4 + 3]);
+            *reinterpret_cast<float4*>(buf + lane * 128 + ((j4 ^ (lane & 7)) << 4)) = v;
+          }
+          asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+          __syncwarp();
+          if (lane == 0) {
+            const int x = (int)(col0 + cc * 32), y = (int)(bm * BM + quarter * 32);
+            if (p.c_mode == 2)
+              asm volatile(
+                  "cp.reduce.async.bulk.tensor.2d.global.shared::cta.add.tile.bulk_group"
+                  " [%0, {%2, %3}], [%1];" ::"l"(reinterpret_cast<uint64_t>(&map_c)),
+                  "r"(smem_u32(buf)), "r"(x), "r"(y)
+                  : "memory");
+            else
+              asm volatile(
+                  "cp.async.bulk.tensor.2d.global.shared::cta.tile.bulk_group"
+                  " [%0, {%2, %3}], [%1];" ::"l"(reinterpret_cast<uint64_t>(&map_c)),
+                  "r"(smem_u32(buf)), "r"(x), "r"(y)
+                  : "memory");
+            asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+          }
+        }
+      } else if (row < p.M) {
         float* cp = p.c + row * p.ldc + col0;
         const bool vec = (col0 + BN <= p.N) && ((reinterpret_cast<uintptr_t>(cp) & 15) == 0);
         if (vec) {
@@ -428,6 +472,8 @@ tf32x3_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__
     }
   }
 
+  // tensor stores must finish (shared memory read, global writes done) before exit
+  if (warp >= 6 && lane == 0) asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
   fence_before();
   __syncthreads();
   if (warp == 1) {
@@ -512,6 +558,12 @@ int launch(int tb, int64_t M, int64_t N, int64_t K, float alpha, const float* A,
   p.nb = (int)ceil_div(N, BN);
   p.num_tiles = p.mb * p.nb;
   p.b_kmajor = tb;
+  CUtensorMap mc = ma;  // unused unless c_mode != 0
+  p.c_mode = 0;
+  if ((beta == 0.f || beta == 1.f) && aligned16(C) && (ldc & 3) == 0 && ldc >= N) {
+    GQ_TRY(make_map(&mc, C, M, N, ldc, 32));
+    p.c_mode = (beta == 0.f) ? 1 : 2;
+  }
   static int attr_device = -1;
   int dev = 0;
   GQ_CHECK_CUDA(cudaGetDevice(&dev));
@@ -521,7 +573,7 @@ int launch(int tb, int64_t M, int64_t N, int64_t K, float alpha, const float* A,
     attr_device = dev;
   }
   const int grid = std::min(p.num_tiles, sm_count());
-  tf32x3_kernel<<<grid, THREADS, SMEM_BYTES, st>>>(ma, mbm, p);
+  tf32x3_kernel<<<grid, THREADS, SMEM_BYTES, st>>>(ma, mbm, mc, p);
   return check_launch("tcgen05 tf32x3 gemm");
 }
 
