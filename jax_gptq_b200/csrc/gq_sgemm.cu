@@ -151,7 +151,8 @@ int sgemm(int ta, int tb, int64_t M, int64_t N, int64_t K, float alpha, const fl
 }
 
 // sgemm with a triangular operand whose zero triangle is stored as zeros and
-// starts on 128 boundaries (tri: 1 A upper, 2 A lower, 3 B lower): the
+// starts on 128 boundaries (tri: 1 A upper, 2 A lower, 3 B lower, 4 B upper;
+// "upper" = zero below the diagonal, B given [N, K]): the
 // tensor-core path skips the all-zero k-slices of each tile; the result is the
 // same as the full product.
 int sgemm_tri(int ta, int tb, int64_t M, int64_t N, int64_t K, float alpha, const float* A,

@@ -62,7 +62,8 @@ struct Params {
   int64_t M, N, K;
   float alpha, beta;
   int uplo;
-  int tri;  // 0 none, 1 A upper (k >= row0), 2 A lower (k < row0 + BM), 3 B lower (k < col0 + BN)
+  int tri;  // 0 none, 1 A upper (k >= row0), 2 A lower (k < row0 + BM), 3 B lower (k < col0 + BN),
+            // 4 B upper (k >= col0)
   int num_tiles;
   int mb, nb;
   int b_kmajor;
@@ -177,6 +178,7 @@ __device__ __forceinline__ void k_range(const Params& p, int bm, int bn, int nkb
   if (p.tri == 1) kb0 = min(nkb, bm * (BM / BK));
   else if (p.tri == 2) kb1 = min(nkb, (bm + 1) * (BM / BK));
   else if (p.tri == 3) kb1 = min(nkb, (bn + 1) * (BN / BK));
+  else if (p.tri == 4) kb0 = min(nkb, bn * (BN / BK));
 }
 
 __global__ void __launch_bounds__(THREADS, 1)
