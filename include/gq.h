@@ -143,6 +143,20 @@ int gq_hessian_factor(const float* h, int64_t d, int64_t ldh, const int32_t* per
                       void* workspace, int64_t workspace_bytes, int* attempt_out,
                       void* stream);
 
+/* One damping attempt of gq_hessian_factor -- iteration `attempt` (0..4) of
+ * gptq_ref.py:80-83, damp = damp_percent * 10^attempt -- enqueued on `stream`
+ * with no host synchronization.  `status` is an int in DEVICE memory: 0 when
+ * the damped Hessian factored (u then holds the factor), non-zero when a
+ * pivot was not positive (u is then meaningless).  Lets a caller run the
+ * factors of several Hessians concurrently on different streams and read all
+ * statuses after one synchronization; gq_hessian_factor is this call in a
+ * loop with a synchronization per attempt.  Same workspace as
+ * gq_hessian_factor (the status word may live anywhere else). */
+int gq_hessian_factor_attempt(const float* h, int64_t d, int64_t ldh, const int32_t* perm,
+                              double damp_percent, int attempt, float* u, int64_t ldu,
+                              float* hd_out, void* workspace, int64_t workspace_bytes,
+                              int* status, void* stream);
+
 /* ------------------------------------------------------------------------
  * GPTQ column sweep (the computation gptq_ref.py:136-155 stands in for).
  * With u = I it reproduces gptq_forward_step bit-exactly.

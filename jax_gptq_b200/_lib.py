@@ -45,6 +45,8 @@ SIGNATURES = {
     "gq_hessian_factor_workspace_size": (c_int64, [c_int64]),
     "gq_hessian_factor": (c_int, [_P, c_int64, c_int64, _P, c_double, _P, c_int64, _P, _P, c_int64,
                                   ctypes.POINTER(c_int), _P]),
+    "gq_hessian_factor_attempt": (c_int, [_P, c_int64, c_int64, _P, c_double, c_int, _P, c_int64,
+                                          _P, _P, c_int64, _P, _P]),
     "gq_gptq_sweep_workspace_size": (c_int64, [c_int64, c_int64]),
     "gq_gptq_sweep": (c_int, [_P, c_int64, c_int64, c_int64, _P, _P, c_int64, _P, c_int, c_int, c_int,
                               c_int, _P, _P, c_int, _P, _P, _P, _P, _P, _P, c_int64, _P]),

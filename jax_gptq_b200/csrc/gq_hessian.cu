@@ -375,6 +375,40 @@ int64_t gq_hessian_factor_workspace_size(int64_t d) {
   return gq::hessian_ws_floats(d) * (int64_t)sizeof(float);
 }
 
+int gq_hessian_factor_attempt(const float* h, int64_t d, int64_t ldh, const int32_t* perm,
+                              double damp_percent, int attempt, float* u, int64_t ldu,
+                              float* hd_out, void* workspace, int64_t workspace_bytes, int* status,
+                              void* stream) {
+  GQ_REQUIRE(h != nullptr && u != nullptr && status != nullptr,
+             "gq_hessian_factor_attempt: NULL h, u or status");
+  GQ_REQUIRE(d > 0 && ldh >= d && ldu >= d, "gq_hessian_factor_attempt: bad shape");
+  GQ_REQUIRE(workspace_bytes >= gq_hessian_factor_workspace_size(d),
+             "gq_hessian_factor_attempt: workspace too small (%lld < %lld)",
+             (long long)workspace_bytes, (long long)gq_hessian_factor_workspace_size(d));
+  GQ_REQUIRE(damp_percent >= 0.0, "gq_hessian_factor_attempt: negative damp_percent");
+  GQ_REQUIRE(attempt >= 0 && attempt < 5, "gq_hessian_factor_attempt: attempt must be 0..4");
+  cudaStream_t st = gq::as_stream(stream);
+  float* ws = reinterpret_cast<float*>(workspace);
+  float* ht = ws;                                  // d*d
+  float* scratch = ht + d * d;                     // (d/2+NB) x (d+NB)
+  int64_t half = d / 2 + gq::NB;
+  float* mean = scratch + half * (d + gq::NB);     // 1 float
+  GQ_TRY(gq::diag_kernel_setup());
+  gq::diag_mean_kernel<<<1, 1024, 0, st>>>(h, d, ldh, mean);
+  GQ_TRY(gq::check_launch("diag_mean"));
+  const double damp = std::pow(10.0, attempt) * damp_percent;
+  GQ_CHECK_CUDA(cudaMemsetAsync(status, 0, sizeof(int), st));
+  dim3 grid((unsigned)std::min<int64_t>(gq::ceil_div(d, 256), 64), (unsigned)d);
+  gq::damp_permute_kernel<<<grid, 256, 0, st>>>(h, d, ldh, perm, mean, (float)damp, ht, hd_out);
+  GQ_TRY(gq::check_launch("damp_permute"));
+  gq::zero_upper_kernel<<<grid, 256, 0, st>>>(ht, d, d);
+  GQ_TRY(gq::check_launch("zero_upper"));
+  // L^-1 in place, then U = J L^-1 J
+  GQ_TRY(gq::inv_chol_rec(ht, d, d, scratch, status, st));
+  gq::reverse_copy_kernel<<<grid, 256, 0, st>>>(ht, d, d, u, ldu);
+  return gq::check_launch("reverse_copy");
+}
+
 int gq_hessian_factor(const float* h, int64_t d, int64_t ldh, const int32_t* perm,
                       double damp_percent, float* u, int64_t ldu, float* hd_out, void* workspace,
                       int64_t workspace_bytes, int* attempt_out, void* stream) {
@@ -386,33 +420,16 @@ int gq_hessian_factor(const float* h, int64_t d, int64_t ldh, const int32_t* per
   GQ_REQUIRE(damp_percent >= 0.0, "gq_hessian_factor: negative damp_percent");
   cudaStream_t st = gq::as_stream(stream);
   float* ws = reinterpret_cast<float*>(workspace);
-  float* ht = ws;                                  // d*d
-  float* scratch = ht + d * d;                     // (d/2+NB) x (d+NB)
   int64_t half = d / 2 + gq::NB;
-  float* mean = scratch + half * (d + gq::NB);     // 1 float
+  float* mean = ws + d * d + half * (d + gq::NB);  // 1 float
   int* status = reinterpret_cast<int*>(mean + 16);  // 1 int
-
-  GQ_TRY(gq::diag_kernel_setup());
-  gq::diag_mean_kernel<<<1, 1024, 0, st>>>(h, d, ldh, mean);
-  GQ_TRY(gq::check_launch("diag_mean"));
   for (int attempt = 0; attempt < 5; ++attempt) {
-    double damp = std::pow(10.0, attempt) * damp_percent;
-    GQ_CHECK_CUDA(cudaMemsetAsync(status, 0, sizeof(int), st));
-    dim3 grid((unsigned)std::min<int64_t>(gq::ceil_div(d, 256), 64), (unsigned)d);
-    gq::damp_permute_kernel<<<grid, 256, 0, st>>>(h, d, ldh, perm, mean, (float)damp, ht, hd_out);
-    GQ_TRY(gq::check_launch("damp_permute"));
-    dim3 gz((unsigned)std::min<int64_t>(gq::ceil_div(d, 256), 64), (unsigned)d);
-    gq::zero_upper_kernel<<<gz, 256, 0, st>>>(ht, d, d);
-    GQ_TRY(gq::check_launch("zero_upper"));
-    // L^-1 in place, then U = J L^-1 J
-    GQ_TRY(gq::inv_chol_rec(ht, d, d, scratch, status, st));
+    GQ_TRY(gq_hessian_factor_attempt(h, d, ldh, perm, damp_percent, attempt, u, ldu, hd_out,
+                                     workspace, workspace_bytes, status, stream));
     int host_status = 0;
     GQ_CHECK_CUDA(cudaMemcpyAsync(&host_status, status, sizeof(int), cudaMemcpyDeviceToHost, st));
     GQ_CHECK_CUDA(cudaStreamSynchronize(st));
     if (host_status != gq::GQ_DEVERR_NONE) continue;
-    dim3 g2((unsigned)std::min<int64_t>(gq::ceil_div(d, 256), 64), (unsigned)d);
-    gq::reverse_copy_kernel<<<g2, 256, 0, st>>>(ht, d, d, u, ldu);
-    GQ_TRY(gq::check_launch("reverse_copy"));
     if (attempt_out) *attempt_out = attempt;
     return GQ_OK;
   }

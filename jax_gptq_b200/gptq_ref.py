@@ -107,6 +107,27 @@ def factor_hessian(h, cfg: QuantConfig, want_hd: bool = False) -> HessianFactor:
     return HessianFactor(u, perm, attempt.value, hd)
 
 
+def factor_hessian_attempt0(h_dev: torch.Tensor, cfg: QuantConfig, want_hd: bool = False):
+    """The first damping attempt of :func:`factor_hessian`, enqueued on the
+    current stream with no host synchronization (``gq_hessian_factor_attempt``).
+
+    Returns ``(factor, status)``: ``status`` is a 1-element int32 device tensor,
+    0 when the factor is valid.  A caller that sees a non-zero status redoes
+    the group with :func:`factor_hessian` (the later attempts and the identity
+    fallback)."""
+    _check_hessian(h_dev, cfg)
+    d = h_dev.shape[0]
+    perm = act_order_perm(h_dev, cfg.ordering_mode)
+    u = A.empty((d, d))
+    hd = A.empty((d, d)) if want_hd else None
+    ws = A.workspace(_lib.lib().gq_hessian_factor_workspace_size(d))
+    status = torch.zeros((1,), dtype=torch.int32, device="cuda")
+    _lib.call("gq_hessian_factor_attempt", A.ptr(h_dev), d, d, A.ptr(perm),
+              float(cfg.damp_percent), 0, A.ptr(u), d, A.ptr(hd), A.ptr(ws), ws.numel(),
+              A.ptr(status), A.stream())
+    return HessianFactor(u, perm, 0, hd), status
+
+
 def process_hessian(h, cfg: QuantConfig, panel_size: int = 32):
     """gptq_ref.py:44 -- returns ``(h_inv_sqrt, perm)``."""
     del panel_size  # only the eigh branches use it (gptq_ref.py:120-131)

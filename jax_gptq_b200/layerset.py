@@ -23,7 +23,8 @@ import torch
 
 from . import stats
 from .config import QuantConfig
-from .gptq_ref import HessianFactor, SweepResult, factor_hessian, gptq_sweep
+from .gptq_ref import (HessianFactor, SweepResult, factor_hessian, factor_hessian_attempt0,
+                       gptq_sweep)
 from .qronos_ref import qronos_quantize
 
 # (name, out_features, in_features, input group)
@@ -151,14 +152,88 @@ def _split_rows(res: SweepResult, members) -> dict:
     return out
 
 
+_SIDE_STREAMS: dict[int, list] = {}
+
+
+def _side_streams(n: int) -> list:
+    """A per-device pool of side streams, one per input group run concurrently."""
+    dev = torch.cuda.current_device()
+    pool = _SIDE_STREAMS.setdefault(dev, [])
+    while len(pool) < n:
+        pool.append(torch.cuda.Stream(device=dev))
+    return pool[:n]
+
+
+def _stack(weights: dict, members) -> torch.Tensor:
+    return weights[members[0][0]] if len(members) == 1 else \
+        torch.cat([weights[name] for name, _ in members], dim=0)
+
+
+def _run_groups_concurrently(hs: dict, work, redo) -> dict:
+    """Per input group, ``work(grp, h) -> (status, result)`` on its own side
+    stream once every H is formed on the current stream; the current stream
+    then waits for all of them.  ``status`` is the device word of the group's
+    first damping attempt; the statuses are read once, and a group whose
+    damped Hessian was not positive definite is recomputed by ``redo(grp, h)``
+    (the retrying, synchronizing path), so the outcome equals the sequential
+    one.  Result tensors are marked as used by the current stream."""
+    main = torch.cuda.current_stream()
+    streams = _side_streams(len(hs))
+    pending = {}
+    for (grp, h), s in zip(hs.items(), streams):
+        s.wait_stream(main)
+        with torch.cuda.stream(s):
+            pending[grp] = work(grp, h)
+    for s in streams:
+        main.wait_stream(s)
+    for status, res in pending.values():
+        status.record_stream(main)
+        for t in (res.dequant, res.codes, res.scales, res.zeros, res.g_idx, res.perm):
+            t.record_stream(main)
+    bad = torch.cat([st for st, _ in pending.values()]).cpu().tolist()
+    out = {}
+    for (grp, (_, res)), b in zip(pending.items(), bad):
+        out[grp] = redo(grp, hs[grp]) if b else res
+    return out
+
+
 def quantize_layer_gptq(weights: dict, inputs: dict, cfg: QuantConfig, shapes=LLAMA2_7B,
-                        timed: bool = False):
+                        timed: bool = False, concurrent: bool = True):
     """GPTQ for every linear of a layer set.  ``inputs[group]`` = bf16 X on the device.
 
     Linears that share an input also share the Hessian factor, and their rows
     are independent, so they are swept together as one row-stacked matrix
     (more rows in flight per column step).
+
+    With ``concurrent`` (ignored when ``timed``, whose per-phase events need
+    one stream) each input group's factor and sweep run on a stream of their
+    own once every H is formed: one group's latency-bound factor leaves and
+    small GEMMs overlap the other groups' GEMMs and sweeps.
     """
+    if timed or not concurrent:
+        return _quantize_layer_gptq_sequential(weights, inputs, cfg, shapes, timed)
+    hs = {}
+    for grp, x in inputs.items():
+        d = x.shape[1]
+        h = torch.empty((d, d), dtype=torch.float32, device=x.device)
+        stats.syrk_into(h, x, accumulate=False)
+        hs[grp] = h
+
+    def work(grp, h):
+        f, status = factor_hessian_attempt0(h, cfg)
+        return status, gptq_sweep(_stack(weights, _members(shapes, grp)), f.u, f.perm, cfg)
+
+    def redo(grp, h):
+        f = factor_hessian(h, cfg)
+        return gptq_sweep(_stack(weights, _members(shapes, grp)), f.u, f.perm, cfg)
+
+    results: dict[str, SweepResult] = {}
+    for grp, res in _run_groups_concurrently(hs, work, redo).items():
+        results.update(_split_rows(res, _members(shapes, grp)))
+    return results, LayerTimes()
+
+
+def _quantize_layer_gptq_sequential(weights, inputs, cfg, shapes, timed):
     tm = _Timer(timed)
     factors: dict[str, HessianFactor] = {}
     for grp, x in inputs.items():
@@ -174,17 +249,46 @@ def quantize_layer_gptq(weights: dict, inputs: dict, cfg: QuantConfig, shapes=LL
         members = _members(shapes, grp)
         tm.mark(f"sweep:{grp}")
         f = factors[grp]
-        w = weights[members[0][0]] if len(members) == 1 else \
-            torch.cat([weights[name] for name, _ in members], dim=0)
-        results.update(_split_rows(gptq_sweep(w, f.u, f.perm, cfg), members))
+        results.update(_split_rows(gptq_sweep(_stack(weights, members), f.u, f.perm, cfg), members))
     tm.mark("end")
     return results, _collect(tm)
 
 
 def quantize_layer_qronos(weights: dict, inputs_float: dict, inputs_quant: dict,
-                          cfg: QuantConfig, shapes=LLAMA2_7B, timed: bool = False):
+                          cfg: QuantConfig, shapes=LLAMA2_7B, timed: bool = False,
+                          concurrent: bool = True):
     """Qronos for every linear: ``h = Xt^T Xt``, ``g = X^T Xt`` per input group;
-    linears sharing an input are updated together as one row-stacked matrix."""
+    linears sharing an input are updated together as one row-stacked matrix.
+    ``concurrent`` as for :func:`quantize_layer_gptq`."""
+    if timed or not concurrent:
+        return _quantize_layer_qronos_sequential(weights, inputs_float, inputs_quant, cfg, shapes,
+                                                 timed)
+    hs, gs = {}, {}
+    for grp, xq in inputs_quant.items():
+        d = xq.shape[1]
+        h = torch.empty((d, d), dtype=torch.float32, device=xq.device)
+        g = torch.empty((d, d), dtype=torch.float32, device=xq.device)
+        stats.syrk_into(h, xq, accumulate=False)
+        stats.gemm_tn_into(g, inputs_float[grp], xq, accumulate=False)
+        hs[grp], gs[grp] = h, g
+
+    def work(grp, h):
+        f, status = factor_hessian_attempt0(h, cfg, want_hd=True)
+        w = _stack(weights, _members(shapes, grp))
+        return status, qronos_quantize(w, w, None, gs[grp], cfg, factor=f)
+
+    def redo(grp, h):
+        f = factor_hessian(h, cfg, want_hd=True)
+        w = _stack(weights, _members(shapes, grp))
+        return qronos_quantize(w, w, None, gs[grp], cfg, factor=f)
+
+    results = {}
+    for grp, res in _run_groups_concurrently(hs, work, redo).items():
+        results.update(_split_rows(res, _members(shapes, grp)))
+    return results, LayerTimes()
+
+
+def _quantize_layer_qronos_sequential(weights, inputs_float, inputs_quant, cfg, shapes, timed):
     tm = _Timer(timed)
     facts = {}
     for grp, xq in inputs_quant.items():
@@ -202,8 +306,7 @@ def quantize_layer_qronos(weights: dict, inputs_float: dict, inputs_quant: dict,
         members = _members(shapes, grp)
         tm.mark(f"sweep:{grp}")
         f, g = facts[grp]
-        w = weights[members[0][0]] if len(members) == 1 else \
-            torch.cat([weights[name] for name, _ in members], dim=0)
+        w = _stack(weights, members)
         results.update(_split_rows(qronos_quantize(w, w, None, g, cfg, factor=f), members))
     tm.mark("end")
     return results, _collect(tm)

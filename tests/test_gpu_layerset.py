@@ -1,0 +1,81 @@
+"""Layer-set drivers on the GPU: the concurrent per-group schedule (each input
+group's factor + sweep on its own stream, first damping attempt without a host
+synchronization) must give exactly the sequential result, and a group whose
+first attempt fails must be redone through the retrying path."""
+
+import numpy as np
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+
+from jax_gptq_b200 import layerset as LS
+from jax_gptq_b200.config import QuantConfig
+from jax_gptq_b200.gptq_ref import factor_hessian, factor_hessian_attempt0, gptq_sweep
+
+SHAPES = [("q", 256, 512, "a"), ("k", 64, 512, "a"), ("o", 200, 384, "b"), ("d", 96, 640, "c")]
+
+
+def _setup(seed=0, tokens=2048):
+    weights = LS.synth_weights(SHAPES, 0.02, seed)
+    dims = LS.group_dims(SHAPES)
+    inputs = {g: LS.synth_activations(tokens, d, seed + 10 + i)[0] for i, (g, d) in enumerate(dims.items())}
+    return weights, inputs
+
+
+def _assert_same(a, b):
+    for name, _m, _n, _g in SHAPES:
+        for field in ("dequant", "codes", "scales", "zeros", "g_idx", "perm"):
+            assert getattr(a[name], field).equal(getattr(b[name], field)), (name, field)
+
+
+def test_concurrent_gptq_equals_sequential():
+    weights, inputs = _setup()
+    cfg = QuantConfig(w_bits=4, group_size=128, ordering_mode="diag_h", semantics="intended")
+    seq, _ = LS.quantize_layer_gptq(weights, inputs, cfg, SHAPES, concurrent=False)
+    for _ in range(2):
+        con, _ = LS.quantize_layer_gptq(weights, inputs, cfg, SHAPES)
+        torch.cuda.synchronize()
+        _assert_same(con, seq)
+
+
+def test_concurrent_qronos_equals_sequential():
+    weights, inputs = _setup(1)
+    xq = {g: LS.perturb_activations(x, LS.synth_activations(8, x.shape[1], 99)[1], 0.05, 5 + i)
+          for i, (g, x) in enumerate(inputs.items())}
+    cfg = QuantConfig(w_bits=3, group_size=128, ordering_mode="diag_h", semantics="intended")
+    seq, _ = LS.quantize_layer_qronos(weights, inputs, xq, cfg, SHAPES, concurrent=False)
+    con, _ = LS.quantize_layer_qronos(weights, inputs, xq, cfg, SHAPES)
+    torch.cuda.synchronize()
+    _assert_same(con, seq)
+
+
+def test_failed_first_attempt_is_redone():
+    n = 256
+    h = np.eye(n, dtype=np.float32)
+    h[5, 5] = -0.5  # 1% damping cannot fix this direction, 100x can
+    h = torch.from_numpy(h).cuda()
+    cfg = QuantConfig(semantics="intended", damp_percent=0.01)
+    _, status = factor_hessian_attempt0(h, cfg)
+    assert status.item() != 0
+    w = torch.randn((64, n), device="cuda") * 0.02
+    calls = []
+
+    def work(grp, hh):
+        f, st = factor_hessian_attempt0(hh, cfg)
+        return st, gptq_sweep(w, f.u, f.perm, cfg)
+
+    def redo(grp, hh):
+        calls.append(grp)
+        f = factor_hessian(hh, cfg)
+        return gptq_sweep(w, f.u, f.perm, cfg)
+
+    good = torch.eye(n, device="cuda")
+    out = LS._run_groups_concurrently({"bad": h, "good": good}, work, redo)
+    assert calls == ["bad"]
+    f = factor_hessian(h, cfg)
+    assert f.attempt >= 1
+    ref = gptq_sweep(w, f.u, f.perm, cfg)
+    assert out["bad"].dequant.equal(ref.dequant)
+    fg = factor_hessian(good, cfg)
+    assert out["good"].dequant.equal(gptq_sweep(w, fg.u, fg.perm, cfg).dequant)
