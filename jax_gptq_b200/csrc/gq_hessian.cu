@@ -136,16 +136,18 @@ __global__ void damp_permute_kernel(const float* __restrict__ h, int64_t n, int6
 constexpr int NB = 128;
 constexpr int SUB = 32;
 constexpr int DIAG_THREADS = 512;
+constexpr int DIAG_WARPS = DIAG_THREADS / 32;
 constexpr int DP = NB + 1;  // shared-memory pitch: row-strided lane reads hit distinct banks
 constexpr size_t DIAG_SMEM = (size_t)(2 * NB + SUB) * DP * sizeof(float) + SUB * sizeof(float);
 
-// acc[q][s] = sum_{k < K} A[(w + 16q) DP + k] * B(k, lane + 32s) for q < nq, s < ns, where
-// w is the warp, B(k, c) = B[c DP + k] (NT) or B[k DP + c] (NN).  Row reads are warp
-// broadcasts; column reads are lane-contiguous (NN) or lane-strided by the odd pitch (NT).
+// acc[q][s] = sum_{k < K} A[r_q DP + k] * B(k, lane + 32s) for rows r_q = r0 + rstride * q
+// below M and s < ns, where B(k, c) = B[c DP + k] (NT) or B[k DP + c] (NN).  Row reads
+// are warp broadcasts; column reads are lane-contiguous (NN) or lane-strided by the odd
+// pitch (NT).  Sums run over k in increasing order.
 template <bool NT>
-__device__ __forceinline__ void smem_mm(const float* A, const float* B, int nq, int ns, int K,
-                                        float (&acc)[6][3]) {
-  const int w = threadIdx.x >> 5, lane = threadIdx.x & 31;
+__device__ __forceinline__ void smem_mm(const float* A, const float* B, int M, int ns, int K,
+                                        float (&acc)[6][3], int r0, int rstride) {
+  const int lane = threadIdx.x & 31;
 #pragma unroll
   for (int q = 0; q < 6; ++q)
 #pragma unroll
@@ -160,8 +162,9 @@ __device__ __forceinline__ void smem_mm(const float* A, const float* B, int nq, 
     }
 #pragma unroll
     for (int q = 0; q < 6; ++q) {
-      if (q < nq) {
-        const float av = A[(w + 16 * q) * DP + k];
+      const int r = r0 + rstride * q;
+      if (r < M) {
+        const float av = A[r * DP + k];
 #pragma unroll
         for (int s = 0; s < 3; ++s) acc[q][s] = fmaf(av, b[s], acc[q][s]);
       }
@@ -201,14 +204,19 @@ __device__ bool sub_factor(float* S, float* X, float* rdiag, int c0) {
   for (int k = 0; k < SUB; ++k) S[(c0 + lane) * DP + c0 + k] = r[k];
   rdiag[lane] = my_rinv;
   __syncwarp();
-  // column `lane` of L^-1 by forward substitution (L rows read as broadcasts)
+  // column `lane` of L^-1 by right-looking forward substitution: once x[k]
+  // is final it is removed from every later row (L columns read as
+  // broadcasts).  Each x[i] receives the same fmaf sequence as a dot product
+  // over k < i would, but the dependent chain is one fmaf + one multiply per
+  // column instead of the whole dot product.
   float x[SUB];
 #pragma unroll
-  for (int i = 0; i < SUB; ++i) {
-    float s = (i == lane) ? 1.f : 0.f;
+  for (int i = 0; i < SUB; ++i) x[i] = (i == lane) ? 1.f : 0.f;
 #pragma unroll
-    for (int k = 0; k < i; ++k) s = fmaf(-S[(c0 + i) * DP + c0 + k], x[k], s);
-    x[i] = s * rdiag[i];
+  for (int k = 0; k < SUB; ++k) {
+    x[k] = x[k] * rdiag[k];
+#pragma unroll
+    for (int i = k + 1; i < SUB; ++i) x[i] = fmaf(-S[(c0 + i) * DP + c0 + k], x[k], x[i]);
   }
 #pragma unroll
   for (int i = 0; i < SUB; ++i) X[(c0 + i) * DP + c0 + lane] = x[i];
@@ -227,11 +235,39 @@ potrf_diag_kernel(float* __restrict__ a, int64_t lda, int kb, int* __restrict__ 
   __shared__ int bad;
   const int w = threadIdx.x >> 5, lane = threadIdx.x & 31;
   if (threadIdx.x == 0) bad = 0;
-  for (int e = threadIdx.x; e < NB * NB; e += DIAG_THREADS) {
-    const int r = e / NB, c = e % NB;
-    S[r * DP + c] = (r < kb && c < kb) ? ((c <= r) ? a[r * lda + c] : 0.f) : ((r == c) ? 1.f : 0.f);
-    X[r * DP + c] = 0.f;
+  // block -> shared memory with every global load of a thread in flight at once
+  constexpr int PER_THREAD = NB * NB / DIAG_THREADS;  // 32
+  if (kb == NB && (lda & 3) == 0 && (reinterpret_cast<uintptr_t>(a) & 15) == 0) {
+    float4 v[PER_THREAD / 4];
+#pragma unroll
+    for (int it = 0; it < PER_THREAD / 4; ++it) {
+      const int e4 = threadIdx.x + it * DIAG_THREADS;  // float4 index, 32 per row
+      v[it] = *reinterpret_cast<const float4*>(a + (int64_t)(e4 >> 5) * lda + ((e4 & 31) << 2));
+    }
+#pragma unroll
+    for (int it = 0; it < PER_THREAD / 4; ++it) {
+      const int e4 = threadIdx.x + it * DIAG_THREADS;
+      const int r = e4 >> 5, c = (e4 & 31) << 2;
+      S[r * DP + c + 0] = (c + 0 <= r) ? v[it].x : 0.f;
+      S[r * DP + c + 1] = (c + 1 <= r) ? v[it].y : 0.f;
+      S[r * DP + c + 2] = (c + 2 <= r) ? v[it].z : 0.f;
+      S[r * DP + c + 3] = (c + 3 <= r) ? v[it].w : 0.f;
+    }
+  } else {
+    float v[PER_THREAD];
+#pragma unroll
+    for (int it = 0; it < PER_THREAD; ++it) {
+      const int e = threadIdx.x + it * DIAG_THREADS, r = e / NB, c = e % NB;
+      v[it] = (r < kb && c <= r) ? a[r * lda + c] : 0.f;
+    }
+#pragma unroll
+    for (int it = 0; it < PER_THREAD; ++it) {
+      const int e = threadIdx.x + it * DIAG_THREADS, r = e / NB, c = e % NB;
+      S[r * DP + c] = (r < kb && c < kb) ? v[it] : ((r == c) ? 1.f : 0.f);
+    }
   }
+#pragma unroll 8
+  for (int e = threadIdx.x; e < NB * NB; e += DIAG_THREADS) X[(e / NB) * DP + e % NB] = 0.f;
   __syncthreads();
   float acc[6][3];
   for (int c0 = 0; c0 < NB; c0 += SUB) {
@@ -243,39 +279,39 @@ potrf_diag_kernel(float* __restrict__ a, int64_t lda, int kb, int* __restrict__ 
     if (m == 0) break;
     float* panel = S + (c0 + SUB) * DP + c0;
     // L21 = A21 X11^T
-    smem_mm<true>(panel, X + c0 * DP + c0, m / 16, 1, SUB, acc);
+    smem_mm<true>(panel, X + c0 * DP + c0, m, 1, SUB, acc, w, DIAG_WARPS);
     __syncthreads();
 #pragma unroll
     for (int q = 0; q < 6; ++q)
-      if (q < m / 16) panel[(w + 16 * q) * DP + lane] = acc[q][0];
+      if (w + DIAG_WARPS * q < m) panel[(w + DIAG_WARPS * q) * DP + lane] = acc[q][0];
     __syncthreads();
     // A22 -= L21 L21^T (lower part)
-    smem_mm<true>(panel, panel, m / 16, m / 32, SUB, acc);
+    smem_mm<true>(panel, panel, m, m / 32, SUB, acc, w, DIAG_WARPS);
     float* a22 = panel + SUB;
 #pragma unroll
     for (int q = 0; q < 6; ++q)
 #pragma unroll
       for (int s = 0; s < 3; ++s) {
-        const int r = w + 16 * q, c = lane + 32 * s;
-        if (q < m / 16 && s < m / 32 && c <= r) a22[r * DP + c] -= acc[q][s];
+        const int r = w + DIAG_WARPS * q, c = lane + 32 * s;
+        if (r < m && s < m / 32 && c <= r) a22[r * DP + c] -= acc[q][s];
       }
     __syncthreads();
   }
   // off-diagonal blocks of L^-1, block row by block row
   for (int i = 1; i < NB / SUB; ++i) {
-    smem_mm<false>(S + SUB * i * DP, X, 2, i, SUB * i, acc);  // W = L[i, :i] X[:i, :i]
+    smem_mm<false>(S + SUB * i * DP, X, SUB, i, SUB * i, acc, w, DIAG_WARPS);  // W = L[i, :i] X[:i, :i]
 #pragma unroll
     for (int q = 0; q < 2; ++q)
 #pragma unroll
       for (int s = 0; s < 3; ++s)
-        if (s < i) W[(w + 16 * q) * DP + lane + 32 * s] = acc[q][s];
+        if (s < i) W[(w + DIAG_WARPS * q) * DP + lane + 32 * s] = acc[q][s];
     __syncthreads();
-    smem_mm<false>(X + SUB * i * DP + SUB * i, W, 2, i, SUB, acc);  // X[i, :i] = -X_ii W
+    smem_mm<false>(X + SUB * i * DP + SUB * i, W, SUB, i, SUB, acc, w, DIAG_WARPS);  // -X_ii W
 #pragma unroll
     for (int q = 0; q < 2; ++q)
 #pragma unroll
       for (int s = 0; s < 3; ++s)
-        if (s < i) X[(SUB * i + w + 16 * q) * DP + lane + 32 * s] = -acc[q][s];
+        if (s < i) X[(SUB * i + w + DIAG_WARPS * q) * DP + lane + 32 * s] = -acc[q][s];
     __syncthreads();
   }
   for (int e = threadIdx.x; e < NB * NB; e += DIAG_THREADS) {
