@@ -28,7 +28,8 @@ typedef enum {
   GQ_ENOTPD = 2,        /* damped Hessian not positive definite after all retries */
   GQ_ETIMEOUT = 3,      /* a bounded device-side wait expired */
   GQ_ECUDA = 4,         /* CUDA runtime error */
-  GQ_EUNSUPPORTED = 5   /* valid input outside what this build supports */
+  GQ_EUNSUPPORTED = 5,  /* valid input outside what this build supports */
+  GQ_ENCCL = 6          /* NCCL missing or an NCCL call failed */
 } gq_status;
 
 /* Library version (major*10000 + minor*100 + patch). */
@@ -255,6 +256,34 @@ int gq_qr_factor_panel(float* a, int64_t m, int64_t n, int64_t lda, int32_t* per
 int gq_qr_apply_panel(float* b, int64_t rows, int64_t cols, int64_t ldb, const float* y,
                       int64_t ldy, const float* t, int64_t ldt, int width, float* scratch,
                       void* stream);
+
+/* ------------------------------------------------------------------------
+ * Multi-GPU: a per-device handle with an optional NCCL communicator and the
+ * in-place fp32 sum all-reduce used for token-sharded Hessians (H = sum over
+ * ranks of X_r^T X_r).  The reference is single-device and has no
+ * counterpart; these are the C-ABI form of jax_gptq_b200/distributed.py.
+ * NCCL is loaded with dlopen on first use (a copy already loaded in the
+ * process is reused); without it these calls return GQ_ENCCL.
+ *
+ * gq_nccl_unique_id     writes a 128-byte NCCL id (rank 0; share it with the
+ *                       other ranks out of band).
+ * gq_handle_create      wraps a caller-owned ncclComm_t (or NULL: a handle
+ *                       without collectives); the comm is not destroyed.
+ * gq_handle_create_nccl creates and owns a communicator: collective over
+ *                       the nranks callers, one per GPU, same id.
+ * gq_allreduce_sum_f32  buf[0:count] summed over the ranks, in place,
+ *                       stream-ordered on `stream` (device of the handle).
+ *                       A rank that never joins leaves the others waiting
+ *                       inside NCCL; hosts that need a bound use NCCL's own
+ *                       timeout settings. */
+typedef struct gq_handle gq_handle;
+int gq_nccl_unique_id(void* id_out, int64_t id_bytes);
+int gq_handle_create(int device, void* nccl_comm, gq_handle** out);
+int gq_handle_create_nccl(int device, const void* unique_id, int nranks, int rank,
+                          gq_handle** out);
+int gq_handle_destroy(gq_handle* h);
+int gq_handle_ranks(const gq_handle* h, int* nranks, int* rank);
+int gq_allreduce_sum_f32(gq_handle* h, float* buf, int64_t count, void* stream);
 
 #ifdef __cplusplus
 }

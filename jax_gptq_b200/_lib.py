@@ -20,6 +20,7 @@ GQ_ENOTPD = 2
 GQ_ETIMEOUT = 3
 GQ_ECUDA = 4
 GQ_EUNSUPPORTED = 5
+GQ_ENCCL = 6
 
 _P = c_void_p
 # name -> (restype, argtypes)
@@ -27,6 +28,12 @@ SIGNATURES = {
     "gq_version": (c_int, []),
     "gq_last_error": (ctypes.c_char_p, []),
     "gq_launch_count": (ctypes.c_longlong, []),
+    "gq_nccl_unique_id": (c_int, [_P, c_int64]),
+    "gq_handle_create": (c_int, [c_int, _P, ctypes.POINTER(_P)]),
+    "gq_handle_create_nccl": (c_int, [c_int, _P, c_int, c_int, ctypes.POINTER(_P)]),
+    "gq_handle_destroy": (c_int, [_P]),
+    "gq_handle_ranks": (c_int, [_P, ctypes.POINTER(c_int), ctypes.POINTER(c_int)]),
+    "gq_allreduce_sum_f32": (c_int, [_P, _P, c_int64, _P]),
     "gq_rtn": (c_int, [_P, c_int64, c_int64, c_int64, _P, c_int, c_int, c_int, _P, _P, _P, _P, _P]),
     "gq_sgemm": (c_int, [c_int, c_int, c_int64, c_int64, c_int64, c_float, _P, c_int64, _P, c_int64,
                          c_float, _P, c_int64, c_int, _P]),

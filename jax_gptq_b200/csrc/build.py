@@ -75,7 +75,7 @@ def build(force: bool = False, jobs: int = 8, verbose: bool = False) -> str:
                 print(out)
     if todo or force or not os.path.exists(LIB) or any(
             os.path.getmtime(o) > os.path.getmtime(LIB) for o in objs):
-        cmd = [nvcc, *ARCH, "-shared", "-o", LIB, *objs]
+        cmd = [nvcc, *ARCH, "-shared", "-o", LIB, *objs, "-ldl"]
         res = subprocess.run(cmd, capture_output=True, text=True)
         if res.returncode != 0:
             raise RuntimeError(f"link failed:\n{res.stderr}")

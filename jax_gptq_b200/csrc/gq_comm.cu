@@ -1,0 +1,161 @@
+// Per-device handle with an optional NCCL communicator, and the in-place fp32
+// all-reduce that sums token-sharded Hessians across GPUs.  The reference has
+// no multi-device path; these are the C-ABI counterparts of what
+// jax_gptq_b200/distributed.py does through torch.distributed.
+//
+// NCCL is opened with dlopen on first use (an already-loaded copy in the
+// process is reused, e.g. the one a framework brought), so the library itself
+// does not depend on libnccl and loads on hosts without it.
+#include <dlfcn.h>
+#include <nccl.h>
+
+#include <cstring>
+#include <mutex>
+
+#include "gq_common.cuh"
+
+struct gq_handle {
+  int device;
+  ncclComm_t comm;  // NULL: no collectives
+  int owns_comm;
+  int nranks;
+  int rank;
+};
+
+namespace gq {
+namespace comm {
+
+struct Api {
+  ncclResult_t (*get_unique_id)(ncclUniqueId*) = nullptr;
+  ncclResult_t (*comm_init_rank)(ncclComm_t*, int, ncclUniqueId, int) = nullptr;
+  ncclResult_t (*comm_destroy)(ncclComm_t) = nullptr;
+  ncclResult_t (*comm_count)(const ncclComm_t, int*) = nullptr;
+  ncclResult_t (*comm_user_rank)(const ncclComm_t, int*) = nullptr;
+  ncclResult_t (*all_reduce)(const void*, void*, size_t, ncclDataType_t, ncclRedOp_t, ncclComm_t,
+                             cudaStream_t) = nullptr;
+  const char* (*error_string)(ncclResult_t) = nullptr;
+  bool ok = false;
+};
+
+static const Api& api() {
+  static Api a;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* h = dlopen("libnccl.so.2", RTLD_NOW | RTLD_NOLOAD);
+    if (!h) h = dlopen("libnccl.so.2", RTLD_NOW | RTLD_LOCAL);
+    if (!h) h = dlopen("libnccl.so", RTLD_NOW | RTLD_LOCAL);
+    if (!h) return;
+    a.get_unique_id = reinterpret_cast<decltype(a.get_unique_id)>(dlsym(h, "ncclGetUniqueId"));
+    a.comm_init_rank = reinterpret_cast<decltype(a.comm_init_rank)>(dlsym(h, "ncclCommInitRank"));
+    a.comm_destroy = reinterpret_cast<decltype(a.comm_destroy)>(dlsym(h, "ncclCommDestroy"));
+    a.comm_count = reinterpret_cast<decltype(a.comm_count)>(dlsym(h, "ncclCommCount"));
+    a.comm_user_rank = reinterpret_cast<decltype(a.comm_user_rank)>(dlsym(h, "ncclCommUserRank"));
+    a.all_reduce = reinterpret_cast<decltype(a.all_reduce)>(dlsym(h, "ncclAllReduce"));
+    a.error_string = reinterpret_cast<decltype(a.error_string)>(dlsym(h, "ncclGetErrorString"));
+    a.ok = a.get_unique_id && a.comm_init_rank && a.comm_destroy && a.comm_count &&
+           a.comm_user_rank && a.all_reduce && a.error_string;
+  });
+  return a;
+}
+
+static int nccl_fail(const char* what, ncclResult_t r) {
+  return fail(GQ_ENCCL, "%s: %s", what, api().error_string ? api().error_string(r) : "NCCL error");
+}
+
+// Makes `device` current for the scope and restores the previous device.
+struct DeviceScope {
+  int prev = -1;
+  cudaError_t err = cudaSuccess;
+  explicit DeviceScope(int device) {
+    err = cudaGetDevice(&prev);
+    if (err == cudaSuccess && prev != device) err = cudaSetDevice(device);
+  }
+  ~DeviceScope() {
+    int cur = -1;
+    if (prev >= 0 && cudaGetDevice(&cur) == cudaSuccess && cur != prev) cudaSetDevice(prev);
+  }
+};
+
+}  // namespace comm
+}  // namespace gq
+
+extern "C" {
+
+int gq_nccl_unique_id(void* id_out, int64_t id_bytes) {
+  GQ_REQUIRE(id_out != nullptr && id_bytes >= (int64_t)sizeof(ncclUniqueId),
+             "gq_nccl_unique_id: need a buffer of at least %d bytes", (int)sizeof(ncclUniqueId));
+  const auto& a = gq::comm::api();
+  if (!a.ok) return gq::fail(GQ_ENCCL, "gq_nccl_unique_id: libnccl.so.2 could not be loaded");
+  ncclUniqueId id;
+  ncclResult_t r = a.get_unique_id(&id);
+  if (r != ncclSuccess) return gq::comm::nccl_fail("ncclGetUniqueId", r);
+  std::memcpy(id_out, &id, sizeof(id));
+  return GQ_OK;
+}
+
+int gq_handle_create(int device, void* nccl_comm, gq_handle** out) {
+  GQ_REQUIRE(out != nullptr, "gq_handle_create: NULL out");
+  GQ_REQUIRE(device >= 0, "gq_handle_create: bad device %d", device);
+  int nranks = 1, rank = 0;
+  if (nccl_comm) {
+    const auto& a = gq::comm::api();
+    if (!a.ok) return gq::fail(GQ_ENCCL, "gq_handle_create: libnccl.so.2 could not be loaded");
+    ncclResult_t r = a.comm_count(static_cast<ncclComm_t>(nccl_comm), &nranks);
+    if (r == ncclSuccess) r = a.comm_user_rank(static_cast<ncclComm_t>(nccl_comm), &rank);
+    if (r != ncclSuccess) return gq::comm::nccl_fail("gq_handle_create", r);
+  }
+  *out = new gq_handle{device, static_cast<ncclComm_t>(nccl_comm), 0, nranks, rank};
+  return GQ_OK;
+}
+
+int gq_handle_create_nccl(int device, const void* unique_id, int nranks, int rank,
+                          gq_handle** out) {
+  GQ_REQUIRE(out != nullptr && unique_id != nullptr, "gq_handle_create_nccl: NULL argument");
+  GQ_REQUIRE(device >= 0 && nranks >= 1 && rank >= 0 && rank < nranks,
+             "gq_handle_create_nccl: bad device %d / rank %d of %d", device, rank, nranks);
+  const auto& a = gq::comm::api();
+  if (!a.ok) return gq::fail(GQ_ENCCL, "gq_handle_create_nccl: libnccl.so.2 could not be loaded");
+  gq::comm::DeviceScope scope(device);
+  GQ_CHECK_CUDA(scope.err);
+  ncclUniqueId id;
+  std::memcpy(&id, unique_id, sizeof(id));
+  ncclComm_t comm = nullptr;
+  ncclResult_t r = a.comm_init_rank(&comm, nranks, id, rank);
+  if (r != ncclSuccess) return gq::comm::nccl_fail("ncclCommInitRank", r);
+  *out = new gq_handle{device, comm, 1, nranks, rank};
+  return GQ_OK;
+}
+
+int gq_handle_destroy(gq_handle* h) {
+  if (!h) return GQ_OK;
+  int status = GQ_OK;
+  if (h->comm && h->owns_comm) {
+    gq::comm::DeviceScope scope(h->device);
+    ncclResult_t r = gq::comm::api().comm_destroy(h->comm);
+    if (r != ncclSuccess) status = gq::comm::nccl_fail("ncclCommDestroy", r);
+  }
+  delete h;
+  return status;
+}
+
+int gq_handle_ranks(const gq_handle* h, int* nranks, int* rank) {
+  GQ_REQUIRE(h != nullptr, "gq_handle_ranks: NULL handle");
+  if (nranks) *nranks = h->nranks;
+  if (rank) *rank = h->rank;
+  return GQ_OK;
+}
+
+int gq_allreduce_sum_f32(gq_handle* h, float* buf, int64_t count, void* stream) {
+  GQ_REQUIRE(h != nullptr, "gq_allreduce_sum_f32: NULL handle");
+  GQ_REQUIRE(h->comm != nullptr, "gq_allreduce_sum_f32: the handle has no communicator");
+  GQ_REQUIRE(count >= 0 && (count == 0 || buf != nullptr), "gq_allreduce_sum_f32: bad buffer");
+  if (count == 0) return GQ_OK;
+  gq::comm::DeviceScope scope(h->device);
+  GQ_CHECK_CUDA(scope.err);
+  ncclResult_t r = gq::comm::api().all_reduce(buf, buf, (size_t)count, ncclFloat32, ncclSum,
+                                              h->comm, gq::as_stream(stream));
+  if (r != ncclSuccess) return gq::comm::nccl_fail("ncclAllReduce", r);
+  return GQ_OK;
+}
+
+}  // extern "C"

@@ -222,8 +222,52 @@ def tokens_for_rank(n_tokens: int, group=None) -> tuple[int, int]:
     return shard_range(n_tokens, rank, world)
 
 
+class CommHandle:
+    """libgq's per-device handle with a library-owned NCCL communicator (the
+    C ABI ``gq_handle_create_nccl`` / ``gq_allreduce_sum_f32``), for callers
+    that sum Hessians without torch.distributed.  Rank 0 makes the id with
+    :meth:`unique_id` and shares it with the other ranks out of band; every
+    rank then constructs its handle (a collective call), one per GPU."""
+
+    def __init__(self, device: int, unique_id: bytes, nranks: int, rank: int):
+        from . import _lib
+        import ctypes
+        self._lib = _lib
+        h = ctypes.c_void_p()
+        buf = ctypes.create_string_buffer(bytes(unique_id), len(unique_id))
+        _lib.call("gq_handle_create_nccl", device, buf, nranks, rank, ctypes.byref(h))
+        self._h = h
+        self.device, self.nranks, self.rank = device, nranks, rank
+
+    @staticmethod
+    def unique_id() -> bytes:
+        from . import _lib
+        import ctypes
+        buf = ctypes.create_string_buffer(128)
+        _lib.call("gq_nccl_unique_id", buf, 128)
+        return buf.raw
+
+    def allreduce_sum_(self, t: torch.Tensor) -> None:
+        """In-place sum of a contiguous float32 tensor on this handle's GPU,
+        ordered on the current stream."""
+        if t.dtype != torch.float32 or not t.is_cuda or not t.is_contiguous():
+            raise ValueError("allreduce_sum_ needs a contiguous float32 CUDA tensor")
+        self._lib.call("gq_allreduce_sum_f32", self._h, A.ptr(t), t.numel(), A.stream())
+
+    def close(self) -> None:
+        if self._h is not None and self._h.value:
+            self._lib.call("gq_handle_destroy", self._h)
+        self._h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
 __all__ = [
     "SWEEP_ROW_ALIGN", "rank_world", "shard_range", "lpt_assign", "layer_set_cost",
     "allreduce_sum_", "gather_rows", "hessians_token_sharded", "quantize_layer_gptq_sharded",
-    "layer_sets_for_rank", "tokens_for_rank",
+    "layer_sets_for_rank", "tokens_for_rank", "CommHandle",
 ]

@@ -71,3 +71,22 @@ def test_hessian_factor_rejects_small_workspace():
     st = lib.gq_hessian_factor(ctypes.c_void_p(16), 64, 64, None, 0.01, ctypes.c_void_p(16), 64,
                                None, ctypes.c_void_p(16), 8, ctypes.byref(att), None)
     assert st == _lib.GQ_EINVAL
+
+
+def test_comm_handle_argument_errors_without_a_gpu():
+    lib = _lib.lib()
+    h = ctypes.c_void_p()
+    assert lib.gq_handle_create(0, None, ctypes.byref(h)) == _lib.GQ_OK and h.value
+    n, r = ctypes.c_int(-1), ctypes.c_int(-1)
+    assert lib.gq_handle_ranks(h, ctypes.byref(n), ctypes.byref(r)) == _lib.GQ_OK
+    assert (n.value, r.value) == (1, 0)
+    # a handle without a communicator cannot reduce
+    assert lib.gq_allreduce_sum_f32(h, ctypes.c_void_p(16), 4, None) == _lib.GQ_EINVAL
+    assert b"no communicator" in lib.gq_last_error()
+    assert lib.gq_handle_destroy(h) == _lib.GQ_OK
+    assert lib.gq_handle_create(0, None, None) == _lib.GQ_EINVAL
+    assert lib.gq_handle_create(-1, None, ctypes.byref(h)) == _lib.GQ_EINVAL
+    assert lib.gq_allreduce_sum_f32(None, None, 0, None) == _lib.GQ_EINVAL
+    small = ctypes.create_string_buffer(16)
+    assert lib.gq_nccl_unique_id(small, 16) == _lib.GQ_EINVAL
+    assert lib.gq_handle_create_nccl(0, small, 2, 2, ctypes.byref(h)) == _lib.GQ_EINVAL

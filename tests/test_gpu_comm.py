@@ -1,0 +1,71 @@
+"""NCCL all-reduce through libgq's C ABI (gq_handle_create_nccl /
+gq_allreduce_sum_f32): one rank on one GPU, and -- when the process sees two
+or more GPUs -- two ranks in spawned processes, one per GPU, summing
+token-shard partial Hessians."""
+
+import os
+import pickle
+
+import numpy as np
+import pytest
+import torch
+import torch.multiprocessing as mp
+
+pytestmark = pytest.mark.gpu
+
+from jax_gptq_b200 import distributed as D
+from jax_gptq_b200 import stats
+
+
+def test_single_rank_allreduce_is_identity():
+    uid = D.CommHandle.unique_id()
+    h = D.CommHandle(torch.cuda.current_device(), uid, 1, 0)
+    try:
+        t = torch.randn(1000, device="cuda")
+        ref = t.clone()
+        h.allreduce_sum_(t)
+        torch.cuda.synchronize()
+        assert t.equal(ref)
+        with pytest.raises(ValueError):
+            h.allreduce_sum_(t.double())
+    finally:
+        h.close()
+
+
+def _rank(rank, world, uid, out_dir):
+    torch.cuda.set_device(rank)
+    from jax_gptq_b200 import _lib
+    _lib.lib()
+    gen = torch.Generator(device="cuda").manual_seed(11)
+    x = torch.randn((4096, 384), generator=gen, device="cuda").to(torch.bfloat16)
+    t0, t1 = D.shard_range(x.shape[0], rank, world)
+    h = torch.empty((384, 384), dtype=torch.float32, device="cuda")
+    stats.syrk_into(h, x[t0:t1], accumulate=False)
+    handle = D.CommHandle(rank, uid, world, rank)
+    try:
+        handle.allreduce_sum_(h)
+        torch.cuda.synchronize()
+        full = torch.empty_like(h)
+        stats.syrk_into(full, x, accumulate=False)
+        rel = (torch.linalg.norm(h - full) / torch.linalg.norm(full)).item()
+        with open(os.path.join(out_dir, f"r{rank}.pkl"), "wb") as f:
+            pickle.dump({"rel": rel, "h": h.cpu().numpy()}, f)
+    finally:
+        handle.close()
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two GPUs")
+def test_two_gpu_hessian_allreduce(tmp_path):
+    world = 2
+    uid = D.CommHandle.unique_id()
+    ctx = mp.get_context("spawn")
+    procs = [ctx.Process(target=_rank, args=(r, world, uid, str(tmp_path))) for r in range(world)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(180)
+        assert p.exitcode == 0, p.exitcode
+    outs = [pickle.load(open(tmp_path / f"r{r}.pkl", "rb")) for r in range(world)]
+    for o in outs:
+        assert o["rel"] < 1e-6, o["rel"]
+    assert np.array_equal(outs[0]["h"], outs[1]["h"])
