@@ -47,6 +47,17 @@ TOKENS = 128 * 2048
 METRIC = "7B-layer-set GPTQ+Qronos s/layer; H-accum TFLOP/s; pivoted-QR GFLOP/s"
 WORKLOAD = "llama2-7b layer set (q,k,v,o 4096x4096; gate,up 11008x4096; down 4096x11008), " \
            "GPTQ 4-bit g128 act-order damp 0.01, H over 262144 bf16 tokens"
+WORKLOAD_70B = "llama3-70b layer set (q,o 8192x8192; k,v 1024x8192; gate,up 28672x8192; " \
+               "down 8192x28672), GPTQ 4-bit g128 act-order damp 0.01, H over 1048576 " \
+               "Student-t bf16 tokens"
+
+
+def _workload(args):
+    """(shapes, weight std, activation kind, tokens, description) of --model."""
+    from jax_gptq_b200 import layerset as LS
+    if args.model == "llama3-70b":
+        return LS.LLAMA3_70B, 0.01, "student_t", args.tokens or 256 * 4096, WORKLOAD_70B
+    return LS.LLAMA2_7B, 0.02, "lognormal", args.tokens or TOKENS, WORKLOAD
 
 
 def _peaks():
@@ -278,6 +289,7 @@ def run_kernel_only(args):
     from jax_gptq_b200 import layerset as LS
     from jax_gptq_b200 import stats
     _lib.lib()
+    args.tokens = args.tokens or TOKENS
     x, _ = LS.synth_activations(args.tokens, args.dim, 7)
     h = torch.empty((args.dim, args.dim), dtype=torch.float32, device="cuda")
     for _ in range(args.warmup):
@@ -305,15 +317,23 @@ def run_ours(args, world, rank, local):
 
     _lib.lib()
     peaks, peak_kind = _peaks()
-    shapes = LS.LLAMA2_7B
+    shapes, w_std, act_kind, args.tokens, workload = _workload(args)
+    skipped = []
+    if args.model == "llama3-70b":
+        # a second copy of the 112 GB of activations (pinned host or X~) does not fit
+        for flag, what in (("no_e2e", "e2e"), ("no_qronos", "qronos"), ("no_qr", "qr")):
+            if not getattr(args, flag):
+                setattr(args, flag, True)
+                skipped.append(what)
     dims = LS.group_dims(shapes)
     seed = 1000 * rank
     cfg = QuantConfig(w_bits=4, group_size=128, sym=False, damp_percent=0.01,
                       ordering_mode="diag_h", semantics="intended")
-    weights = LS.synth_weights(shapes, 0.02, seed)
+    weights = LS.synth_weights(shapes, w_std, seed)
     inputs, stds = {}, {}
     for i, (grp, d) in enumerate(dims.items()):
-        inputs[grp], stds[grp] = LS.synth_activations(args.tokens, d, seed + 10 + i)
+        inputs[grp], stds[grp] = LS.synth_activations(args.tokens, d, seed + 10 + i, kind=act_kind)
+    x_gb = sum(x.numel() * x.element_size() for x in inputs.values()) / 1e9
     torch.cuda.synchronize()
 
     # --- headline: device-resident GPTQ layer set
@@ -414,6 +434,12 @@ def run_ours(args, world, rank, local):
             import importlib
             BQ = importlib.import_module("jax_gptq_b200.pallas.blocked_pivoted_qr")
             qr = BQ.benchmark(n=4096, panel=64, reps=2)
+            # the BLAS-2 part reads the trailing block once per pivot step
+            blas2 = 4.0 * sum(i * i for i in range(1, qr["n"] + 1))
+            qr["blas2_bytes"] = blas2
+            for v in qr.values():
+                if isinstance(v, dict) and "ms" in v:
+                    v["blas2_gbs"] = blas2 / (v["ms"] / 1e3) / 1e9
         except Exception as exc:  # report, do not hide
             qr = {"error": repr(exc)[:200]}
 
@@ -429,12 +455,16 @@ def run_ours(args, world, rank, local):
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
             "higher_is_better": False, "scaling": "weak", "vs_baseline": None,
             "dtype": "bf16 in / f32 accumulate (H); f32 sweep", "data": "synthetic",
-            "config": {"workload": WORKLOAD, "tokens": args.tokens, "layers_per_rank": 1,
+            "config": {"workload": workload, "tokens": args.tokens, "layers_per_rank": 1,
                        "parallelism": f"layer-parallel x{world}",
-                       "l2": "inputs (12.2 GB) larger than L2; no flush"},
+                       "l2": f"inputs ({x_gb:.1f} GB) larger than L2; no flush",
+                       "skipped_for_memory": skipped},
             "phases_ms": {"h_accum": phases.stats_ms, "factor": phases.factor_ms,
                           "sweeps": phases.sweep_ms, "h_by_group": phases.per_group_stats_ms},
-            "h_accum": {"tflops": h_tflops, "ms_by_group": dict(zip(dims, syrk_ms))},
+            "h_accum": {"tflops": h_tflops, "ms_by_group": dict(zip(dims, syrk_ms)),
+                        "tflop_per_layer_distinct_inputs": sum(syrk_flop) / 1e12,
+                        "tflop_per_layer_per_linear":
+                            sum(LS.syrk_flops(args.tokens, n) for _, _, n, _ in shapes) / 1e12},
             "roofline": roofline, "e2e": e2e, "gpu_launches": int(launches), "clocks": clocks,
             "qronos": qronos, "qr": qr, "cpu_baseline": cpu,
         }
@@ -452,13 +482,13 @@ def run_sharded(args, world, rank, local):
     from jax_gptq_b200.config import QuantConfig
 
     _lib.lib()
-    shapes = LS.LLAMA2_7B
+    shapes, w_std, act_kind, args.tokens, workload = _workload(args)
     dims = LS.group_dims(shapes)
     cfg = QuantConfig(w_bits=4, group_size=128, sym=False, damp_percent=0.01,
                       ordering_mode="diag_h", semantics="intended")
-    weights = LS.synth_weights(shapes, 0.02, 0)
+    weights = LS.synth_weights(shapes, w_std, 0)
     t0, t1 = D.shard_range(args.tokens, rank, world)
-    inputs = {grp: LS.synth_activations(t1 - t0, d, 10 + i + 100 * rank)[0]
+    inputs = {grp: LS.synth_activations(t1 - t0, d, 10 + i + 100 * rank, kind=act_kind)[0]
               for i, (grp, d) in enumerate(dims.items())}
     torch.cuda.synchronize()
     for _ in range(args.warmup):
@@ -481,7 +511,7 @@ def run_sharded(args, world, rank, local):
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
             "higher_is_better": False, "scaling": "strong", "vs_baseline": None, "dtype": "f32",
             "data": "synthetic (seeded, on device)",
-            "config": {"workload": WORKLOAD, "tokens": args.tokens,
+            "config": {"workload": workload, "tokens": args.tokens,
                        "parallelism": f"token-sharded H (NCCL all-reduce) + row-sharded sweep x{world}",
                        "l2_flush": "inputs larger than L2"},
             "clocks": clocks}), flush=True)
@@ -493,7 +523,11 @@ def main():
     ap.add_argument("--steps", type=int, default=5)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--tokens", type=int, default=TOKENS)
+    ap.add_argument("--tokens", type=int, default=None,
+                    help="tokens per input (default: 262144 for llama2-7b, 1048576 for llama3-70b)")
+    ap.add_argument("--model", choices=["llama2-7b", "llama3-70b"], default="llama2-7b",
+                    help="layer set: the 7B set is the headline; the 70B block (Student-t "
+                         "activations, 112 GB of them) runs GPTQ only")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-qronos", action="store_true")
     ap.add_argument("--no-qr", action="store_true")
