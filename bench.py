@@ -308,6 +308,64 @@ def run_kernel_only(args):
                       "tflops": tf}), flush=True)
 
 
+def _time(fn, steps: int, warmup: int) -> float:
+    """Milliseconds per call of ``fn`` on the current stream (CUDA events)."""
+    import torch
+    for _ in range(warmup):
+        fn()
+    a = torch.cuda.Event(enable_timing=True)
+    b = torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize()
+    a.record()
+    for _ in range(max(steps, 1)):
+        fn()
+    b.record()
+    torch.cuda.synchronize()
+    return a.elapsed_time(b) / max(steps, 1)
+
+
+def run_component(args):
+    """``--only gemm|factor|sweep``: one component in isolation (profiling runs).
+
+    gemm:   C[m, n] += -A[m, k] B[n, k]^T on the 3xTF32 tensor-core kernel
+            (beta 1: the sweep's lazy update shape);
+    factor: damped inverse-Cholesky factor of a --dim x --dim H (from 4 * dim tokens);
+    sweep:  GPTQ sweep of an --m x --dim weight with that factor."""
+    import torch
+    from jax_gptq_b200 import _arrays as A
+    from jax_gptq_b200 import _lib
+    from jax_gptq_b200 import layerset as LS
+    from jax_gptq_b200 import stats
+    from jax_gptq_b200.config import QuantConfig
+    from jax_gptq_b200.gptq_ref import factor_hessian, gptq_sweep
+    _lib.lib()
+    out = {"kernel": args.only}
+    if args.only == "gemm":
+        m, n, k = args.m, args.n or args.dim, args.k
+        a = torch.randn(m, k, device="cuda")
+        b = torch.randn(n, k, device="cuda")
+        c = torch.randn(m, n, device="cuda")
+        ms = _time(lambda: _lib.call("gq_gemm_f32_tc", 1, m, n, k, -1.0, A.ptr(a), k, A.ptr(b), k,
+                                     1.0, A.ptr(c), n, 0, A.stream()), args.steps, args.warmup)
+        out.update(m=m, n=n, k=k, ms=ms, tflops=2.0 * m * n * k / (ms / 1e3) / 1e12,
+                   c_gbs=8.0 * m * n / (ms / 1e3) / 1e9)
+    else:
+        d = args.dim
+        x, _ = LS.synth_activations(4 * d, d, 7)
+        h = torch.empty((d, d), dtype=torch.float32, device="cuda")
+        stats.syrk_into(h, x, accumulate=False)
+        cfg = QuantConfig(w_bits=4, group_size=128, ordering_mode="diag_h", semantics="intended")
+        if args.only == "factor":
+            ms = _time(lambda: factor_hessian(h, cfg), args.steps, args.warmup)
+            out.update(d=d, ms=ms, gflops=(2.0 * d ** 3 / 3.0) / (ms / 1e3) / 1e9)
+        else:
+            f = factor_hessian(h, cfg)
+            w = torch.randn(args.m, d, device="cuda") * 0.02
+            ms = _time(lambda: gptq_sweep(w, f.u, f.perm, cfg), args.steps, args.warmup)
+            out.update(m=args.m, d=d, ms=ms)
+    print(json.dumps(out), flush=True)
+
+
 def run_ours(args, world, rank, local):
     import torch
     from jax_gptq_b200 import _lib
@@ -346,8 +404,10 @@ def run_ours(args, world, rank, local):
     e0 = torch.cuda.Event(enable_timing=True)
     e1 = torch.cuda.Event(enable_timing=True)
     e0.record()
+    torch.cuda.nvtx.range_push("gptq_layer_step")  # ncu --nvtx-include selects these launches
     for _ in range(args.steps):
         LS.quantize_layer_gptq(weights, inputs, cfg, shapes)
+    torch.cuda.nvtx.range_pop()
     e1.record()
     _barrier(world)
     launches = (_lib.lib().gq_launch_count() - launches0) // max(args.steps, 1)
@@ -534,20 +594,27 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--syrk-traffic", type=float, default=None,
                     help="DRAM bytes per H-accumulation launch from an ncu capture")
-    ap.add_argument("--only", choices=["all", "syrk", "qr"], default="all",
+    ap.add_argument("--only", choices=["all", "syrk", "qr", "gemm", "factor", "sweep"],
+                    default="all",
                     help="syrk: time only the H kernel on [--tokens, --dim]; qr: only the "
-                         "pivoted QR on a --dim x --dim matrix (profiling)")
+                         "pivoted QR on a --dim x --dim matrix; gemm / factor / sweep: one "
+                         "component (profiling)")
+    ap.add_argument("--m", type=int, default=12288)
+    ap.add_argument("--n", type=int, default=None)
+    ap.add_argument("--k", type=int, default=128)
     ap.add_argument("--dim", type=int, default=4096)
     ap.add_argument("--panel", type=int, default=64)
     ap.add_argument("--strategy", choices=["layer", "sharded"], default="layer",
                     help="layer: each rank quantizes its own layer set (weak scaling, no "
                          "collective); sharded: one layer set over all ranks (strong scaling)")
     args = ap.parse_args()
-    if args.only in ("syrk", "qr"):
+    if args.only != "all":
         import torch
         torch.cuda.set_device(0)
         if args.only == "syrk":
             run_kernel_only(args)
+        elif args.only in ("gemm", "factor", "sweep"):
+            run_component(args)
         else:
             import importlib
             BQ = importlib.import_module("jax_gptq_b200.pallas.blocked_pivoted_qr")
