@@ -12,8 +12,10 @@
 //      a contiguous 128-float row);
 //   2. sweep_rows_kernel: one lane per weight row, one warp per CTA; the
 //      lane quantizes its row's columns one by one (32-column sub-blocks in
-//      registers, the rest of the block in a shared-memory row buffer) and
-//      writes codes, dequantized values and scaled errors (w - dq) / U_ii;
+//      registers, the rest of the block in a shared-memory row buffer, the U
+//      rows of each sub-block's trailing update copied in by cp.async while
+//      the sub-block's columns are quantized) and writes codes, dequantized
+//      values and scaled errors (w - dq) / U_ii;
 //   3. wp[:, b1:] -= err @ U[b0:b1, b1:]  (fp32 GEMM).
 // Finally codes/dequant are scattered back to original column order.
 #include "gq_common.cuh"
@@ -127,6 +129,8 @@ __global__ void __launch_bounds__(32) sweep_rows_kernel(SweepArgs a) {
   __shared__ float ws[SW_BLOCK * SW_WP];
   __shared__ __align__(16) float tile[SW_SUB * SW_TP];
   __shared__ float rinv[SW_BLOCK];
+  // U rows the current sub-block's errors update: stg[j - c0 - 32][k] = U[b0 + c0 + k][b0 + j]
+  __shared__ __align__(16) float stg[(SW_BLOCK - SW_SUB) * SW_SUB];
   const int lane = threadIdx.x;
   const int bw = a.bw;
   const float* __restrict__ ubt = a.ubt;
@@ -152,6 +156,18 @@ __global__ void __launch_bounds__(32) sweep_rows_kernel(SweepArgs a) {
   __syncwarp();
 
   for (int c0 = 0; c0 < bw; c0 += SW_SUB) {
+    // start copying the U rows for this sub-block's trailing update; they land
+    // while the column loop below runs
+    const int trail = bw - c0 - SW_SUB;
+    for (int ch = lane; ch < trail * (SW_SUB / 4); ch += 32) {
+      const int r = ch / (SW_SUB / 4), part = ch % (SW_SUB / 4);
+      const float* src = ubt + (int64_t)(c0 + SW_SUB + r) * SW_BLOCK + c0 + 4 * part;
+      asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(
+                       (uint32_t)__cvta_generic_to_shared(stg + r * SW_SUB + 4 * part)),
+                   "l"(src)
+                   : "memory");
+    }
+    asm volatile("cp.async.commit_group;" ::: "memory");
     // tile[k][t] = U[b0 + c0 + k][b0 + c0 + t]  (lane t copies its row of the band)
     if (c0 + lane < bw) {
       const float4* src = reinterpret_cast<const float4*>(ubt + (int64_t)(c0 + lane) * SW_BLOCK + c0);
@@ -252,7 +268,9 @@ __global__ void __launch_bounds__(32) sweep_rows_kernel(SweepArgs a) {
     }
 
     // the block's later columns: ws[j] -= sum_k e[k] U[c0 + k][j], k increasing
-    const float4* ub4 = reinterpret_cast<const float4*>(ubt);
+    asm volatile("cp.async.wait_group 0;" ::: "memory");
+    __syncwarp();
+    const float4* ub4 = reinterpret_cast<const float4*>(stg);
     for (int j0 = c0 + SW_SUB; j0 < bw; j0 += 4) {
       float v[4];
 #pragma unroll
@@ -262,7 +280,7 @@ __global__ void __launch_bounds__(32) sweep_rows_kernel(SweepArgs a) {
         float4 u4[4];
 #pragma unroll
         for (int jj = 0; jj < 4; ++jj)
-          u4[jj] = (j0 + jj < bw) ? __ldg(ub4 + (int64_t)(j0 + jj) * (SW_BLOCK / 4) + c0 / 4 + kc)
+          u4[jj] = (j0 + jj < bw) ? ub4[(j0 + jj - c0 - SW_SUB) * (SW_SUB / 4) + kc]
                                   : make_float4(0.f, 0.f, 0.f, 0.f);
 #pragma unroll
         for (int jj = 0; jj < 4; ++jj) {
