@@ -140,12 +140,23 @@ __global__ void __launch_bounds__(32) sweep_rows_kernel(SweepArgs a) {
   const bool valid = row < a.m;
   float* wrow = valid ? a.wp + row * a.ldp + a.b0 : nullptr;
   if (valid) {
-    for (int j = 0; j < bw; j += 4) {
-      const float4 v = *reinterpret_cast<const float4*>(wrow + j);
-      ws[(j + 0) * SW_WP + lane] = v.x;
-      ws[(j + 1) * SW_WP + lane] = v.y;
-      ws[(j + 2) * SW_WP + lane] = v.z;
-      ws[(j + 3) * SW_WP + lane] = v.w;
+    // the row's block in two batches of 16 loads in flight (not one load per round trip)
+#pragma unroll
+    for (int half = 0; half < 2; ++half) {
+      float4 v[SW_BLOCK / 8];
+#pragma unroll
+      for (int q = 0; q < SW_BLOCK / 8; ++q) {
+        const int j = half * (SW_BLOCK / 2) + 4 * q;
+        v[q] = (j < bw) ? *reinterpret_cast<const float4*>(wrow + j) : make_float4(0.f, 0.f, 0.f, 0.f);
+      }
+#pragma unroll
+      for (int q = 0; q < SW_BLOCK / 8; ++q) {
+        const int j = half * (SW_BLOCK / 2) + 4 * q;
+        ws[(j + 0) * SW_WP + lane] = v[q].x;
+        ws[(j + 1) * SW_WP + lane] = v[q].y;
+        ws[(j + 2) * SW_WP + lane] = v[q].z;
+        ws[(j + 3) * SW_WP + lane] = v[q].w;
+      }
     }
   }
   float scale = 1.f, zero = 0.f;
