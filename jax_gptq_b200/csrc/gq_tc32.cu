@@ -15,7 +15,7 @@
 // 32-float-deep (128-byte) k-slices:
 //   warp 0     TMA producer (one thread)
 //   warp 1     MMA issuer (one thread), 2 TMEM accumulators of 128 columns
-//   warps 2-5  hi/lo converters (in place: raw -> hi; lo to its own buffer)
+//   warps 2-5  lo converters (lo = raw - hi to its own buffer; the raw tile is the hi operand)
 //   warps 6-9  epilogue: tcgen05.ld, then for beta 0 / 1 swizzled 32 x 32
 //              chunks written by TMA tensor stores / fp32 reduce-adds (no
 //              read of C by the SM), for other beta per-row loads and stores
@@ -160,6 +160,16 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
         "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
       : "r"(taddr));
   asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+}
+
+// lo = x - hi with hi = x with the low 13 mantissa bits cleared (exact).  The
+// MMA reads the raw fp32 tile as the hi operand: kind::tf32 ignores those 13
+// bits, so the raw value and hi multiply identically.
+__device__ __forceinline__ uint4 lo_part(uint4 x) {
+  return make_uint4(__float_as_uint(__uint_as_float(x.x) - __uint_as_float(x.x & 0xFFFFE000u)),
+                    __float_as_uint(__uint_as_float(x.y) - __uint_as_float(x.y & 0xFFFFE000u)),
+                    __float_as_uint(__uint_as_float(x.z) - __uint_as_float(x.z & 0xFFFFE000u)),
+                    __float_as_uint(__uint_as_float(x.w) - __uint_as_float(x.w & 0xFFFFE000u)));
 }
 
 __device__ __forceinline__ bool tile_skipped(const Params& p, int bm, int bn) {
@@ -313,7 +323,7 @@ tf32x3_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__
       }
     }
   } else if (warp < 6) {
-    // converters: raw -> hi in place, lo = raw - hi
+    // converters: lo = raw - hi (the raw tile itself serves as hi)
     const int ct = threadIdx.x - 64;  // 0..127
     int stage = 0;
     uint32_t phase = 0;
@@ -334,29 +344,13 @@ tf32x3_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__
         uint4* bl4 = reinterpret_cast<uint4*>(b_lo(stage));
 #pragma unroll 4
         for (int i = ct; i < A_BYTES / 16; i += 128) {
-          uint4 x = ah4[i];
-          uint4 h = make_uint4(x.x & 0xFFFFE000u, x.y & 0xFFFFE000u, x.z & 0xFFFFE000u,
-                               x.w & 0xFFFFE000u);
-          uint4 l = make_uint4(
-              __float_as_uint(__uint_as_float(x.x) - __uint_as_float(h.x)),
-              __float_as_uint(__uint_as_float(x.y) - __uint_as_float(h.y)),
-              __float_as_uint(__uint_as_float(x.z) - __uint_as_float(h.z)),
-              __float_as_uint(__uint_as_float(x.w) - __uint_as_float(h.w)));
-          ah4[i] = h;
-          al4[i] = l;
+          const uint4 x = ah4[i];
+          al4[i] = lo_part(x);
         }
 #pragma unroll 4
         for (int i = ct; i < B_BYTES / 16; i += 128) {
-          uint4 x = bh4[i];
-          uint4 h = make_uint4(x.x & 0xFFFFE000u, x.y & 0xFFFFE000u, x.z & 0xFFFFE000u,
-                               x.w & 0xFFFFE000u);
-          uint4 l = make_uint4(
-              __float_as_uint(__uint_as_float(x.x) - __uint_as_float(h.x)),
-              __float_as_uint(__uint_as_float(x.y) - __uint_as_float(h.y)),
-              __float_as_uint(__uint_as_float(x.z) - __uint_as_float(h.z)),
-              __float_as_uint(__uint_as_float(x.w) - __uint_as_float(h.w)));
-          bh4[i] = h;
-          bl4[i] = l;
+          const uint4 x = bh4[i];
+          bl4[i] = lo_part(x);
         }
         asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
         mbar_arrive(&conv[stage]);
