@@ -43,13 +43,17 @@ int read_status(int reset, int* out) {
   return GQ_OK;
 }
 
-constexpr int BM = 128, BN = 128, BK = 32, STAGES = 3;
+constexpr int BM = 128, BN = 128, BK = 32, STAGES = 4;
 constexpr int CHUNK_KB = 4;  // k-slices (x 32 of K) per TMEM accumulation
 constexpr int A_BYTES = BM * BK * 4;   // 16 KB
 constexpr int B_BYTES = BN * BK * 4;   // 16 KB
-constexpr int STAGE_BYTES = 2 * (A_BYTES + B_BYTES);  // raw/hi + lo for A and B
+constexpr int STAGE_BYTES = A_BYTES + 2 * B_BYTES;  // raw A | raw B (= B hi) | B lo
 constexpr int THREADS = 320;
-constexpr int TMEM_COLS = 256;
+// TMEM: two 128-column accumulators, then per stage the A slice as MMA
+// operand, hi in 32 columns and lo in the next 32 (one row per lane)
+constexpr int TMEM_COLS = 512;
+constexpr int A_TMEM_COL0 = 2 * BN;
+static_assert(A_TMEM_COL0 + STAGES * 2 * BK <= TMEM_COLS, "TMEM columns");
 // epilogue staging: per epilogue warp two 32 x 32 fp32 chunks (4 KB each,
 // 128-byte swizzled rows, the layout a SWIZZLE_128B tensor store reads)
 constexpr int C_CHUNK_BYTES = 32 * 32 * 4;
@@ -142,6 +146,26 @@ __device__ __forceinline__ void umma_tf32(uint32_t d_tmem, uint64_t adesc, uint6
       " tcgen05.mma.cta_group::1.kind::tf32 [%0], %1, %2, %3, p;\n}" ::"r"(d_tmem),
       "l"(adesc), "l"(bdesc), "r"(id), "r"(accum));
 }
+// A operand from TMEM (a_tmem: column of its first k), B from shared memory.
+__device__ __forceinline__ void umma_tf32_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t bdesc,
+                                             uint32_t id, uint32_t accum) {
+  asm volatile(
+      "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
+      " tcgen05.mma.cta_group::1.kind::tf32 [%0], [%1], %2, %3, p;\n}" ::"r"(d_tmem),
+      "r"(a_tmem), "l"(bdesc), "r"(id), "r"(accum));
+}
+__device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t (&r)[32]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, "
+      "%11, %12, %13, %14, %15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, "
+      "%29, %30, %31, %32};" ::"r"(taddr),
+      "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]),
+      "r"(r[8]), "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]),
+      "r"(r[15]), "r"(r[16]), "r"(r[17]), "r"(r[18]), "r"(r[19]), "r"(r[20]), "r"(r[21]),
+      "r"(r[22]), "r"(r[23]), "r"(r[24]), "r"(r[25]), "r"(r[26]), "r"(r[27]), "r"(r[28]),
+      "r"(r[29]), "r"(r[30]), "r"(r[31])
+      : "memory");
+}
 __device__ __forceinline__ void umma_commit(uint64_t* bar) {
   asm volatile(
       "tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
@@ -197,11 +221,10 @@ tf32x3_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~uintptr_t(1023));
-  // per stage: A raw/hi | B raw/hi | A lo | B lo
-  auto a_hi = [&](int s) { return smem + s * STAGE_BYTES; };
+  // per stage: A raw | B raw (= B hi) | B lo
+  auto a_raw = [&](int s) { return smem + s * STAGE_BYTES; };
   auto b_hi = [&](int s) { return smem + s * STAGE_BYTES + A_BYTES; };
-  auto a_lo = [&](int s) { return smem + s * STAGE_BYTES + A_BYTES + B_BYTES; };
-  auto b_lo = [&](int s) { return smem + s * STAGE_BYTES + 2 * A_BYTES + B_BYTES; };
+  auto b_lo = [&](int s) { return smem + s * STAGE_BYTES + A_BYTES + B_BYTES; };
   uint8_t* c_stage = smem + STAGES * STAGE_BYTES;
   uint64_t* full = reinterpret_cast<uint64_t*>(c_stage + C_STAGE_BYTES);
   uint64_t* conv = full + STAGES;
@@ -252,7 +275,7 @@ tf32x3_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__
           if (!mbar_wait(&empty[stage], phase ^ 1, abort_flag)) break;
           mbar_expect_tx(&full[stage], A_BYTES + B_BYTES);
           const int k0 = kb * BK;
-          tma_load_2d(&map_a, &full[stage], a_hi(stage), k0, bm * BM);
+          tma_load_2d(&map_a, &full[stage], a_raw(stage), k0, bm * BM);
           if (p.b_kmajor) {
             tma_load_2d(&map_b, &full[stage], b_hi(stage), k0, bn * BN);
           } else {
@@ -293,19 +316,19 @@ tf32x3_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__
               break;
             }
             fence_after();
-            const uint32_t ah = smem_u32(a_hi(stage)), al = smem_u32(a_lo(stage));
             const uint32_t bh = smem_u32(b_hi(stage)), bl = smem_u32(b_lo(stage));
+            const uint32_t a_hi_t = tmem_base + (uint32_t)(A_TMEM_COL0 + stage * 2 * BK);
 #pragma unroll
             for (int kk = 0; kk < BK / 8; ++kk) {
-              // K-major SW128: 8 tf32 = 32 bytes per k-step inside each 128-byte row
-              const uint64_t dah = make_desc(ah + kk * 32, 16, 1024);
-              const uint64_t dal = make_desc(al + kk * 32, 16, 1024);
+              // B: K-major SW128, 8 tf32 = 32 bytes per k-step inside each 128-byte row;
+              // A: 8 TMEM columns per k-step
               const uint64_t dbh = make_desc(bh + kk * 32, 16, 1024);
               const uint64_t dbl = make_desc(bl + kk * 32, 16, 1024);
+              const uint32_t ah = a_hi_t + kk * 8, al = a_hi_t + BK + kk * 8;
               const uint32_t first = (kb == kc && kk == 0) ? 0u : 1u;
-              umma_tf32(d_tmem, dal, dbh, id, first);
-              umma_tf32(d_tmem, dah, dbl, id, 1u);
-              umma_tf32(d_tmem, dah, dbh, id, 1u);
+              umma_tf32_ts(d_tmem, al, dbh, id, first);
+              umma_tf32_ts(d_tmem, ah, dbl, id, 1u);
+              umma_tf32_ts(d_tmem, ah, dbh, id, 1u);
             }
             umma_commit(&empty[stage]);
             if (++stage == STAGES) {
@@ -323,8 +346,13 @@ tf32x3_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__
       }
     }
   } else if (warp < 6) {
-    // converters: lo = raw - hi (the raw tile itself serves as hi)
+    // converters: A row `arow` (this warp's TMEM lane quarter) split into hi and
+    // lo straight into TMEM; B lo = raw - hi into shared memory (the raw B tile
+    // itself serves as B hi: kind::tf32 ignores the low 13 bits)
     const int ct = threadIdx.x - 64;  // 0..127
+    const int quarter = warp & 3;
+    const int arow = quarter * 32 + lane;
+    const uint32_t a_lane = (uint32_t)(quarter * 32) << 16;
     int stage = 0;
     uint32_t phase = 0;
     for (int t = blockIdx.x; t < p.num_tiles && !*abort_flag; t += gridDim.x) {
@@ -338,21 +366,34 @@ tf32x3_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__
           ok = false;
           break;
         }
-        uint4* ah4 = reinterpret_cast<uint4*>(a_hi(stage));
-        uint4* bh4 = reinterpret_cast<uint4*>(b_hi(stage));
-        uint4* al4 = reinterpret_cast<uint4*>(a_lo(stage));
-        uint4* bl4 = reinterpret_cast<uint4*>(b_lo(stage));
-#pragma unroll 4
-        for (int i = ct; i < A_BYTES / 16; i += 128) {
-          const uint4 x = ah4[i];
-          al4[i] = lo_part(x);
+        {
+          // row arow of the SW128 K-major A tile: 16-byte chunk c sits at c ^ (row % 8)
+          const uint8_t* rowp = a_raw(stage) + arow * 128;
+          uint32_t hi[32], lo[32];
+#pragma unroll
+          for (int c = 0; c < 8; ++c) {
+            const uint4 x = *reinterpret_cast<const uint4*>(rowp + ((c ^ (arow & 7)) << 4));
+            const uint32_t v[4] = {x.x, x.y, x.z, x.w};
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+              hi[4 * c + e] = v[e] & 0xFFFFE000u;
+              lo[4 * c + e] = __float_as_uint(__uint_as_float(v[e]) - __uint_as_float(hi[4 * c + e]));
+            }
+          }
+          const uint32_t tcol = tmem_base + a_lane + (uint32_t)(A_TMEM_COL0 + stage * 2 * BK);
+          tmem_st32(tcol, hi);
+          tmem_st32(tcol + BK, lo);
         }
+        uint4* bh4 = reinterpret_cast<uint4*>(b_hi(stage));
+        uint4* bl4 = reinterpret_cast<uint4*>(b_lo(stage));
 #pragma unroll 4
         for (int i = ct; i < B_BYTES / 16; i += 128) {
           const uint4 x = bh4[i];
           bl4[i] = lo_part(x);
         }
+        asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
         asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+        fence_before();
         mbar_arrive(&conv[stage]);
         if (++stage == STAGES) {
           stage = 0;
