@@ -258,6 +258,23 @@ int gq_qr_apply_panel(float* b, int64_t rows, int64_t cols, int64_t ldb, const f
                       void* stream);
 
 /* ------------------------------------------------------------------------
+ * Packed quantized weights (the reference returns only the dequantized
+ * floats of quant.py:37; this is the checkpoint form of a sweep's output).
+ * packed [m, ldp] uint32: row r's codes (original column order, as
+ * gq_gptq_sweep / gq_rtn write them) as one little-endian bit stream -- code c
+ * in bits [c*bits, (c+1)*bits), word w = stream bits [32w, 32w+32).
+ * gq_packed_words(n, bits) = ceil(n * bits / 32) words per row (-1 on bad
+ * arguments).  gq_unpack_dequant returns the codes and/or the dequantized
+ * weights (code + qmin - zero[g_idx[c]]) * scale[g_idx[c]], bit-identical to
+ * the sweep's dequant output; scales/zeros [m, n_groups], g_idx [n]. */
+int64_t gq_packed_words(int64_t n, int bits);
+int gq_pack_codes(const uint8_t* codes, int64_t m, int64_t n, int64_t ldc, int bits,
+                  uint32_t* packed, int64_t ldp, void* stream);
+int gq_unpack_dequant(const uint32_t* packed, int64_t m, int64_t n, int64_t ldp, int bits, int sym,
+                      const float* scales, const float* zeros, int64_t n_groups,
+                      const int32_t* g_idx, float* dequant, uint8_t* codes, void* stream);
+
+/* ------------------------------------------------------------------------
  * Multi-GPU: a per-device handle with an optional NCCL communicator and the
  * in-place fp32 sum all-reduce used for token-sharded Hessians (H = sum over
  * ranks of X_r^T X_r).  The reference is single-device and has no
