@@ -63,6 +63,29 @@ __global__ void act_order_rank_kernel(const float* __restrict__ h, int64_t d, in
   if (i < d) perm[rank] = (int32_t)i;
 }
 
+// The same ranking with 16 lanes per element, each lane counting every 16th
+// key of a shared-memory copy of the whole diagonal (dynamic smem, 4d bytes),
+// so d * 16 threads share the d^2 comparisons.
+constexpr int RANK_LANES = 16;
+__global__ void act_order_rank16_kernel(const float* __restrict__ h, int64_t d, int64_t ldh,
+                                        int32_t* __restrict__ perm) {
+  extern __shared__ float diag[];
+  for (int64_t t = threadIdx.x; t < d; t += blockDim.x) diag[t] = h[t * ldh + t];
+  __syncthreads();
+  const int sub = threadIdx.x & (RANK_LANES - 1);
+  const int64_t i = (blockIdx.x * (int64_t)blockDim.x + threadIdx.x) / RANK_LANES;
+  const float ki = (i < d) ? diag[i] : 0.f;
+  int rank = 0;
+#pragma unroll 4
+  for (int64_t j = sub; j < d; j += RANK_LANES) {
+    const float kj = diag[j];
+    rank += key_gt(kj, ki) || (key_eq(kj, ki) && j > i);
+  }
+#pragma unroll
+  for (int o = RANK_LANES / 2; o > 0; o >>= 1) rank += __shfl_xor_sync(0xffffffffu, rank, o);
+  if (i < d && sub == 0) perm[rank] = (int32_t)i;
+}
+
 __global__ void iota_kernel(int32_t* perm, int64_t d) {
   int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
   if (i < d) perm[i] = (int32_t)i;
@@ -72,8 +95,23 @@ int act_order_perm(const float* h, int64_t d, int64_t ldh, int ordering, int32_t
                    cudaStream_t st) {
   if (d == 0) return GQ_OK;
   unsigned blocks = (unsigned)ceil_div(d, 256);
-  if (ordering == 0) iota_kernel<<<blocks, 256, 0, st>>>(perm, d);
-  else act_order_rank_kernel<<<blocks, 256, 0, st>>>(h, d, ldh, perm);
+  const size_t diag_bytes = (size_t)d * sizeof(float);
+  if (ordering == 0) {
+    iota_kernel<<<blocks, 256, 0, st>>>(perm, d);
+  } else if (diag_bytes <= 200 * 1024) {
+    static int attr_device = -1;
+    int dev = 0;
+    GQ_CHECK_CUDA(cudaGetDevice(&dev));
+    if (attr_device != dev) {
+      GQ_CHECK_CUDA(cudaFuncSetAttribute(act_order_rank16_kernel,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024));
+      attr_device = dev;
+    }
+    act_order_rank16_kernel<<<(unsigned)ceil_div(d * RANK_LANES, 256), 256, diag_bytes, st>>>(
+        h, d, ldh, perm);
+  } else {
+    act_order_rank_kernel<<<blocks, 256, 0, st>>>(h, d, ldh, perm);
+  }
   return check_launch("gq_act_order_perm");
 }
 
@@ -97,26 +135,32 @@ __global__ void diag_mean_kernel(const float* __restrict__ h, int64_t d, int64_t
   }
 }
 
-// ht[i][j] = h[p[n-1-i]][p[n-1-j]] + damp * mean * (i == j)   (reversed order)
-// hd[i][j] = h[p[i]][p[j]] + damp * mean * (i == j)            (optional)
-__global__ void damp_permute_kernel(const float* __restrict__ h, int64_t n, int64_t ldh,
-                                    const int32_t* __restrict__ perm, const float* __restrict__ mean,
-                                    float damp, float* __restrict__ ht, float* __restrict__ hd) {
-  int64_t i = blockIdx.y;
-  float dv = damp * mean[0];
-  int64_t pi_rev = perm ? perm[n - 1 - i] : (n - 1 - i);
-  int64_t pi = perm ? perm[i] : i;
-  for (int64_t j = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; j < n;
-       j += (int64_t)gridDim.x * blockDim.x) {
-    int64_t pj_rev = perm ? perm[n - 1 - j] : (n - 1 - j);
-    float v = h[pi_rev * ldh + pj_rev];
-    if (i == j) v = v + dv;
-    ht[i * n + j] = v;
-    if (hd) {
-      int64_t pj = perm ? perm[j] : j;
-      float w = h[pi * ldh + pj];
-      if (i == j) w = w + dv;
-      hd[i * n + j] = w;
+// Row i of the output is a gathered row of h: rows are read whole and
+// coalesced into shared memory (n floats), then permuted out of it.
+//   lower: ht[i][j] = h[q_i][q_j] + damp * mean * (i == j) for j <= i, 0 for
+//          j > i, with q = the permutation reversed (q_i = p[n-1-i]);
+//   full:  hd[i][j] = h[p_i][p_j] + damp * mean * (i == j).
+template <bool LOWER>
+__global__ void damp_permute_rows_kernel(const float* __restrict__ h, int64_t n, int64_t ldh,
+                                         const int32_t* __restrict__ perm,
+                                         const float* __restrict__ mean, float damp,
+                                         float* __restrict__ out) {
+  extern __shared__ float srow[];
+  const float dv = damp * mean[0];
+  for (int64_t i = blockIdx.x; i < n; i += gridDim.x) {
+    const int64_t ri = LOWER ? (n - 1 - i) : i;
+    const int64_t pi = perm ? perm[ri] : ri;
+    __syncthreads();
+    for (int64_t c = threadIdx.x; c < n; c += blockDim.x) srow[c] = h[pi * ldh + c];
+    __syncthreads();
+    for (int64_t j = threadIdx.x; j < n; j += blockDim.x) {
+      float v = 0.f;
+      if (!LOWER || j <= i) {
+        const int64_t rj = LOWER ? (n - 1 - j) : j;
+        v = srow[perm ? perm[rj] : rj];
+        if (i == j) v = v + dv;
+      }
+      out[i * n + j] = v;
     }
   }
 }
@@ -321,21 +365,13 @@ potrf_diag_kernel(float* __restrict__ a, int64_t lda, int kb, int* __restrict__ 
   if (threadIdx.x == 0 && bad) atomicExch(status, GQ_DEVERR_NOTPD);
 }
 
-// Zero the strict upper triangle of an n x n matrix (ld).
-__global__ void zero_upper_kernel(float* __restrict__ a, int64_t n, int64_t lda) {
-  int64_t r = blockIdx.y;
-  for (int64_t c = r + 1 + blockIdx.x * (int64_t)blockDim.x + threadIdx.x; c < n;
-       c += (int64_t)gridDim.x * blockDim.x)
-    a[r * lda + c] = 0.f;
-}
-
-// u[i][j] = linv[n-1-i][n-1-j]
+// u[i][j] = linv[n-1-i][n-1-j], one block per row (both sides coalesced)
 __global__ void reverse_copy_kernel(const float* __restrict__ linv, int64_t n, int64_t ldl,
                                     float* __restrict__ u, int64_t ldu) {
-  int64_t i = blockIdx.y;
-  for (int64_t j = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; j < n;
-       j += (int64_t)gridDim.x * blockDim.x)
-    u[i * ldu + j] = linv[(n - 1 - i) * ldl + (n - 1 - j)];
+  for (int64_t i = blockIdx.x; i < n; i += gridDim.x) {
+    const float* src = linv + (n - 1 - i) * ldl + (n - 1);
+    for (int64_t j = threadIdx.x; j < n; j += blockDim.x) u[i * ldu + j] = src[-j];
+  }
 }
 
 int transpose2d(const float* src, int64_t rows, int64_t cols, int64_t lds, float* dst, int64_t ldd,
@@ -352,6 +388,8 @@ int transpose2d(const float* src, int64_t rows, int64_t cols, int64_t lds, float
 // operands K-major (tensor-core path): X11^T is formed by a transpose and the
 // last product is taken as X21 = -X22 Tt^T with Tt = X11^T L21^T.
 // scratch: n1 * n floats suffice (n1 <= n / 2 + NB).
+constexpr int MAX_ROW_BYTES = 220 * 1024;  // the row-staged permute holds one row of h
+
 int diag_kernel_setup() {
   static int attr_device = -1;
   int dev = 0;
@@ -359,6 +397,10 @@ int diag_kernel_setup() {
   if (attr_device != dev) {
     GQ_CHECK_CUDA(cudaFuncSetAttribute(potrf_diag_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                        (int)DIAG_SMEM));
+    GQ_CHECK_CUDA(cudaFuncSetAttribute(damp_permute_rows_kernel<true>,
+                                       cudaFuncAttributeMaxDynamicSharedMemorySize, MAX_ROW_BYTES));
+    GQ_CHECK_CUDA(cudaFuncSetAttribute(damp_permute_rows_kernel<false>,
+                                       cudaFuncAttributeMaxDynamicSharedMemorySize, MAX_ROW_BYTES));
     attr_device = dev;
   }
   return GQ_OK;
@@ -423,6 +465,9 @@ int gq_hessian_factor_attempt(const float* h, int64_t d, int64_t ldh, const int3
              (long long)workspace_bytes, (long long)gq_hessian_factor_workspace_size(d));
   GQ_REQUIRE(damp_percent >= 0.0, "gq_hessian_factor_attempt: negative damp_percent");
   GQ_REQUIRE(attempt >= 0 && attempt < 5, "gq_hessian_factor_attempt: attempt must be 0..4");
+  GQ_REQUIRE(d * (int64_t)sizeof(float) <= gq::MAX_ROW_BYTES,
+             "gq_hessian_factor_attempt: d = %lld exceeds %d", (long long)d,
+             gq::MAX_ROW_BYTES / (int)sizeof(float));
   cudaStream_t st = gq::as_stream(stream);
   float* ws = reinterpret_cast<float*>(workspace);
   float* ht = ws;                                  // d*d
@@ -434,14 +479,19 @@ int gq_hessian_factor_attempt(const float* h, int64_t d, int64_t ldh, const int3
   GQ_TRY(gq::check_launch("diag_mean"));
   const double damp = std::pow(10.0, attempt) * damp_percent;
   GQ_CHECK_CUDA(cudaMemsetAsync(status, 0, sizeof(int), st));
-  dim3 grid((unsigned)std::min<int64_t>(gq::ceil_div(d, 256), 64), (unsigned)d);
-  gq::damp_permute_kernel<<<grid, 256, 0, st>>>(h, d, ldh, perm, mean, (float)damp, ht, hd_out);
+  const unsigned rows_grid = (unsigned)std::min<int64_t>(d, 148 * 16);
+  const size_t row_bytes = (size_t)d * sizeof(float);
+  gq::damp_permute_rows_kernel<true><<<rows_grid, 256, row_bytes, st>>>(h, d, ldh, perm, mean,
+                                                                        (float)damp, ht);
   GQ_TRY(gq::check_launch("damp_permute"));
-  gq::zero_upper_kernel<<<grid, 256, 0, st>>>(ht, d, d);
-  GQ_TRY(gq::check_launch("zero_upper"));
-  // L^-1 in place, then U = J L^-1 J
+  if (hd_out) {
+    gq::damp_permute_rows_kernel<false><<<rows_grid, 256, row_bytes, st>>>(h, d, ldh, perm, mean,
+                                                                           (float)damp, hd_out);
+    GQ_TRY(gq::check_launch("damp_permute"));
+  }
+  // L^-1 in place (lower triangle; the strict upper part is zero), then U = J L^-1 J
   GQ_TRY(gq::inv_chol_rec(ht, d, d, scratch, status, st));
-  gq::reverse_copy_kernel<<<grid, 256, 0, st>>>(ht, d, d, u, ldu);
+  gq::reverse_copy_kernel<<<rows_grid, 256, 0, st>>>(ht, d, d, u, ldu);
   return gq::check_launch("reverse_copy");
 }
 
