@@ -156,11 +156,13 @@ _SIDE_STREAMS: dict[int, list] = {}
 
 
 def _side_streams(n: int) -> list:
-    """A per-device pool of side streams, one per input group run concurrently."""
+    """A per-device pool of side streams, one per input group run concurrently;
+    the first has the highest scheduling priority (it carries the longest
+    chain: the largest Hessian's factor and its sweep)."""
     dev = torch.cuda.current_device()
     pool = _SIDE_STREAMS.setdefault(dev, [])
     while len(pool) < n:
-        pool.append(torch.cuda.Stream(device=dev))
+        pool.append(torch.cuda.Stream(device=dev, priority=-1 if not pool else 0))
     return pool[:n]
 
 
@@ -180,10 +182,12 @@ def _run_groups_concurrently(hs: dict, work, redo) -> dict:
     main = torch.cuda.current_stream()
     streams = _side_streams(len(hs))
     pending = {}
-    for (grp, h), s in zip(hs.items(), streams):
+    # largest H first, on the high-priority stream: its chain is the longest
+    order = sorted(hs, key=lambda g: -hs[g].shape[0])
+    for grp, s in zip(order, streams):
         s.wait_stream(main)
         with torch.cuda.stream(s):
-            pending[grp] = work(grp, h)
+            pending[grp] = work(grp, hs[grp])
     for s in streams:
         main.wait_stream(s)
     for status, res in pending.values():
