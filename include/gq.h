@@ -32,6 +32,14 @@ typedef enum {
   GQ_ENCCL = 6          /* NCCL missing or an NCCL call failed */
 } gq_status;
 
+/* Grid cap for the persistent tensor-core kernels (fp32 GEMM, H
+ * accumulation) launched afterwards by the calling host thread: at most n
+ * CTAs, one per SM (0 = every SM, the default).  For hosts that run several
+ * independent chains on different streams and want SMs left free for a
+ * latency-bound one; results do not depend on it.  No counterpart in the
+ * reference (single stream). */
+int gq_set_cta_budget(int n);
+
 /* Library version (major*10000 + minor*100 + patch). */
 int gq_version(void);
 

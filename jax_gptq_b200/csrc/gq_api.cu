@@ -33,6 +33,14 @@ int sm_count() {
   return cached[dev];
 }
 
+// Grid cap for the persistent tensor-core kernels launched by this host thread.
+static thread_local int g_cta_budget = 0;
+
+int cta_budget() {
+  const int n = sm_count();
+  return (g_cta_budget > 0 && g_cta_budget < n) ? g_cta_budget : n;
+}
+
 // Copy the upper triangle (j > i) of h into the lower triangle.  Tiled
 // through shared memory so both the read and the write are coalesced.
 __global__ void symmetrize_upper_kernel(float* __restrict__ h, int64_t d, int64_t ldh) {
@@ -101,3 +109,9 @@ int gq_symmetrize_upper(float* h, int64_t d, int64_t ldh, void* stream) {
 }
 
 }  // extern "C"
+
+extern "C" int gq_set_cta_budget(int n) {
+  GQ_REQUIRE(n >= 0, "gq_set_cta_budget: negative budget");
+  gq::g_cta_budget = n;
+  return GQ_OK;
+}

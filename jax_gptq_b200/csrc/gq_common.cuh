@@ -95,5 +95,8 @@ __device__ __forceinline__ float warp_min(float v) {
 
 // Number of SMs of the current device (cached per device).
 int sm_count();
+// Grid size for persistent kernels: sm_count(), or less when this host thread
+// set a budget with gq_set_cta_budget.
+int cta_budget();
 
 }  // namespace gq

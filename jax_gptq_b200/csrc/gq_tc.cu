@@ -445,7 +445,7 @@ int launch(const void* xa, int64_t lda, const void* xb, int64_t ldb, int64_t K, 
                                        SMEM_BYTES));
     attr_set = true;
   }
-  const int grid = std::min(p.num_tiles, sm_count());
+  const int grid = std::min(p.num_tiles, cta_budget());
   gemm_tn_kernel<<<grid, THREADS, SMEM_BYTES, st>>>(ma, mbm, p);
   return check_launch("tcgen05 gemm_tn");
 }

@@ -609,7 +609,7 @@ int launch(int tb, int64_t M, int64_t N, int64_t K, float alpha, const float* A,
                                        SMEM_BYTES));
     attr_device = dev;
   }
-  const int grid = std::min(p.num_tiles, sm_count());
+  const int grid = std::min(p.num_tiles, cta_budget());
   tf32x3_kernel<<<grid, THREADS, SMEM_BYTES, st>>>(ma, mbm, mc, p);
   return check_launch("tcgen05 tf32x3 gemm");
 }

@@ -21,7 +21,7 @@ from dataclasses import dataclass, field
 
 import torch
 
-from . import stats
+from . import _lib, stats
 from .config import QuantConfig
 from .gptq_ref import (HessianFactor, SweepResult, factor_hessian, factor_hessian_attempt0,
                        gptq_sweep)
@@ -153,6 +153,7 @@ def _split_rows(res: SweepResult, members) -> dict:
 
 
 _SIDE_STREAMS: dict[int, list] = {}
+RESERVED_SMS = 16  # SMs the non-priority groups' persistent kernels leave free
 
 
 def _side_streams(n: int) -> list:
@@ -182,12 +183,19 @@ def _run_groups_concurrently(hs: dict, work, redo) -> dict:
     main = torch.cuda.current_stream()
     streams = _side_streams(len(hs))
     pending = {}
-    # largest H first, on the high-priority stream: its chain is the longest
+    # largest H first, on the high-priority stream: its chain is the longest;
+    # the other groups' persistent kernels leave RESERVED_SMS SMs to it
     order = sorted(hs, key=lambda g: -hs[g].shape[0])
-    for grp, s in zip(order, streams):
+    sms = torch.cuda.get_device_properties(main.device).multi_processor_count
+    lib = _lib.lib()
+    for idx, (grp, s) in enumerate(zip(order, streams)):
         s.wait_stream(main)
-        with torch.cuda.stream(s):
-            pending[grp] = work(grp, hs[grp])
+        lib.gq_set_cta_budget(0 if idx == 0 else max(1, sms - RESERVED_SMS))
+        try:
+            with torch.cuda.stream(s):
+                pending[grp] = work(grp, hs[grp])
+        finally:
+            lib.gq_set_cta_budget(0)
     for s in streams:
         main.wait_stream(s)
     for status, res in pending.values():
