@@ -62,8 +62,8 @@ def _check_hessian(h, cfg: QuantConfig) -> None:
             raise ValueError(
                 f"ordering_mode={cfg.ordering_mode} is not supported for solver_mode='chol'")
     elif cfg.solver_mode == "eigh":
-        raise NotImplementedError(
-            "solver_mode='eigh' (gptq_ref.py:95-133) is not implemented by the CUDA path yet")
+        if cfg.ordering_mode not in {"none", "diag_h", "pivot_sqrt_h", "pivot_sqrt_hinv_smallest"}:
+            raise ValueError(f"unsupported ordering_mode={cfg.ordering_mode}")
     else:
         raise ValueError(f"unsupported solver_mode={cfg.solver_mode}")
 
@@ -128,10 +128,55 @@ def factor_hessian_attempt0(h_dev: torch.Tensor, cfg: QuantConfig, want_hd: bool
     return HessianFactor(u, perm, 0, hd), status
 
 
+def _process_hessian_eigh(h, cfg: QuantConfig, panel_size: int):
+    """gptq_ref.py:95-133 on the device.
+
+    The eigendecomposition and the unpivoted reduced QR are cuSOLVER calls
+    (``torch.linalg.eigh`` / ``torch.linalg.qr``); the act-order ranking and
+    the blocked pivoted QR of the pivot_* modes are this library's kernels.
+    ``sqrt_h = sqrt(lam) V^T`` and ``sqrt_hinv = lam^-1/2 V^T`` over the kept
+    eigenpairs (descending, rank from the truncation rule).  For none / diag_h
+    / pivot_sqrt_h the factor is R of ``sqrt_hinv.T[:, perm]``: in reference
+    semantics the permutation indexes the eigen axis and, for rank < n, the
+    gather past the kept columns is clamped to the last one (JAX's rule for
+    out-of-range gathers), which leaves R diagonal in exact arithmetic; in
+    intended semantics it acts on the feature axis, ``sqrt_hinv[:, perm]``,
+    so ``R^T R`` is the permuted pseudo-inverse.  pivot_sqrt_hinv_smallest
+    returns the pivoted QR of ``sqrt_hinv`` itself (rank x n)."""
+    import importlib
+    BQ = importlib.import_module("jax_gptq_b200.pallas.blocked_pivoted_qr")
+    hd = A.to_device(h)
+    n = hd.shape[0]
+    evals, evecs = torch.linalg.eigh(hd)
+    evals, evecs = evals.flip(0), evecs.flip(1)
+    rank = _select_truncation_rank(evals, cfg)
+    lam, v = evals[:rank], evecs[:, :rank]
+    sqrt_h = (torch.sqrt(lam)[:, None] * v.T).contiguous()
+    sqrt_hinv = (torch.pow(lam, -0.5)[:, None] * v.T).contiguous()
+    if cfg.ordering_mode == "pivot_sqrt_hinv_smallest":
+        res = BQ.qrcp(sqrt_hinv, panel_size, "smallest", cfg.semantics)
+        return res.work, res.perm
+    if cfg.ordering_mode == "none":
+        perm = torch.arange(n, dtype=torch.int32, device="cuda")
+    elif cfg.ordering_mode == "diag_h":
+        perm = act_order_perm(hd, "diag_h")
+    else:
+        perm = BQ.qrcp(sqrt_h, panel_size, "largest", cfg.semantics).perm
+    idx = perm.long()
+    if cfg.semantics == "reference":
+        m = sqrt_hinv.T[:, idx.clamp(max=rank - 1)]
+    else:
+        m = sqrt_hinv[:, idx]
+    r = torch.linalg.qr(m.contiguous(), mode="r").R
+    return r.contiguous(), perm
+
+
 def process_hessian(h, cfg: QuantConfig, panel_size: int = 32):
     """gptq_ref.py:44 -- returns ``(h_inv_sqrt, perm)``."""
-    del panel_size  # only the eigh branches use it (gptq_ref.py:120-131)
     _check_hessian(h, cfg)
+    if cfg.solver_mode == "eigh":
+        r, perm = _process_hessian_eigh(h, cfg, panel_size)
+        return A.like_input(r, h), A.like_input(perm, h)
     if cfg.semantics == "reference":
         hd = A.to_device(h)
         perm = act_order_perm(hd, cfg.ordering_mode)

@@ -77,12 +77,65 @@ def check_hessian_args(h: np.ndarray, solver_mode: str, ordering_mode: str) -> N
         raise ValueError(f"unsupported solver_mode={solver_mode}")
 
 
-def process_hessian_reference(h, ordering_mode: str = "none", solver_mode: str = "chol"):
-    """Observed output of gptq_ref.py:61-93: ``(eye(n), perm)``."""
+def process_hessian_reference(h, ordering_mode: str = "none", solver_mode: str = "chol",
+                              truncation_mode: str = "abs", truncation_value: float = 1e-5,
+                              panel_size: int = 32):
+    """Observed output of gptq_ref.py:44-133: ``(eye(n), perm)`` for the
+    Cholesky branch (it always falls back, :85-92), the eigh branch as
+    written otherwise (:95-133, see :func:`process_hessian_eigh`)."""
     h = np.asarray(h)
     check_hessian_args(h, solver_mode, ordering_mode)
+    if solver_mode == "eigh":
+        return process_hessian_eigh(h, ordering_mode, truncation_mode, truncation_value,
+                                    panel_size, semantics="reference")
     perm = act_order_perm(h, ordering_mode)
     return np.eye(h.shape[0], dtype=h.dtype), perm
+
+
+def process_hessian_eigh(h, ordering_mode: str = "none", truncation_mode: str = "abs",
+                         truncation_value: float = 1e-5, panel_size: int = 32,
+                         semantics: str = "reference", dtype=np.float32):
+    """gptq_ref.py:95-133: eigendecomposition, truncation, and an upper factor.
+
+    ``sqrt_h = sqrt(lam) V^T`` and ``sqrt_hinv = lam^-1/2 V^T`` (rank x n, the
+    kept eigenpairs in descending order).  For none / diag_h / pivot_sqrt_h the
+    factor is R of the QR of ``sqrt_hinv.T[:, perm]`` (:112, :117, :122): in
+    ``reference`` semantics exactly that -- the permutation indexes the eigen
+    axis, and for rank < n the gather runs past the kept columns and is
+    clamped to the last one, as JAX clamps out-of-range gathers; in
+    ``intended`` semantics the permutation acts on the feature axis,
+    ``sqrt_hinv[:, perm]``, so that ``R^T R = H^+[perm][:, perm]``.  For
+    pivot_sqrt_hinv_smallest the factor is the blocked pivoted QR of
+    ``sqrt_hinv`` itself (:125-131).  The QR's own semantics follow
+    ``semantics`` (compiled-path quirks for reference)."""
+    from . import qr as oqr
+    h = np.asarray(h, dtype)
+    n = h.shape[0]
+    evals, evecs = np.linalg.eigh(h)
+    evals, evecs = evals[::-1], evecs[:, ::-1]
+    rank = select_truncation_rank(np.asarray(evals, np.float64), truncation_mode,
+                                  truncation_value)
+    lam, v = evals[:rank], evecs[:, :rank]
+    sqrt_h = (np.sqrt(lam)[:, None] * v.T).astype(dtype)
+    sqrt_hinv = (np.power(lam, -0.5)[:, None] * v.T).astype(dtype)
+    compiled = semantics == "reference"
+    if ordering_mode == "pivot_sqrt_hinv_smallest":
+        work, perm = oqr.blocked_pivoted_qr(sqrt_hinv, panel_size, "smallest", compiled=compiled)
+        return np.asarray(work, dtype), np.asarray(perm, np.int32)
+    if ordering_mode == "none":
+        perm = np.arange(n, dtype=np.int32)
+    elif ordering_mode == "diag_h":
+        perm = act_order_perm(h, "diag_h")
+    elif ordering_mode == "pivot_sqrt_h":
+        _, perm = oqr.blocked_pivoted_qr(sqrt_h, panel_size, "largest", compiled=compiled)
+        perm = np.asarray(perm, np.int32)
+    else:
+        raise ValueError(f"unsupported ordering_mode={ordering_mode}")
+    if semantics == "reference":
+        m = sqrt_hinv.T[:, np.clip(perm, 0, rank - 1)]
+    else:
+        m = sqrt_hinv[:, perm]
+    return np.linalg.qr(m, mode="r").astype(dtype), perm
 
 
 def damped_permuted(h: np.ndarray, perm: np.ndarray, damp: float, dtype=np.float64):

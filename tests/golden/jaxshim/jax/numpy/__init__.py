@@ -50,6 +50,30 @@ class _At:
         return _AtIndexer(self._arr, idx)
 
 
+def _clamp_gather(idx, shape):
+    """JAX clamps out-of-range integer-array gathers into bounds (negative
+    indices wrap first); numpy would raise.  Applied to every integer-array
+    component of an index."""
+    parts = idx if isinstance(idx, tuple) else (idx,)
+    out, axis = [], 0
+    for p in parts:
+        if p is None:
+            out.append(p)
+            continue
+        if p is Ellipsis:
+            axis = len(shape) - (len(parts) - len(out) - 1)
+            out.append(p)
+            continue
+        if isinstance(p, _np.ndarray) and p.dtype.kind in "iu" and axis < len(shape):
+            dim = shape[axis]
+            q = _np.where(p < 0, p + dim, p)
+            out.append(_np.clip(q, 0, dim - 1))
+        else:
+            out.append(p)
+        axis += 1
+    return tuple(out) if isinstance(idx, tuple) else out[0]
+
+
 class Array(_np.ndarray):
     """ndarray with JAX's functional update helpers."""
 
@@ -61,7 +85,7 @@ class Array(_np.ndarray):
         return self
 
     def __getitem__(self, idx):
-        out = super().__getitem__(idx)
+        out = super().__getitem__(_clamp_gather(idx, self.shape))
         if isinstance(out, _np.generic):
             return _np.asarray(out).view(Array)
         return out

@@ -169,6 +169,25 @@ def make_qr_cases(jnp, bpq):
     return cases
 
 
+def make_eigh_cases(jnp, ref, gptq_ref):
+    """process_hessian with solver_mode="eigh" (gptq_ref.py:95-133), all four
+    ordering modes, for a full-rank H and a rank-deficient one (fewer tokens
+    than features, so the default truncation drops eigenvalues and the
+    none/diag_h gathers run past the kept columns)."""
+    cases = {}
+    rng = np.random.Generator(np.random.PCG64(102))
+    for name, (n, tokens) in {"full": (48, 400), "deficient": (48, 40)}.items():
+        x = (rng.standard_normal((tokens, n)) * rng.uniform(0.5, 2.0, n)).astype(np.float32)
+        h = (x.T.astype(np.float64) @ x / tokens).astype(np.float32)
+        cases[f"eigh_{name}_h"] = h
+        for mode in ("none", "diag_h", "pivot_sqrt_h", "pivot_sqrt_hinv_smallest"):
+            cfg = ref.QuantConfig(solver_mode="eigh", ordering_mode=mode)
+            r, perm = gptq_ref.process_hessian(jnp.asarray(h), cfg, panel_size=8)
+            cases[f"eigh_{name}_{mode}_r"] = _np(r)
+            cases[f"eigh_{name}_{mode}_perm"] = _np(perm)
+    return cases
+
+
 def main() -> None:
     ap = argparse.ArgumentParser()
     ap.add_argument("--reference-src", default="/root/reference/src")
@@ -179,6 +198,8 @@ def main() -> None:
     np.savez_compressed(os.path.join(args.out, "gptq_golden.npz"),
                         **make_gptq_cases(jnp, ref, gptq_ref))
     np.savez_compressed(os.path.join(args.out, "qr_golden.npz"), **make_qr_cases(jnp, bpq))
+    np.savez_compressed(os.path.join(args.out, "eigh_golden.npz"),
+                        **make_eigh_cases(jnp, ref, gptq_ref))
     print("wrote golden vectors to", args.out)
 
 

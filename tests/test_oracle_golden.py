@@ -168,3 +168,15 @@ def test_intended_qronos_improves_on_rtn():
     def err(w_hat):
         return np.linalg.norm(x.astype(np.float64) @ w.T - xt.astype(np.float64) @ w_hat.T)
     assert err(out["dequant"]) < 0.8 * err(oq.quantize_dequantize(w, 3, 128, False))
+
+
+def test_eigh_branch_matches_reference_golden(golden_dir):
+    """gptq_ref.py:95-133 run by the reference itself (numpy shim): every
+    ordering mode, full-rank and truncated H."""
+    g = _load(golden_dir, "eigh_golden.npz")
+    for name in ("full", "deficient"):
+        h = g[f"eigh_{name}_h"]
+        for mode in ("none", "diag_h", "pivot_sqrt_h", "pivot_sqrt_hinv_smallest"):
+            r, p = og.process_hessian_reference(h, mode, "eigh", panel_size=8)
+            assert np.array_equal(p, g[f"eigh_{name}_{mode}_perm"]), (name, mode)
+            assert np.array_equal(r, g[f"eigh_{name}_{mode}_r"]), (name, mode)
