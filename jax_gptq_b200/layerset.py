@@ -153,7 +153,10 @@ def _split_rows(res: SweepResult, members) -> dict:
 
 
 _SIDE_STREAMS: dict[int, list] = {}
-RESERVED_SMS = 16  # SMs the non-priority groups' persistent kernels leave free
+# SMs that the persistent kernels launched while a higher-priority chain is
+# running leave free to it.  12 on a 148-SM part: the d = 4096 Hessians then
+# run in exactly two waves of 136 tiles.
+RESERVED_SMS = 12
 
 
 def _side_streams(n: int) -> list:
@@ -172,26 +175,35 @@ def _stack(weights: dict, members) -> torch.Tensor:
         torch.cat([weights[name] for name, _ in members], dim=0)
 
 
-def _run_groups_concurrently(hs: dict, work, redo) -> dict:
-    """Per input group, ``work(grp, h) -> (status, result)`` on its own side
-    stream once every H is formed on the current stream; the current stream
-    then waits for all of them.  ``status`` is the device word of the group's
-    first damping attempt; the statuses are read once, and a group whose
-    damped Hessian was not positive definite is recomputed by ``redo(grp, h)``
-    (the retrying, synchronizing path), so the outcome equals the sequential
-    one.  Result tensors are marked as used by the current stream."""
+def _run_groups_concurrently(sizes: dict, form, work, redo) -> dict:
+    """Run each input group's chain on its own side stream.
+
+    ``sizes[grp]`` orders the groups (largest first).  ``form(grp) -> h``
+    runs on the current stream and forms the group's statistics;
+    ``work(grp, h) -> (status, result)`` then runs on the group's side stream
+    as soon as that h is ready, while the current stream goes on to the next
+    group's statistics.  The largest group's chain (the longest) runs on the
+    high-priority stream and starts first; every persistent kernel launched
+    after it leaves ``RESERVED_SMS`` SMs free, so its latency-bound steps
+    overlap the remaining statistics and the other chains.
+
+    ``status`` is the device word of the group's first damping attempt; the
+    statuses are read once at the end, and a group whose damped Hessian was
+    not positive definite is recomputed by ``redo(grp, h)`` (the retrying,
+    synchronizing path), so the outcome equals the sequential one.  Result
+    tensors are marked as used by the current stream, which waits for every
+    side stream before returning."""
     main = torch.cuda.current_stream()
-    streams = _side_streams(len(hs))
-    pending = {}
-    # largest H first, on the high-priority stream: its chain is the longest;
-    # the other groups' persistent kernels leave RESERVED_SMS SMs to it
-    order = sorted(hs, key=lambda g: -hs[g].shape[0])
+    order = sorted(sizes, key=lambda g: -sizes[g])
+    streams = _side_streams(len(order))
     sms = torch.cuda.get_device_properties(main.device).multi_processor_count
     lib = _lib.lib()
+    pending, hs = {}, {}
     for idx, (grp, s) in enumerate(zip(order, streams)):
-        s.wait_stream(main)
         lib.gq_set_cta_budget(0 if idx == 0 else max(1, sms - RESERVED_SMS))
         try:
+            hs[grp] = form(grp)
+            s.wait_stream(main)
             with torch.cuda.stream(s):
                 pending[grp] = work(grp, hs[grp])
         finally:
@@ -219,17 +231,18 @@ def quantize_layer_gptq(weights: dict, inputs: dict, cfg: QuantConfig, shapes=LL
 
     With ``concurrent`` (ignored when ``timed``, whose per-phase events need
     one stream) each input group's factor and sweep run on a stream of their
-    own once every H is formed: one group's latency-bound factor leaves and
-    small GEMMs overlap the other groups' GEMMs and sweeps.
+    own as soon as that group's H is formed, largest group first: its
+    latency-bound factor leaves and small GEMMs overlap the remaining H
+    accumulations and the other groups' GEMMs and sweeps.
     """
     if timed or not concurrent:
         return _quantize_layer_gptq_sequential(weights, inputs, cfg, shapes, timed)
-    hs = {}
-    for grp, x in inputs.items():
+    def form(grp):
+        x = inputs[grp]
         d = x.shape[1]
         h = torch.empty((d, d), dtype=torch.float32, device=x.device)
         stats.syrk_into(h, x, accumulate=False)
-        hs[grp] = h
+        return h
 
     def work(grp, h):
         f, status = factor_hessian_attempt0(h, cfg)
@@ -240,7 +253,8 @@ def quantize_layer_gptq(weights: dict, inputs: dict, cfg: QuantConfig, shapes=LL
         return gptq_sweep(_stack(weights, _members(shapes, grp)), f.u, f.perm, cfg)
 
     results: dict[str, SweepResult] = {}
-    for grp, res in _run_groups_concurrently(hs, work, redo).items():
+    sizes = {grp: x.shape[1] for grp, x in inputs.items()}
+    for grp, res in _run_groups_concurrently(sizes, form, work, redo).items():
         results.update(_split_rows(res, _members(shapes, grp)))
     return results, LayerTimes()
 
@@ -275,14 +289,17 @@ def quantize_layer_qronos(weights: dict, inputs_float: dict, inputs_quant: dict,
     if timed or not concurrent:
         return _quantize_layer_qronos_sequential(weights, inputs_float, inputs_quant, cfg, shapes,
                                                  timed)
-    hs, gs = {}, {}
-    for grp, xq in inputs_quant.items():
+    gs = {}
+
+    def form(grp):
+        xq = inputs_quant[grp]
         d = xq.shape[1]
         h = torch.empty((d, d), dtype=torch.float32, device=xq.device)
         g = torch.empty((d, d), dtype=torch.float32, device=xq.device)
         stats.syrk_into(h, xq, accumulate=False)
         stats.gemm_tn_into(g, inputs_float[grp], xq, accumulate=False)
-        hs[grp], gs[grp] = h, g
+        gs[grp] = g
+        return h
 
     def work(grp, h):
         f, status = factor_hessian_attempt0(h, cfg, want_hd=True)
@@ -295,7 +312,8 @@ def quantize_layer_qronos(weights: dict, inputs_float: dict, inputs_quant: dict,
         return qronos_quantize(w, w, None, gs[grp], cfg, factor=f)
 
     results = {}
-    for grp, res in _run_groups_concurrently(hs, work, redo).items():
+    sizes = {grp: x.shape[1] for grp, x in inputs_quant.items()}
+    for grp, res in _run_groups_concurrently(sizes, form, work, redo).items():
         results.update(_split_rows(res, _members(shapes, grp)))
     return results, LayerTimes()
 

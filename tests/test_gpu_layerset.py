@@ -71,7 +71,8 @@ def test_failed_first_attempt_is_redone():
         return gptq_sweep(w, f.u, f.perm, cfg)
 
     good = torch.eye(n, device="cuda")
-    out = LS._run_groups_concurrently({"bad": h, "good": good}, work, redo)
+    hs = {"bad": h, "good": good}
+    out = LS._run_groups_concurrently({"bad": n, "good": n}, hs.__getitem__, work, redo)
     assert calls == ["bad"]
     f = factor_hessian(h, cfg)
     assert f.attempt >= 1
