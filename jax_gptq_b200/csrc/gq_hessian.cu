@@ -167,69 +167,83 @@ __global__ void damp_permute_rows_kernel(const float* __restrict__ h, int64_t n,
 
 // ---------------------------------------------------------------------------
 // Diagonal blocks of NB x NB are factored and inverted by one 512-thread CTA
-// in shared memory, in four sub-panels of 32 columns (right-looking):
-//   1. warp 0 factors the 32 x 32 diagonal sub-block with lane i holding row i
-//      in registers (columns published by warp shuffles, no block barrier),
-//      then inverts it with lane c solving L x = e_c;
-//   2. all warps form the panel below, L21 = A21 X11^T (X11 = L11^-1);
-//   3. all warps apply the rank-32 trailing update A22 -= L21 L21^T.
-// The 128 x 128 inverse is then completed block row by block row,
-// X_ij = -X_ii sum_k L_ik X_kj.  The block's inverse (not L) is written back:
-// the panel solve below and the triangular inverse of the whole factor only
-// need L^-1 on the diagonal.
+// in shared memory: four 32-column sub-panels, right-looking, with the
+// block's inverse completed along the way, X_ij = -X_ii sum_k L_ik X_kj.
+// Only the inverse is written back: the panel solve of the recursion and the
+// triangular inverse of the whole factor need L^-1 on the diagonal, not L.
+//
+// The 32 pivots of a sub-panel form the serial chain.  Warp 0 factors and
+// inverts each 32 x 32 diagonal sub-block in registers (lane i holds row i;
+// columns published by shuffles) while warps 1-15 do every piece of the
+// parallel work that does not feed the next pivot (look-ahead):
+//   phase p, warp 0:     sub-block p -> X_pp
+//   phase p, warps 1-15: the trailing update from panel p-1 outside block
+//                        column p, W_pj = sum_{k<p} L_pk X_kj, and the global
+//                        stores of finished rows of the inverse;
+//   then all 16 warps:   the panel L_ip = A_ip X_pp^T, X_pj = -X_pp W_pj, and
+//                        the update of the next diagonal sub-block.
+// Every product sums over k in increasing order from zero with fmaf and each
+// block receives the updates of panels 0, 1, ... in order, so the result does
+// not depend on how the work is split between warps.
 constexpr int NB = 128;
 constexpr int SUB = 32;
 constexpr int DIAG_THREADS = 512;
 constexpr int DIAG_WARPS = DIAG_THREADS / 32;
-constexpr int DP = NB + 1;  // shared-memory pitch: row-strided lane reads hit distinct banks
-constexpr size_t DIAG_SMEM = (size_t)(2 * NB + SUB) * DP * sizeof(float) + SUB * sizeof(float);
+constexpr int DP = NB + 1;   // shared-memory pitch: row-strided lane reads hit distinct banks
+constexpr int LTP = SUB + 4;  // pitch of the transposed sub-block (rows 16-byte aligned)
+constexpr size_t DIAG_SMEM = ((size_t)(2 * NB + SUB) * DP + (size_t)SUB * LTP) * sizeof(float);
 
-// acc[q][s] = sum_{k < K} A[r_q DP + k] * B(k, lane + 32s) for rows r_q = r0 + rstride * q
-// below M and s < ns, where B(k, c) = B[c DP + k] (NT) or B[k DP + c] (NN).  Row reads
-// are warp broadcasts; column reads are lane-contiguous (NN) or lane-strided by the odd
-// pitch (NT).  Sums run over k in increasing order.
-template <bool NT>
-__device__ __forceinline__ void smem_mm(const float* A, const float* B, int M, int ns, int K,
-                                        float (&acc)[6][3], int r0, int rstride) {
+// acc[q][s] = sum_{k0 <= k < k1} A(r_q, k) B(k, c_s) for the rows r_q = w + nw q
+// (q < QN, r_q < nrows) and columns c_s = lane + 32 s, with A(r, k) = A[r DP + k]
+// and B(k, c) = B[c DP + k] (NT) or B[k DP + c] (NN).  Row reads are warp
+// broadcasts; column reads are lane-contiguous (NN) or lane-strided by the odd
+// pitch (NT), so no access has a bank conflict.
+template <bool NT, int QN, int NS>
+__device__ __forceinline__ void bprod(const float* __restrict__ A, const float* __restrict__ B,
+                                      int nrows, int w, int nw, int k0, int k1,
+                                      float (&acc)[QN][NS]) {
   const int lane = threadIdx.x & 31;
 #pragma unroll
-  for (int q = 0; q < 6; ++q)
+  for (int q = 0; q < QN; ++q)
 #pragma unroll
-    for (int s = 0; s < 3; ++s) acc[q][s] = 0.f;
+    for (int s = 0; s < NS; ++s) acc[q][s] = 0.f;
 #pragma unroll 4
-  for (int k = 0; k < K; ++k) {
-    float b[3];
+  for (int k = k0; k < k1; ++k) {
+    float b[NS];
 #pragma unroll
-    for (int s = 0; s < 3; ++s) {
+    for (int s = 0; s < NS; ++s) {
       const int c = lane + 32 * s;
-      b[s] = (s < ns) ? (NT ? B[c * DP + k] : B[k * DP + c]) : 0.f;
+      b[s] = NT ? B[c * DP + k] : B[k * DP + c];
     }
 #pragma unroll
-    for (int q = 0; q < 6; ++q) {
-      const int r = r0 + rstride * q;
-      if (r < M) {
+    for (int q = 0; q < QN; ++q) {
+      const int r = w + nw * q;
+      if (r < nrows) {
         const float av = A[r * DP + k];
 #pragma unroll
-        for (int s = 0; s < 3; ++s) acc[q][s] = fmaf(av, b[s], acc[q][s]);
+        for (int s = 0; s < NS; ++s) acc[q][s] = fmaf(av, b[s], acc[q][s]);
       }
     }
   }
 }
 
-// Warp-level Cholesky + inverse of the 32 x 32 sub-block at S[c0][c0]: L goes
-// back to S, L^-1 to X.  rdiag: 32 floats of scratch.  Returns true (uniform)
-// if a pivot was not > 0 or not finite; that pivot is replaced by 1.
-__device__ bool sub_factor(float* S, float* X, float* rdiag, int c0) {
+// Warp-level Cholesky + inverse of a 32 x 32 block held as r (lane i: row i,
+// lower part; the upper part is ignored).  L^-1 goes to xd (pitch DP, zeros
+// above the diagonal); lt is 32 x LTP floats of scratch (16-byte aligned).
+// The diagonal is replicated in every lane and updated with the same fmaf
+// sequence as its own row, so a pivot is available without a shuffle.
+// Returns true (uniform) if a pivot was not > 0 or not finite; that pivot is
+// replaced by 1.
+__device__ bool sub_factor(float (&r)[SUB], float* xd, float* lt) {
   const unsigned FULL = 0xffffffffu;
   const int lane = threadIdx.x & 31;
-  float r[SUB];
+  float dg[SUB], rinv[SUB];
 #pragma unroll
-  for (int k = 0; k < SUB; ++k) r[k] = S[(c0 + lane) * DP + c0 + k];
+  for (int k = 0; k < SUB; ++k) dg[k] = __shfl_sync(FULL, r[k], k);
   bool bad = false;
-  float my_rinv = 1.f;
 #pragma unroll
   for (int j = 0; j < SUB; ++j) {
-    float djj = __shfl_sync(FULL, r[j], j);
+    float djj = dg[j];
     if (!(djj > 0.f) || !isfinite(djj)) {
       bad = true;
       djj = 1.f;
@@ -237,132 +251,293 @@ __device__ bool sub_factor(float* S, float* X, float* rdiag, int c0) {
     // rsqrtf (2 ulp) keeps the serial pivot chain short; the factor's own
     // float32 rounding error is orders of magnitude larger
     const float rl = rsqrtf(djj);
-    const float ljj = djj * rl;
-    if (lane == j) my_rinv = rl;
-    const float lij = (lane < j) ? 0.f : ((lane == j) ? ljj : r[j] * rl);
+    rinv[j] = rl;
+    const float lij = (lane < j) ? 0.f : ((lane == j) ? djj * rl : r[j] * rl);
     r[j] = lij;
 #pragma unroll
-    for (int k = j + 1; k < SUB; ++k) r[k] = fmaf(-lij, __shfl_sync(FULL, lij, k), r[k]);
+    for (int k = j + 1; k < SUB; ++k) {
+      const float lkj = __shfl_sync(FULL, lij, k);
+      r[k] = fmaf(-lij, lkj, r[k]);
+      dg[k] = fmaf(-lkj, lkj, dg[k]);
+    }
   }
+  // L transposed, so that a column of L is one run of float4 broadcasts
 #pragma unroll
-  for (int k = 0; k < SUB; ++k) S[(c0 + lane) * DP + c0 + k] = r[k];
-  rdiag[lane] = my_rinv;
+  for (int k = 0; k < SUB; ++k) lt[k * LTP + lane] = r[k];
   __syncwarp();
-  // column `lane` of L^-1 by right-looking forward substitution: once x[k]
-  // is final it is removed from every later row (L columns read as
-  // broadcasts).  Each x[i] receives the same fmaf sequence as a dot product
-  // over k < i would, but the dependent chain is one fmaf + one multiply per
-  // column instead of the whole dot product.
+  // column `lane` of L^-1 by right-looking forward substitution: once x[k] is
+  // final it is removed from every later row
   float x[SUB];
 #pragma unroll
   for (int i = 0; i < SUB; ++i) x[i] = (i == lane) ? 1.f : 0.f;
 #pragma unroll
   for (int k = 0; k < SUB; ++k) {
-    x[k] = x[k] * rdiag[k];
+    x[k] = x[k] * rinv[k];
+    const float4* col = reinterpret_cast<const float4*>(lt + k * LTP);
 #pragma unroll
-    for (int i = k + 1; i < SUB; ++i) x[i] = fmaf(-S[(c0 + i) * DP + c0 + k], x[k], x[i]);
+    for (int g = (k + 1) / 4; g < SUB / 4; ++g) {
+      const float4 l4 = col[g];
+      const float lv[4] = {l4.x, l4.y, l4.z, l4.w};
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const int i = 4 * g + e;
+        if (i > k) x[i] = fmaf(-lv[e], x[k], x[i]);
+      }
+    }
   }
 #pragma unroll
-  for (int i = 0; i < SUB; ++i) X[(c0 + i) * DP + c0 + lane] = x[i];
+  for (int i = 0; i < SUB; ++i) xd[i * DP + lane] = x[i];
+  __syncwarp();
   return bad;
+}
+
+// Rows [32 rb, 32 rb + 32) of the block's inverse to global memory (zeros
+// above the diagonal), by threads t0 .. t0 + nt - 1.
+__device__ __forceinline__ void store_inverse_rows(float* __restrict__ a, int64_t lda, int kb,
+                                                   bool vec, const float* X, int rb, int t,
+                                                   int nt) {
+  if (vec) {
+    for (int e4 = t; e4 < SUB * NB / 4; e4 += nt) {
+      const int r = SUB * rb + (e4 >> 5), c = (e4 & 31) << 2;
+      float4 v;
+      v.x = (c + 0 <= r) ? X[r * DP + c + 0] : 0.f;
+      v.y = (c + 1 <= r) ? X[r * DP + c + 1] : 0.f;
+      v.z = (c + 2 <= r) ? X[r * DP + c + 2] : 0.f;
+      v.w = (c + 3 <= r) ? X[r * DP + c + 3] : 0.f;
+      *reinterpret_cast<float4*>(a + (int64_t)r * lda + c) = v;
+    }
+  } else {
+    for (int e = t; e < SUB * NB; e += nt) {
+      const int r = SUB * rb + e / NB, c = e % NB;
+      if (r < kb && c < kb) a[(int64_t)r * lda + c] = (c <= r) ? X[r * DP + c] : 0.f;
+    }
+  }
 }
 
 // Cholesky of the kb x kb lower block at a (ld lda); a receives L^-1 (strict
 // upper part zeroed).  Rows/columns beyond kb are treated as identity.
 __global__ void __launch_bounds__(DIAG_THREADS)
 potrf_diag_kernel(float* __restrict__ a, int64_t lda, int kb, int* __restrict__ status) {
-  extern __shared__ float smem[];
-  float* S = smem;               // NB x DP: the block, becoming L
-  float* X = S + NB * DP;        // NB x DP: L^-1
-  float* W = X + NB * DP;        // SUB x DP: block-row products of the inverse
-  float* rdiag = W + SUB * DP;   // SUB
-  __shared__ int bad;
+  extern __shared__ __align__(16) float smem[];
+  float* S = smem;               // NB x DP: the block; off-diagonal blocks become L
+  float* X = S + NB * DP;        // NB x DP: L^-1 (blocks above the diagonal never written)
+  float* Wb = X + NB * DP;       // SUB x DP: W_pj = sum_k L_pk X_kj of the current block row
+  float* lt = Wb + SUB * DP;     // SUB x LTP: warp 0's transposed sub-block
   const int w = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  if (threadIdx.x == 0) bad = 0;
-  // block -> shared memory with every global load of a thread in flight at once
-  constexpr int PER_THREAD = NB * NB / DIAG_THREADS;  // 32
-  if (kb == NB && (lda & 3) == 0 && (reinterpret_cast<uintptr_t>(a) & 15) == 0) {
-    float4 v[PER_THREAD / 4];
+  const bool vec = kb == NB && (lda & 3) == 0 && (reinterpret_cast<uintptr_t>(a) & 15) == 0;
+  const int lw = w - 1, LW = DIAG_WARPS - 1;  // look-ahead warp index and count
+  const int lt_thread = threadIdx.x - 32, LT_THREADS = DIAG_THREADS - 32;
+  bool bad = false;  // warp 0 only
+  float r[SUB];
+  float acc6[6][1], acc5[5][3], acc3[3][2], acc2[2][1], acc2b[2][2], acc2c[2][3], acc3b[3][1];
+
+  // ---- phase 0: warp 0 loads and factors sub-block 0 while warps 1-15 load rows 32..127
+  if (w == 0) {
+    if (vec) {
 #pragma unroll
-    for (int it = 0; it < PER_THREAD / 4; ++it) {
-      const int e4 = threadIdx.x + it * DIAG_THREADS;  // float4 index, 32 per row
-      v[it] = *reinterpret_cast<const float4*>(a + (int64_t)(e4 >> 5) * lda + ((e4 & 31) << 2));
+      for (int g = 0; g < SUB / 4; ++g) {
+        const float4 v = *reinterpret_cast<const float4*>(a + (int64_t)lane * lda + 4 * g);
+        r[4 * g + 0] = (4 * g + 0 <= lane) ? v.x : 0.f;
+        r[4 * g + 1] = (4 * g + 1 <= lane) ? v.y : 0.f;
+        r[4 * g + 2] = (4 * g + 2 <= lane) ? v.z : 0.f;
+        r[4 * g + 3] = (4 * g + 3 <= lane) ? v.w : 0.f;
+      }
+    } else {
+#pragma unroll
+      for (int k = 0; k < SUB; ++k)
+        r[k] = (lane < kb && k < kb) ? ((k <= lane) ? a[(int64_t)lane * lda + k] : 0.f)
+                                     : ((lane == k) ? 1.f : 0.f);
+    }
+    bad |= sub_factor(r, X, lt);
+  } else if (vec) {
+    constexpr int N4 = (NB - SUB) * NB / 4;  // float4s in rows 32..127
+    constexpr int IT = (N4 + DIAG_THREADS - 32 - 1) / (DIAG_THREADS - 32);
+    float4 v[IT];
+#pragma unroll
+    for (int it = 0; it < IT; ++it) {
+      const int e4 = lt_thread + it * LT_THREADS;
+      if (e4 < N4)
+        v[it] = *reinterpret_cast<const float4*>(a + (int64_t)(SUB + (e4 >> 5)) * lda +
+                                                 ((e4 & 31) << 2));
     }
 #pragma unroll
-    for (int it = 0; it < PER_THREAD / 4; ++it) {
-      const int e4 = threadIdx.x + it * DIAG_THREADS;
-      const int r = e4 >> 5, c = (e4 & 31) << 2;
-      S[r * DP + c + 0] = (c + 0 <= r) ? v[it].x : 0.f;
-      S[r * DP + c + 1] = (c + 1 <= r) ? v[it].y : 0.f;
-      S[r * DP + c + 2] = (c + 2 <= r) ? v[it].z : 0.f;
-      S[r * DP + c + 3] = (c + 3 <= r) ? v[it].w : 0.f;
+    for (int it = 0; it < IT; ++it) {
+      const int e4 = lt_thread + it * LT_THREADS;
+      if (e4 < N4) {
+        const int rr = SUB + (e4 >> 5), c = (e4 & 31) << 2;
+        S[rr * DP + c + 0] = (c + 0 <= rr) ? v[it].x : 0.f;
+        S[rr * DP + c + 1] = (c + 1 <= rr) ? v[it].y : 0.f;
+        S[rr * DP + c + 2] = (c + 2 <= rr) ? v[it].z : 0.f;
+        S[rr * DP + c + 3] = (c + 3 <= rr) ? v[it].w : 0.f;
+      }
     }
   } else {
-    float v[PER_THREAD];
-#pragma unroll
-    for (int it = 0; it < PER_THREAD; ++it) {
-      const int e = threadIdx.x + it * DIAG_THREADS, r = e / NB, c = e % NB;
-      v[it] = (r < kb && c <= r) ? a[r * lda + c] : 0.f;
-    }
-#pragma unroll
-    for (int it = 0; it < PER_THREAD; ++it) {
-      const int e = threadIdx.x + it * DIAG_THREADS, r = e / NB, c = e % NB;
-      S[r * DP + c] = (r < kb && c < kb) ? v[it] : ((r == c) ? 1.f : 0.f);
+    for (int e = lt_thread; e < (NB - SUB) * NB; e += LT_THREADS) {
+      const int rr = SUB + e / NB, c = e % NB;
+      const float v = (rr < kb && c <= rr) ? a[(int64_t)rr * lda + c] : 0.f;
+      S[rr * DP + c] = (rr < kb && c < kb) ? v : ((rr == c) ? 1.f : 0.f);
     }
   }
-#pragma unroll 8
-  for (int e = threadIdx.x; e < NB * NB; e += DIAG_THREADS) X[(e / NB) * DP + e % NB] = 0.f;
   __syncthreads();
-  float acc[6][3];
-  for (int c0 = 0; c0 < NB; c0 += SUB) {
-    if (w == 0) {
-      if (sub_factor(S, X, rdiag, c0) && lane == 0) bad = 1;
-    }
-    __syncthreads();
-    const int m = NB - c0 - SUB;
-    if (m == 0) break;
-    float* panel = S + (c0 + SUB) * DP + c0;
-    // L21 = A21 X11^T
-    smem_mm<true>(panel, X + c0 * DP + c0, m, 1, SUB, acc, w, DIAG_WARPS);
-    __syncthreads();
+  // panel 0: L_i0 = A_i0 X_00^T (rows 32..127)
+  bprod<true, 6, 1>(S + SUB * DP, X, NB - SUB, w, DIAG_WARPS, 0, SUB, acc6);
+  __syncwarp();
 #pragma unroll
-    for (int q = 0; q < 6; ++q)
-      if (w + DIAG_WARPS * q < m) panel[(w + DIAG_WARPS * q) * DP + lane] = acc[q][0];
-    __syncthreads();
-    // A22 -= L21 L21^T (lower part)
-    smem_mm<true>(panel, panel, m, m / 32, SUB, acc, w, DIAG_WARPS);
-    float* a22 = panel + SUB;
+  for (int q = 0; q < 6; ++q) {
+    const int rr = w + DIAG_WARPS * q;
+    if (rr < NB - SUB) S[(SUB + rr) * DP + lane] = acc6[q][0];
+  }
+  __syncthreads();
+  // A_11 -= L_10 L_10^T
+  bprod<true, 2, 1>(S + SUB * DP, S + SUB * DP, SUB, w, DIAG_WARPS, 0, SUB, acc2);
 #pragma unroll
-    for (int q = 0; q < 6; ++q)
+  for (int q = 0; q < 2; ++q) {
+    const int rr = w + DIAG_WARPS * q;
+    if (lane <= rr) S[(SUB + rr) * DP + SUB + lane] -= acc2[q][0];
+  }
+  __syncthreads();
+
+  // ---- phase 1
+  if (w == 0) {
+#pragma unroll
+    for (int k = 0; k < SUB; ++k) r[k] = S[(SUB + lane) * DP + SUB + k];
+    bad |= sub_factor(r, X + SUB * DP + SUB, lt);
+  } else {
+    // rows 64..127, columns 32..127: A -= L_i0 L_j0^T (lower part)
+    bprod<true, 5, 3>(S + 2 * SUB * DP, S + SUB * DP, 2 * SUB, lw, LW, 0, SUB, acc5);
+#pragma unroll
+    for (int q = 0; q < 5; ++q)
 #pragma unroll
       for (int s = 0; s < 3; ++s) {
-        const int r = w + DIAG_WARPS * q, c = lane + 32 * s;
-        if (r < m && s < m / 32 && c <= r) a22[r * DP + c] -= acc[q][s];
+        const int rr = lw + LW * q, c = lane + 32 * s;
+        if (rr < 2 * SUB && SUB + c <= 2 * SUB + rr) S[(2 * SUB + rr) * DP + SUB + c] -= acc5[q][s];
       }
-    __syncthreads();
+    // W_10 = L_10 X_00
+    bprod<false, 3, 1>(S + SUB * DP, X, SUB, lw, LW, 0, SUB, acc3b);
+#pragma unroll
+    for (int q = 0; q < 3; ++q) {
+      const int rr = lw + LW * q;
+      if (rr < SUB) Wb[rr * DP + lane] = acc3b[q][0];
+    }
   }
-  // off-diagonal blocks of L^-1, block row by block row
-  for (int i = 1; i < NB / SUB; ++i) {
-    smem_mm<false>(S + SUB * i * DP, X, SUB, i, SUB * i, acc, w, DIAG_WARPS);  // W = L[i, :i] X[:i, :i]
+  __syncthreads();
+  // panel 1: L_i1 = A_i1 X_11^T (rows 64..127); X_10 = -X_11 W_10
+  {
+    float acc4[4][1];
+    bprod<true, 4, 1>(S + 2 * SUB * DP, X + SUB * DP, 2 * SUB, w, DIAG_WARPS, SUB, 2 * SUB, acc4);
+    __syncwarp();
 #pragma unroll
-    for (int q = 0; q < 2; ++q)
-#pragma unroll
-      for (int s = 0; s < 3; ++s)
-        if (s < i) W[(w + DIAG_WARPS * q) * DP + lane + 32 * s] = acc[q][s];
-    __syncthreads();
-    smem_mm<false>(X + SUB * i * DP + SUB * i, W, SUB, i, SUB, acc, w, DIAG_WARPS);  // -X_ii W
-#pragma unroll
-    for (int q = 0; q < 2; ++q)
-#pragma unroll
-      for (int s = 0; s < 3; ++s)
-        if (s < i) X[(SUB * i + w + DIAG_WARPS * q) * DP + lane + 32 * s] = -acc[q][s];
-    __syncthreads();
+    for (int q = 0; q < 4; ++q) {
+      const int rr = w + DIAG_WARPS * q;
+      if (rr < 2 * SUB) S[(2 * SUB + rr) * DP + SUB + lane] = acc4[q][0];
+    }
   }
-  for (int e = threadIdx.x; e < NB * NB; e += DIAG_THREADS) {
-    const int r = e / NB, c = e % NB;
-    if (r < kb && c < kb) a[r * lda + c] = (c <= r) ? X[r * DP + c] : 0.f;
+  bprod<false, 2, 1>(X + SUB * DP + SUB, Wb, SUB, w, DIAG_WARPS, 0, SUB, acc2);
+#pragma unroll
+  for (int q = 0; q < 2; ++q) {
+    const int rr = w + DIAG_WARPS * q;
+    X[(SUB + rr) * DP + lane] = -acc2[q][0];
   }
-  if (threadIdx.x == 0 && bad) atomicExch(status, GQ_DEVERR_NOTPD);
+  __syncthreads();
+  // A_22 -= L_21 L_21^T
+  bprod<true, 2, 1>(S + 2 * SUB * DP, S + 2 * SUB * DP, SUB, w, DIAG_WARPS, SUB, 2 * SUB, acc2);
+#pragma unroll
+  for (int q = 0; q < 2; ++q) {
+    const int rr = w + DIAG_WARPS * q;
+    if (lane <= rr) S[(2 * SUB + rr) * DP + 2 * SUB + lane] -= acc2[q][0];
+  }
+  __syncthreads();
+
+  // ---- phase 2
+  if (w == 0) {
+#pragma unroll
+    for (int k = 0; k < SUB; ++k) r[k] = S[(2 * SUB + lane) * DP + 2 * SUB + k];
+    bad |= sub_factor(r, X + 2 * SUB * DP + 2 * SUB, lt);
+  } else {
+    // rows 96..127, columns 64..127: A -= L_i1 L_j1^T (lower part)
+    bprod<true, 3, 2>(S + 3 * SUB * DP, S + 2 * SUB * DP, SUB, lw, LW, SUB, 2 * SUB, acc3);
+#pragma unroll
+    for (int q = 0; q < 3; ++q)
+#pragma unroll
+      for (int s = 0; s < 2; ++s) {
+        const int rr = lw + LW * q, c = lane + 32 * s;
+        if (rr < SUB && c <= SUB + rr) S[(3 * SUB + rr) * DP + 2 * SUB + c] -= acc3[q][s];
+      }
+    // W_20 = L_20 X_00 + L_21 X_10, W_21 = L_21 X_11
+    bprod<false, 3, 1>(S + 2 * SUB * DP, X, SUB, lw, LW, 0, 2 * SUB, acc3b);
+#pragma unroll
+    for (int q = 0; q < 3; ++q) {
+      const int rr = lw + LW * q;
+      if (rr < SUB) Wb[rr * DP + lane] = acc3b[q][0];
+    }
+    bprod<false, 3, 1>(S + 2 * SUB * DP, X + SUB, SUB, lw, LW, SUB, 2 * SUB, acc3b);
+#pragma unroll
+    for (int q = 0; q < 3; ++q) {
+      const int rr = lw + LW * q;
+      if (rr < SUB) Wb[rr * DP + SUB + lane] = acc3b[q][0];
+    }
+    // rows 0..63 of the inverse are final
+    store_inverse_rows(a, lda, kb, vec, X, 0, lt_thread, LT_THREADS);
+    store_inverse_rows(a, lda, kb, vec, X, 1, lt_thread, LT_THREADS);
+  }
+  __syncthreads();
+  // panel 2: L_32 = A_32 X_22^T; X_2j = -X_22 W_2j (j = 0, 1)
+  bprod<true, 2, 1>(S + 3 * SUB * DP, X + 2 * SUB * DP, SUB, w, DIAG_WARPS, 2 * SUB, 3 * SUB, acc2);
+  __syncwarp();
+#pragma unroll
+  for (int q = 0; q < 2; ++q) {
+    const int rr = w + DIAG_WARPS * q;
+    S[(3 * SUB + rr) * DP + 2 * SUB + lane] = acc2[q][0];
+  }
+  bprod<false, 2, 2>(X + 2 * SUB * DP + 2 * SUB, Wb, SUB, w, DIAG_WARPS, 0, SUB, acc2b);
+#pragma unroll
+  for (int q = 0; q < 2; ++q)
+#pragma unroll
+    for (int s = 0; s < 2; ++s) {
+      const int rr = w + DIAG_WARPS * q;
+      X[(2 * SUB + rr) * DP + lane + 32 * s] = -acc2b[q][s];
+    }
+  __syncthreads();
+  // A_33 -= L_32 L_32^T
+  bprod<true, 2, 1>(S + 3 * SUB * DP, S + 3 * SUB * DP, SUB, w, DIAG_WARPS, 2 * SUB, 3 * SUB, acc2);
+#pragma unroll
+  for (int q = 0; q < 2; ++q) {
+    const int rr = w + DIAG_WARPS * q;
+    if (lane <= rr) S[(3 * SUB + rr) * DP + 3 * SUB + lane] -= acc2[q][0];
+  }
+  __syncthreads();
+
+  // ---- phase 3
+  if (w == 0) {
+#pragma unroll
+    for (int k = 0; k < SUB; ++k) r[k] = S[(3 * SUB + lane) * DP + 3 * SUB + k];
+    bad |= sub_factor(r, X + 3 * SUB * DP + 3 * SUB, lt);
+  } else {
+    // W_3j = sum_{j <= k < 3} L_3k X_kj
+#pragma unroll
+    for (int j = 0; j < 3; ++j) {
+      bprod<false, 3, 1>(S + 3 * SUB * DP, X + SUB * j, SUB, lw, LW, SUB * j, 3 * SUB, acc3b);
+#pragma unroll
+      for (int q = 0; q < 3; ++q) {
+        const int rr = lw + LW * q;
+        if (rr < SUB) Wb[rr * DP + SUB * j + lane] = acc3b[q][0];
+      }
+    }
+    store_inverse_rows(a, lda, kb, vec, X, 2, lt_thread, LT_THREADS);
+  }
+  __syncthreads();
+  // X_3j = -X_33 W_3j (j = 0, 1, 2)
+  bprod<false, 2, 3>(X + 3 * SUB * DP + 3 * SUB, Wb, SUB, w, DIAG_WARPS, 0, SUB, acc2c);
+#pragma unroll
+  for (int q = 0; q < 2; ++q)
+#pragma unroll
+    for (int s = 0; s < 3; ++s) {
+      const int rr = w + DIAG_WARPS * q;
+      X[(3 * SUB + rr) * DP + lane + 32 * s] = -acc2c[q][s];
+    }
+  __syncthreads();
+  store_inverse_rows(a, lda, kb, vec, X, 3, threadIdx.x, DIAG_THREADS);
+  if (w == 0 && lane == 0 && bad) atomicExch(status, GQ_DEVERR_NOTPD);
 }
 
 // u[i][j] = linv[n-1-i][n-1-j], one block per row (both sides coalesced)
