@@ -174,10 +174,11 @@ __global__ void damp_permute_rows_kernel(const float* __restrict__ h, int64_t n,
 //
 // The 32 pivots of a sub-panel form the serial chain.  Warp 0 factors and
 // inverts each 32 x 32 diagonal sub-block in registers (lane i holds row i;
-// columns published by shuffles) while warps 1-15 do every piece of the
-// parallel work that does not feed the next pivot (look-ahead):
+// columns published through shared memory) while the 12 warps that do not
+// share its scheduler do every piece of the parallel work that does not feed
+// the next pivot (look-ahead):
 //   phase p, warp 0:     sub-block p -> X_pp
-//   phase p, warps 1-15: the trailing update from panel p-1 outside block
+//   phase p, 12 warps:   the trailing update from panel p-1 outside block
 //                        column p, W_pj = sum_{k<p} L_pk X_kj, and the global
 //                        stores of finished rows of the inverse;
 //   then all 16 warps:   the panel L_ip = A_ip X_pp^T, X_pj = -X_pp W_pj, and
@@ -191,7 +192,7 @@ constexpr int DIAG_THREADS = 512;
 constexpr int DIAG_WARPS = DIAG_THREADS / 32;
 constexpr int DP = NB + 1;   // shared-memory pitch: row-strided lane reads hit distinct banks
 constexpr int LTP = SUB + 4;  // pitch of the transposed sub-block (rows 16-byte aligned)
-constexpr size_t DIAG_SMEM = ((size_t)(2 * NB + SUB) * DP + (size_t)SUB * LTP) * sizeof(float);
+constexpr size_t DIAG_SMEM = ((size_t)(2 * NB + SUB) * DP + (size_t)SUB * LTP + 3 * SUB) * sizeof(float);
 
 // acc[q][s] = sum_{k0 <= k < k1} A(r_q, k) B(k, c_s) for the rows r_q = w + nw q
 // (q < QN, r_q < nrows) and columns c_s = lane + 32 s, with A(r, k) = A[r DP + k]
@@ -229,20 +230,38 @@ __device__ __forceinline__ void bprod(const float* __restrict__ A, const float* 
 
 // Warp-level Cholesky + inverse of a 32 x 32 block held as r (lane i: row i,
 // lower part; the upper part is ignored).  L^-1 goes to xd (pitch DP, zeros
-// above the diagonal); lt is 32 x LTP floats of scratch (16-byte aligned).
-// The diagonal is replicated in every lane and updated with the same fmaf
-// sequence as its own row, so a pivot is available without a shuffle.
+// above the diagonal).  Scratch (16-byte aligned): lt, 32 x LTP floats; cb,
+// 2 x 32 floats; rdiag, 32 floats.
+// Column j of the trailing matrix is published in cb as soon as it is final
+// (one pivot ahead) and read back as float4 broadcasts, so each lane forms
+// the whole column of L itself, l_kj = a_kj / l_jj.  The diagonal is
+// replicated in every lane and updated with the same fmaf sequence as its own
+// row, so the pivot chain is rsqrt -> multiply -> fmaf per column, with no
+// shuffle or shared-memory round trip on it.
 // Returns true (uniform) if a pivot was not > 0 or not finite; that pivot is
 // replaced by 1.
-__device__ bool sub_factor(float (&r)[SUB], float* xd, float* lt) {
+__device__ bool sub_factor(float (&r)[SUB], float* xd, float* lt, float* cb, float* rdiag) {
   const unsigned FULL = 0xffffffffu;
   const int lane = threadIdx.x & 31;
-  float dg[SUB], rinv[SUB];
+  float dg[SUB];
 #pragma unroll
   for (int k = 0; k < SUB; ++k) dg[k] = __shfl_sync(FULL, r[k], k);
+  cb[lane] = r[0];
+  __syncwarp();
   bool bad = false;
 #pragma unroll
   for (int j = 0; j < SUB; ++j) {
+    // column j (rows below the pivot), published during the previous pivot
+    float cv[SUB];
+    const float4* c4 = reinterpret_cast<const float4*>(cb + (j & 1) * SUB);
+#pragma unroll
+    for (int g = (j + 1) / 4; g < SUB / 4; ++g) {
+      const float4 v = c4[g];
+      cv[4 * g + 0] = v.x;
+      cv[4 * g + 1] = v.y;
+      cv[4 * g + 2] = v.z;
+      cv[4 * g + 3] = v.w;
+    }
     float djj = dg[j];
     if (!(djj > 0.f) || !isfinite(djj)) {
       bad = true;
@@ -251,14 +270,23 @@ __device__ bool sub_factor(float (&r)[SUB], float* xd, float* lt) {
     // rsqrtf (2 ulp) keeps the serial pivot chain short; the factor's own
     // float32 rounding error is orders of magnitude larger
     const float rl = rsqrtf(djj);
-    rinv[j] = rl;
+    if (lane == 0) rdiag[j] = rl;
     const float lij = (lane < j) ? 0.f : ((lane == j) ? djj * rl : r[j] * rl);
     r[j] = lij;
+    if (j + 1 < SUB) {
+      // the next pivot first, then publish column j + 1 (final in every lane)
+      const float l1 = cv[j + 1] * rl;
+      dg[j + 1] = fmaf(-l1, l1, dg[j + 1]);
+      r[j + 1] = fmaf(-lij, l1, r[j + 1]);
+      // double-buffered: this buffer's previous readers are past the last __syncwarp
+      cb[((j + 1) & 1) * SUB + lane] = r[j + 1];
+      __syncwarp();
 #pragma unroll
-    for (int k = j + 1; k < SUB; ++k) {
-      const float lkj = __shfl_sync(FULL, lij, k);
-      r[k] = fmaf(-lij, lkj, r[k]);
-      dg[k] = fmaf(-lkj, lkj, dg[k]);
+      for (int k = j + 2; k < SUB; ++k) {
+        const float lkj = cv[k] * rl;
+        dg[k] = fmaf(-lkj, lkj, dg[k]);
+        r[k] = fmaf(-lij, lkj, r[k]);
+      }
     }
   }
   // L transposed, so that a column of L is one run of float4 broadcasts
@@ -272,7 +300,7 @@ __device__ bool sub_factor(float (&r)[SUB], float* xd, float* lt) {
   for (int i = 0; i < SUB; ++i) x[i] = (i == lane) ? 1.f : 0.f;
 #pragma unroll
   for (int k = 0; k < SUB; ++k) {
-    x[k] = x[k] * rinv[k];
+    x[k] = x[k] * rdiag[k];
     const float4* col = reinterpret_cast<const float4*>(lt + k * LTP);
 #pragma unroll
     for (int g = (k + 1) / 4; g < SUB / 4; ++g) {
@@ -323,13 +351,22 @@ potrf_diag_kernel(float* __restrict__ a, int64_t lda, int kb, int* __restrict__ 
   float* X = S + NB * DP;        // NB x DP: L^-1 (blocks above the diagonal never written)
   float* Wb = X + NB * DP;       // SUB x DP: W_pj = sum_k L_pk X_kj of the current block row
   float* lt = Wb + SUB * DP;     // SUB x LTP: warp 0's transposed sub-block
+  float* cb = lt + SUB * LTP;    // 2 x SUB: warp 0's published pivot columns
+  float* rdiag = cb + 2 * SUB;   // SUB: reciprocal pivots
   const int w = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const bool vec = kb == NB && (lda & 3) == 0 && (reinterpret_cast<uintptr_t>(a) & 15) == 0;
-  const int lw = w - 1, LW = DIAG_WARPS - 1;  // look-ahead warp index and count
-  const int lt_thread = threadIdx.x - 32, LT_THREADS = DIAG_THREADS - 32;
+  // look-ahead warps: every warp not on warp 0's scheduler (warps 4, 8, 12
+  // share it), so the pivot chain is never waiting for an issue slot
+  const bool la = (w & 3) != 0;
+  const int lw = w - 1 - (w >> 2);
+  constexpr int LW = DIAG_WARPS - DIAG_WARPS / 4;
+  const int lt_thread = lw * 32 + lane;
+  constexpr int LT_THREADS = 32 * LW;
+  const int ld_thread = threadIdx.x - 32;  // warps 1-15 load rows 32..127
+  constexpr int LD_THREADS = DIAG_THREADS - 32;
   bool bad = false;  // warp 0 only
   float r[SUB];
-  float acc6[6][1], acc5[5][3], acc3[3][2], acc2[2][1], acc2b[2][2], acc2c[2][3], acc3b[3][1];
+  float acc6[6][1], acc6c[6][3], acc3[3][2], acc2[2][1], acc2b[2][2], acc2c[2][3], acc3b[3][1];
 
   // ---- phase 0: warp 0 loads and factors sub-block 0 while warps 1-15 load rows 32..127
   if (w == 0) {
@@ -348,21 +385,21 @@ potrf_diag_kernel(float* __restrict__ a, int64_t lda, int kb, int* __restrict__ 
         r[k] = (lane < kb && k < kb) ? ((k <= lane) ? a[(int64_t)lane * lda + k] : 0.f)
                                      : ((lane == k) ? 1.f : 0.f);
     }
-    bad |= sub_factor(r, X, lt);
+    bad |= sub_factor(r, X, lt, cb, rdiag);
   } else if (vec) {
     constexpr int N4 = (NB - SUB) * NB / 4;  // float4s in rows 32..127
-    constexpr int IT = (N4 + DIAG_THREADS - 32 - 1) / (DIAG_THREADS - 32);
+    constexpr int IT = (N4 + LD_THREADS - 1) / LD_THREADS;
     float4 v[IT];
 #pragma unroll
     for (int it = 0; it < IT; ++it) {
-      const int e4 = lt_thread + it * LT_THREADS;
+      const int e4 = ld_thread + it * LD_THREADS;
       if (e4 < N4)
         v[it] = *reinterpret_cast<const float4*>(a + (int64_t)(SUB + (e4 >> 5)) * lda +
                                                  ((e4 & 31) << 2));
     }
 #pragma unroll
     for (int it = 0; it < IT; ++it) {
-      const int e4 = lt_thread + it * LT_THREADS;
+      const int e4 = ld_thread + it * LD_THREADS;
       if (e4 < N4) {
         const int rr = SUB + (e4 >> 5), c = (e4 & 31) << 2;
         S[rr * DP + c + 0] = (c + 0 <= rr) ? v[it].x : 0.f;
@@ -372,7 +409,7 @@ potrf_diag_kernel(float* __restrict__ a, int64_t lda, int kb, int* __restrict__ 
       }
     }
   } else {
-    for (int e = lt_thread; e < (NB - SUB) * NB; e += LT_THREADS) {
+    for (int e = ld_thread; e < (NB - SUB) * NB; e += LD_THREADS) {
       const int rr = SUB + e / NB, c = e % NB;
       const float v = (rr < kb && c <= rr) ? a[(int64_t)rr * lda + c] : 0.f;
       S[rr * DP + c] = (rr < kb && c < kb) ? v : ((rr == c) ? 1.f : 0.f);
@@ -401,16 +438,16 @@ potrf_diag_kernel(float* __restrict__ a, int64_t lda, int kb, int* __restrict__ 
   if (w == 0) {
 #pragma unroll
     for (int k = 0; k < SUB; ++k) r[k] = S[(SUB + lane) * DP + SUB + k];
-    bad |= sub_factor(r, X + SUB * DP + SUB, lt);
-  } else {
+    bad |= sub_factor(r, X + SUB * DP + SUB, lt, cb, rdiag);
+  } else if (la) {
     // rows 64..127, columns 32..127: A -= L_i0 L_j0^T (lower part)
-    bprod<true, 5, 3>(S + 2 * SUB * DP, S + SUB * DP, 2 * SUB, lw, LW, 0, SUB, acc5);
+    bprod<true, 6, 3>(S + 2 * SUB * DP, S + SUB * DP, 2 * SUB, lw, LW, 0, SUB, acc6c);
 #pragma unroll
-    for (int q = 0; q < 5; ++q)
+    for (int q = 0; q < 6; ++q)
 #pragma unroll
       for (int s = 0; s < 3; ++s) {
         const int rr = lw + LW * q, c = lane + 32 * s;
-        if (rr < 2 * SUB && SUB + c <= 2 * SUB + rr) S[(2 * SUB + rr) * DP + SUB + c] -= acc5[q][s];
+        if (rr < 2 * SUB && SUB + c <= 2 * SUB + rr) S[(2 * SUB + rr) * DP + SUB + c] -= acc6c[q][s];
       }
     // W_10 = L_10 X_00
     bprod<false, 3, 1>(S + SUB * DP, X, SUB, lw, LW, 0, SUB, acc3b);
@@ -452,8 +489,8 @@ potrf_diag_kernel(float* __restrict__ a, int64_t lda, int kb, int* __restrict__ 
   if (w == 0) {
 #pragma unroll
     for (int k = 0; k < SUB; ++k) r[k] = S[(2 * SUB + lane) * DP + 2 * SUB + k];
-    bad |= sub_factor(r, X + 2 * SUB * DP + 2 * SUB, lt);
-  } else {
+    bad |= sub_factor(r, X + 2 * SUB * DP + 2 * SUB, lt, cb, rdiag);
+  } else if (la) {
     // rows 96..127, columns 64..127: A -= L_i1 L_j1^T (lower part)
     bprod<true, 3, 2>(S + 3 * SUB * DP, S + 2 * SUB * DP, SUB, lw, LW, SUB, 2 * SUB, acc3);
 #pragma unroll
@@ -511,8 +548,8 @@ potrf_diag_kernel(float* __restrict__ a, int64_t lda, int kb, int* __restrict__ 
   if (w == 0) {
 #pragma unroll
     for (int k = 0; k < SUB; ++k) r[k] = S[(3 * SUB + lane) * DP + 3 * SUB + k];
-    bad |= sub_factor(r, X + 3 * SUB * DP + 3 * SUB, lt);
-  } else {
+    bad |= sub_factor(r, X + 3 * SUB * DP + 3 * SUB, lt, cb, rdiag);
+  } else if (la) {
     // W_3j = sum_{j <= k < 3} L_3k X_kj
 #pragma unroll
     for (int j = 0; j < 3; ++j) {

@@ -454,6 +454,19 @@ int64_t ws_bytes(int64_t m, int64_t n, int P) {
   return b;
 }
 
+// The step kernel's shared-memory opt-in, once per device.
+int step_kernel_setup() {
+  static int attr_device = -1;
+  int dev = 0;
+  GQ_CHECK_CUDA(cudaGetDevice(&dev));
+  if (attr_device != dev) {
+    GQ_CHECK_CUDA(cudaFuncSetAttribute(qr_step_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       200 * 1024));
+    attr_device = dev;
+  }
+  return GQ_OK;
+}
+
 Work carve(void* ws, int64_t m, int64_t n, int P) {
   char* p = reinterpret_cast<char*>(ws);
   Work w;
@@ -568,12 +581,7 @@ int gq_qrcp(float* a, int64_t m, int64_t n, int64_t lda, int panel_size, int piv
   GQ_REQUIRE(v_out == nullptr || ldv >= limit, "gq_qrcp: ldv too small");
   cudaStream_t st = as_stream(stream);
   qr::Work W = qr::carve(workspace, m, n, P);
-  static bool attr = false;
-  if (!attr) {
-    GQ_CHECK_CUDA(cudaFuncSetAttribute(qr::qr_step_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                       200 * 1024));
-    attr = true;
-  }
+  GQ_TRY(qr::step_kernel_setup());
   dim3 tb(32, 8);
   qr::transpose_kernel<<<dim3((unsigned)ceil_div(n, 32), (unsigned)ceil_div(m, 32)), tb, 0, st>>>(
       a, m, n, lda, W.at, m);
@@ -635,12 +643,7 @@ int gq_qr_factor_panel(float* a, int64_t m, int64_t n, int64_t lda, int32_t* per
   GQ_REQUIRE(workspace_bytes >= gq_qrcp_workspace_size(m, n, P), "gq_qr_factor_panel: workspace too small");
   cudaStream_t st = as_stream(stream);
   qr::Work W = qr::carve(workspace, m, n, P);
-  static bool attr = false;
-  if (!attr) {
-    GQ_CHECK_CUDA(cudaFuncSetAttribute(qr::qr_step_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                       200 * 1024));
-    attr = true;
-  }
+  GQ_TRY(qr::step_kernel_setup());
   dim3 tb(32, 8);
   qr::transpose_kernel<<<dim3((unsigned)ceil_div(n, 32), (unsigned)ceil_div(m, 32)), tb, 0, st>>>(
       a, m, n, lda, W.at, m);

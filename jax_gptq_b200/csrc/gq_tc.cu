@@ -156,23 +156,40 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
   asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 }
 
-// Tile index -> (row tile, column tile).  Symmetric: column tile bn owns
-// row tiles 0 .. min(mb, 2 bn + 2) - 1 (those touching the upper triangle).
+// Rows of column tile bn that are computed: all of them, or for the
+// symmetric case the row tiles 0 .. min(mb, 2 bn + 2) - 1 touching the upper
+// triangle (non-decreasing in bn).
+__device__ __forceinline__ int col_height(const Params& p, int bn) {
+  return p.symmetric ? min(p.mb, 2 * bn + 2) : p.mb;
+}
+
+// Tile index -> (row tile, column tile).  Tiles are taken in groups of
+// GROUP_COLS column tiles and, inside a group, row by row, so the CTAs that
+// stream the same token slabs at the same time share about GROUP_COLS column
+// panels and grid / GROUP_COLS row panels of the operands: each wave of tiles
+// reads under half of X from DRAM and L2 serves the rest.
+constexpr int GROUP_COLS = 8;
 __device__ __forceinline__ void tile_coords(const Params& p, int t, int& bm, int& bn) {
-  if (!p.symmetric) {
-    bm = t % p.mb;
-    bn = t / p.mb;
-    return;
-  }
-  int acc = 0;
-  for (int j = 0; j < p.nb; ++j) {
-    int c = min(p.mb, 2 * j + 2);
-    if (t < acc + c) {
-      bn = j;
-      bm = t - acc;
-      return;
+  for (int g0 = 0; g0 < p.nb; g0 += GROUP_COLS) {
+    const int g1 = min(p.nb, g0 + GROUP_COLS);
+    int cnt = 0;
+    for (int j = g0; j < g1; ++j) cnt += col_height(p, j);
+    if (t >= cnt) {
+      t -= cnt;
+      continue;
     }
-    acc += c;
+    // row r of the group holds the columns whose height exceeds r: a suffix
+    int first = g0;
+    for (int r = 0; r < col_height(p, g1 - 1); ++r) {
+      while (first < g1 && col_height(p, first) <= r) ++first;
+      const int n = g1 - first;
+      if (t < n) {
+        bm = r;
+        bn = first + t;
+        return;
+      }
+      t -= n;
+    }
   }
   bm = 0;
   bn = 0;
@@ -439,11 +456,13 @@ int launch(const void* xa, int64_t lda, const void* xb, int64_t ldb, int64_t K, 
   } else {
     p.num_tiles = p.mb * p.nb;
   }
-  static bool attr_set = false;
-  if (!attr_set) {
+  static int attr_device = -1;
+  int dev = 0;
+  GQ_CHECK_CUDA(cudaGetDevice(&dev));
+  if (attr_device != dev) {
     GQ_CHECK_CUDA(cudaFuncSetAttribute(gemm_tn_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                        SMEM_BYTES));
-    attr_set = true;
+    attr_device = dev;
   }
   const int grid = std::min(p.num_tiles, cta_budget());
   gemm_tn_kernel<<<grid, THREADS, SMEM_BYTES, st>>>(ma, mbm, p);
