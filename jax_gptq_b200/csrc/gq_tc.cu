@@ -11,8 +11,8 @@
 //               stage into one of two TMEM accumulators (2 x 256 columns),
 //               restarting the accumulation every CHUNK_KB stages (512 tokens);
 //   warps 2-9   epilogue: add each chunk's TMEM result into fp32 registers
-//               (128 columns per thread) and store the tile once, optionally
-//               accumulating into C.
+//               (128 columns per thread) and store the tile once; when
+//               accumulating, the register sum starts from C's contents.
 // Summing 512-token chunks outside the tensor core keeps H within 1e-5 of a
 // float64 reference over hundreds of thousands of tokens; a single TMEM
 // accumulation over 4096 tokens already drifts past that bound.
@@ -323,9 +323,30 @@ gemm_tn_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant_
     for (int t = blockIdx.x; ok && t < p.num_tiles && !*abort_flag; t += gridDim.x) {
       int bm, bn;
       tile_coords(p, t, bm, bn);
+      const int64_t row = (int64_t)bm * BM + row_in_tile;
+      const int64_t col0 = (int64_t)bn * BN + half * HALF_COLS;
+      const bool inside = row < p.M && col0 < p.N;
+      float* cp = p.c + row * p.ldc + col0;
+      const bool vec = inside && (col0 + HALF_COLS <= p.N) &&
+                       ((reinterpret_cast<uintptr_t>(cp) & 15) == 0);
+      // the running sum starts from C when accumulating, so a product split
+      // into launches at multiples of CHUNK_KB * BK tokens adds the same
+      // chunk results in the same order as one launch over all tokens
       float sum[HALF_COLS];
+      if (p.accumulate && vec) {
 #pragma unroll
-      for (int j = 0; j < HALF_COLS; ++j) sum[j] = 0.f;
+        for (int j = 0; j < HALF_COLS; j += 4) {
+          const float4 o = *reinterpret_cast<const float4*>(cp + j);
+          sum[j] = o.x;
+          sum[j + 1] = o.y;
+          sum[j + 2] = o.z;
+          sum[j + 3] = o.w;
+        }
+      } else {
+#pragma unroll
+        for (int j = 0; j < HALF_COLS; ++j)
+          sum[j] = (p.accumulate && inside && col0 + j < p.N) ? cp[j] : 0.f;
+      }
       for (int kc = 0; kc < nkb; kc += CHUNK_KB) {
         if (!mbar_wait(&tfull[acc], acc_phase, abort_flag)) {
           ok = false;
@@ -347,31 +368,14 @@ gemm_tn_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant_
         }
       }
       if (!ok) break;
-      const int64_t row = (int64_t)bm * BM + row_in_tile;
-      const int64_t col0 = (int64_t)bn * BN + half * HALF_COLS;
-      if (row < p.M && col0 < p.N) {
-        float* cp = p.c + row * p.ldc + col0;
-        const bool vec = (col0 + HALF_COLS <= p.N) && ((reinterpret_cast<uintptr_t>(cp) & 15) == 0);
-        if (vec) {
+      if (vec) {
 #pragma unroll
-          for (int j = 0; j < HALF_COLS; j += 4) {
-            float4 v = make_float4(sum[j], sum[j + 1], sum[j + 2], sum[j + 3]);
-            if (p.accumulate) {
-              float4 o = *reinterpret_cast<const float4*>(cp + j);
-              v.x += o.x; v.y += o.y; v.z += o.z; v.w += o.w;
-            }
-            *reinterpret_cast<float4*>(cp + j) = v;
-          }
-        } else {
+        for (int j = 0; j < HALF_COLS; j += 4)
+          *reinterpret_cast<float4*>(cp + j) = make_float4(sum[j], sum[j + 1], sum[j + 2], sum[j + 3]);
+      } else if (inside) {
 #pragma unroll
-          for (int j = 0; j < HALF_COLS; ++j) {
-            if (col0 + j < p.N) {
-              float v = sum[j];
-              if (p.accumulate) v += cp[j];
-              cp[j] = v;
-            }
-          }
-        }
+        for (int j = 0; j < HALF_COLS; ++j)
+          if (col0 + j < p.N) cp[j] = sum[j];
       }
     }
   }

@@ -157,6 +157,10 @@ _SIDE_STREAMS: dict[int, list] = {}
 # running leave free to it.  12 on a 148-SM part: the d = 4096 Hessians then
 # run in exactly two waves of 136 tiles.
 RESERVED_SMS = 12
+# Statistics formed while a chain is running are split into launches of this
+# many tokens (bit-identical to one launch), so the chain's kernels, on a
+# higher-priority stream, get the SMs between them.
+STATS_TOKEN_CHUNK = 32768
 
 
 def _side_streams(n: int) -> list:
@@ -178,8 +182,9 @@ def _stack(weights: dict, members) -> torch.Tensor:
 def _run_groups_concurrently(sizes: dict, form, work, redo) -> dict:
     """Run each input group's chain on its own side stream.
 
-    ``sizes[grp]`` orders the groups (largest first).  ``form(grp) -> h``
-    runs on the current stream and forms the group's statistics;
+    ``sizes[grp]`` orders the groups (largest first).  ``form(grp, chunk)
+    -> h`` runs on the current stream and forms the group's statistics, in
+    launches of ``chunk`` tokens (None: one launch) once a chain is running;
     ``work(grp, h) -> (status, result)`` then runs on the group's side stream
     as soon as that h is ready, while the current stream goes on to the next
     group's statistics.  The largest group's chain (the longest) runs on the
@@ -202,7 +207,7 @@ def _run_groups_concurrently(sizes: dict, form, work, redo) -> dict:
     for idx, (grp, s) in enumerate(zip(order, streams)):
         lib.gq_set_cta_budget(0 if idx == 0 else max(1, sms - RESERVED_SMS))
         try:
-            hs[grp] = form(grp)
+            hs[grp] = form(grp, None if idx == 0 else STATS_TOKEN_CHUNK)
             s.wait_stream(main)
             with torch.cuda.stream(s):
                 pending[grp] = work(grp, hs[grp])
@@ -237,11 +242,11 @@ def quantize_layer_gptq(weights: dict, inputs: dict, cfg: QuantConfig, shapes=LL
     """
     if timed or not concurrent:
         return _quantize_layer_gptq_sequential(weights, inputs, cfg, shapes, timed)
-    def form(grp):
+    def form(grp, chunk):
         x = inputs[grp]
         d = x.shape[1]
         h = torch.empty((d, d), dtype=torch.float32, device=x.device)
-        stats.syrk_into(h, x, accumulate=False)
+        stats.syrk_into(h, x, accumulate=False, token_chunk=chunk)
         return h
 
     def work(grp, h):
@@ -291,13 +296,13 @@ def quantize_layer_qronos(weights: dict, inputs_float: dict, inputs_quant: dict,
                                                  timed)
     gs = {}
 
-    def form(grp):
+    def form(grp, chunk):
         xq = inputs_quant[grp]
         d = xq.shape[1]
         h = torch.empty((d, d), dtype=torch.float32, device=xq.device)
         g = torch.empty((d, d), dtype=torch.float32, device=xq.device)
-        stats.syrk_into(h, xq, accumulate=False)
-        stats.gemm_tn_into(g, inputs_float[grp], xq, accumulate=False)
+        stats.syrk_into(h, xq, accumulate=False, token_chunk=chunk)
+        stats.gemm_tn_into(g, inputs_float[grp], xq, accumulate=False, token_chunk=chunk)
         gs[grp] = g
         return h
 

@@ -34,27 +34,51 @@ def _is_bf16(x) -> bool:
     return isinstance(x, torch.Tensor) and x.dtype == torch.bfloat16
 
 
-def syrk_into(h: torch.Tensor, x: torch.Tensor, accumulate: bool) -> None:
-    """h (+)= x^T x on the device (h: [d, d] float32 contiguous)."""
-    tokens, d = x.shape
-    if x.dtype == torch.bfloat16:
-        _lib.call("gq_syrk_bf16", A.ptr(x), tokens, d, x.stride(0), A.ptr(h), d, int(accumulate),
-                  A.stream())
-    else:
-        _lib.call("gq_syrk_f32", A.ptr(x), tokens, d, x.stride(0), A.ptr(h), d, int(accumulate),
-                  A.stream())
+# bf16 products are summed in tensor-memory chunks of this many tokens; calls
+# split at multiples of it give the same bits as one call (see gq.h)
+TOKEN_CHUNK_QUANTUM = 512
 
 
-def gemm_tn_into(g: torch.Tensor, xa: torch.Tensor, xb: torch.Tensor, accumulate: bool) -> None:
-    """g (+)= xa^T xb on the device."""
-    tokens, da = xa.shape
+def _token_slices(tokens: int, token_chunk):
+    if not token_chunk or token_chunk >= tokens:
+        return [(0, tokens)]
+    if token_chunk % TOKEN_CHUNK_QUANTUM:
+        raise ValueError(f"token_chunk must be a multiple of {TOKEN_CHUNK_QUANTUM}, got {token_chunk}")
+    return [(t0, min(tokens, t0 + token_chunk)) for t0 in range(0, tokens, token_chunk)]
+
+
+def syrk_into(h: torch.Tensor, x: torch.Tensor, accumulate: bool, token_chunk=None) -> None:
+    """h (+)= x^T x on the device (h: [d, d] float32 contiguous).
+
+    ``token_chunk`` splits the product into launches over that many tokens
+    each (shorter kernels, so work on higher-priority streams is scheduled in
+    between); for bf16 the result is bit-identical to a single launch."""
+    d = x.shape[1]
+    for i, (t0, t1) in enumerate(_token_slices(x.shape[0], token_chunk)):
+        xs = x[t0:t1]
+        acc = int(accumulate or i > 0)
+        if x.dtype == torch.bfloat16:
+            _lib.call("gq_syrk_bf16", A.ptr(xs), t1 - t0, d, x.stride(0), A.ptr(h), d, acc,
+                      A.stream())
+        else:
+            _lib.call("gq_syrk_f32", A.ptr(xs), t1 - t0, d, x.stride(0), A.ptr(h), d, acc,
+                      A.stream())
+
+
+def gemm_tn_into(g: torch.Tensor, xa: torch.Tensor, xb: torch.Tensor, accumulate: bool,
+                 token_chunk=None) -> None:
+    """g (+)= xa^T xb on the device; ``token_chunk`` as for :func:`syrk_into`."""
+    da = xa.shape[1]
     db = xb.shape[1]
-    if xa.dtype == torch.bfloat16:
-        _lib.call("gq_gemm_tn_bf16", A.ptr(xa), xa.stride(0), A.ptr(xb), xb.stride(0), tokens, da,
-                  db, A.ptr(g), db, int(accumulate), A.stream())
-    else:
-        _lib.call("gq_gemm_tn_f32", A.ptr(xa), xa.stride(0), A.ptr(xb), xb.stride(0), tokens, da, db,
-                  A.ptr(g), db, int(accumulate), A.stream())
+    for i, (t0, t1) in enumerate(_token_slices(xa.shape[0], token_chunk)):
+        sa, sb = xa[t0:t1], xb[t0:t1]
+        acc = int(accumulate or i > 0)
+        if xa.dtype == torch.bfloat16:
+            _lib.call("gq_gemm_tn_bf16", A.ptr(sa), xa.stride(0), A.ptr(sb), xb.stride(0), t1 - t0,
+                      da, db, A.ptr(g), db, acc, A.stream())
+        else:
+            _lib.call("gq_gemm_tn_f32", A.ptr(sa), xa.stride(0), A.ptr(sb), xb.stride(0), t1 - t0,
+                      da, db, A.ptr(g), db, acc, A.stream())
 
 
 def h_g_from_activations(x_quant, x_float=None):

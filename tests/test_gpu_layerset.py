@@ -72,7 +72,7 @@ def test_failed_first_attempt_is_redone():
 
     good = torch.eye(n, device="cuda")
     hs = {"bad": h, "good": good}
-    out = LS._run_groups_concurrently({"bad": n, "good": n}, hs.__getitem__, work, redo)
+    out = LS._run_groups_concurrently({"bad": n, "good": n}, lambda g, _chunk: hs[g], work, redo)
     assert calls == ["bad"]
     f = factor_hessian(h, cfg)
     assert f.attempt >= 1

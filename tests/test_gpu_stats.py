@@ -100,3 +100,39 @@ def test_zero_tokens_gives_zero_h():
     _lib.call("gq_syrk_bf16", A.ptr(x) if x.numel() else ctypes.c_void_p(256), 0, 64, 64, A.ptr(h),
               64, 0, A.stream())
     assert float(h.abs().max()) == 0.0
+
+
+@pytest.mark.parametrize("tokens,d,chunk", [(4096, 520, 512), (6144, 1024, 2048), (5000, 384, 1024)])
+def test_token_chunked_launches_equal_one_launch(tokens, d, chunk):
+    """Splitting the tokens at multiples of 512 continues the same float32
+    running sum: H and G are bit-identical to a single launch (the tail chunk
+    may be ragged)."""
+    from jax_gptq_b200 import stats
+    rng = np.random.default_rng(tokens + chunk)
+    xq = _bf16(rng, (tokens, d))[0].cuda()
+    xf = _bf16(rng, (tokens, d))[0].cuda()
+    h1 = torch.empty((d, d), device="cuda")
+    h2 = torch.empty((d, d), device="cuda")
+    g1 = torch.empty((d, d), device="cuda")
+    g2 = torch.empty((d, d), device="cuda")
+    stats.syrk_into(h1, xq, accumulate=False)
+    stats.syrk_into(h2, xq, accumulate=False, token_chunk=chunk)
+    stats.gemm_tn_into(g1, xf, xq, accumulate=False)
+    stats.gemm_tn_into(g2, xf, xq, accumulate=False, token_chunk=chunk)
+    assert _status() == 0
+    assert torch.equal(h1, h2)
+    assert torch.equal(g1, g2)
+    # a streamed accumulator over 512-multiple batches is the same sum again
+    acc = HessianAccumulator(d, with_cross=True)
+    for t0 in range(0, tokens, chunk):
+        acc.add(xq[t0:t0 + chunk], xf[t0:t0 + chunk])
+    assert torch.equal(acc.h, h1)
+    assert torch.equal(acc.g, g1)
+
+
+def test_token_chunk_must_be_a_multiple_of_512():
+    from jax_gptq_b200 import stats
+    x = torch.zeros((2048, 64), dtype=torch.bfloat16, device="cuda")
+    h = torch.empty((64, 64), device="cuda")
+    with pytest.raises(ValueError):
+        stats.syrk_into(h, x, accumulate=False, token_chunk=1000)
