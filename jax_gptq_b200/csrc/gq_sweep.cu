@@ -7,16 +7,24 @@
 // with the dequantized values; cp [m, ldp] uint8 -- codes in permuted order;
 // err [m, 128] float32 -- the scaled errors of the current block.
 //
-// Per 128-column block [b0, b1):
-//   1. the band U[b0:b1, b0:] is transposed into ubt (column j of the band is
-//      a contiguous 128-float row);
+// The lazy updates are two-level: blocks of 128 columns inside super-blocks
+// of 512.  Per block [b0, b1) of super-block [s0, s1):
+//   1. the band U[b0:b1, b0:s1] is transposed into ubt (column j of the band
+//      is a contiguous 128-float row);
 //   2. sweep_rows_kernel: one lane per weight row, one warp per CTA; the
 //      lane quantizes its row's columns one by one (32-column sub-blocks in
 //      registers, the rest of the block in a shared-memory row buffer, the U
 //      rows of each sub-block's trailing update copied in by cp.async while
 //      the sub-block's columns are quantized) and writes codes, dequantized
-//      values and scaled errors (w - dq) / U_ii;
-//   3. wp[:, b1:] -= err @ U[b0:b1, b1:]  (fp32 GEMM).
+//      values and scaled errors (w - dq) / U_ii into its 128 columns of err;
+//   3. near update: wp[:, b1:s1] -= err[:, b0-s0:b1-s0] @ U[b0:b1, b1:s1].
+// After the super-block, one far update with K = 512:
+//   wp[:, s1:] -= err @ U[s0:s1, s1:]   (U[s0:s1, s1:] transposed first).
+// The far update is most of the work; at K = 512 it moves a quarter of the
+// weight traffic of four K = 128 updates and keeps the tensor cores busier.
+// A group wider than a block must not start inside a super-block and end
+// past it (its parameters are taken from the columns at its start, before
+// the far update); other group sizes fall back to 128-column super-blocks.
 // Finally codes/dequant are scattered back to original column order.
 #include "gq_common.cuh"
 #include "gq_quant.cuh"
@@ -28,6 +36,7 @@ int sgemm(int ta, int tb, int64_t M, int64_t N, int64_t K, float alpha, const fl
 int check_quant_args(const char* who, int64_t m, int64_t n, int w_bits, int group_size, int sym);
 
 constexpr int SW_BLOCK = 128;
+constexpr int SW_SUPER = 512;  // columns per super-block (far updates)
 constexpr int SW_SUB = 32;   // columns of a register-resident sub-block
 constexpr int SW_WP = 33;    // pitch of the row buffer (lane-private columns, conflict-free)
 constexpr int SW_TP = 36;    // pitch of the sub-block U tile (16-byte rows for broadcast reads)
@@ -79,7 +88,8 @@ __global__ void group_params_kernel(const float* __restrict__ wp, int64_t m, int
 struct SweepArgs {
   float* wp;            // [m, ldp]
   uint8_t* cp;          // [m, ldp]
-  float* err;           // [m, 128]
+  float* err;           // [m, ld_err]: this block's scaled errors
+  int64_t ld_err;
   const float* ubt;     // [n - b0, 128]: ubt[j][i] = U[b0 + i][b0 + j]
   int64_t m, n, ldp;
   int64_t b0;           // first column of this block
@@ -255,7 +265,7 @@ __global__ void __launch_bounds__(32) sweep_rows_kernel(SweepArgs a) {
     }
 
     if (valid) {
-      float* erow = a.err + row * SW_BLOCK + c0;
+      float* erow = a.err + row * a.ld_err + c0;
       uint8_t* crow = a.cp + row * a.ldp + a.b0 + c0;
       if (c0 + SW_SUB <= bw) {
 #pragma unroll
@@ -333,15 +343,23 @@ __global__ void g_idx_kernel(const int32_t* __restrict__ perm, int64_t n, int g,
   if (j < n) g_idx[perm ? perm[j] : j] = (int32_t)(j / g);
 }
 
+// Super-block width for a group size (see the file comment).
+inline int sweep_super(int group_size) {
+  const bool fits = group_size <= SW_BLOCK || SW_SUPER % group_size == 0 ||
+                    group_size % SW_SUPER == 0;
+  return fits ? SW_SUPER : SW_BLOCK;
+}
+
 // Byte offset of the transposed U band (after wp, cp, err, bscale, bzero).
 inline int64_t sweep_ubt_offset(int64_t m, int64_t n) {
   int64_t ldp = round4(n);
-  int64_t off = m * ldp * 4 + ((m * ldp + 15) & ~int64_t(15)) + m * SW_BLOCK * 4 + 2 * m * 4;
+  int64_t off = m * ldp * 4 + ((m * ldp + 15) & ~int64_t(15)) + m * SW_SUPER * 4 + 2 * m * 4;
   return (off + 255) & ~int64_t(255);
 }
 
+// ubt holds a band [<= 512, 128] or the far block U[s0:s1, s1:]^T [n - s1, 512].
 int64_t sweep_ws_bytes(int64_t m, int64_t n) {
-  return sweep_ubt_offset(m, n) + n * SW_BLOCK * 4 + 256;
+  return sweep_ubt_offset(m, n) + n * SW_SUPER * 4 + 256;
 }
 
 int transpose2d(const float* src, int64_t rows, int64_t cols, int64_t lds, float* dst, int64_t ldd,
@@ -382,9 +400,10 @@ int gq_gptq_sweep(const float* w, int64_t m, int64_t n, int64_t ldw, const float
   float* wp = reinterpret_cast<float*>(ws);
   uint8_t* cp = reinterpret_cast<uint8_t*>(ws + m * ldp * 4);
   float* err = reinterpret_cast<float*>(ws + m * ldp * 4 + ((m * ldp + 15) & ~int64_t(15)));
-  float* bscale = err + m * SW_BLOCK;
+  float* bscale = err + m * SW_SUPER;
   float* bzero = bscale + m;
-  float* ubt = reinterpret_cast<float*>(ws + sweep_ubt_offset(m, n));  // [n, 128]
+  float* ubt = reinterpret_cast<float*>(ws + sweep_ubt_offset(m, n));  // [n, 512]
+  const int super_w = sweep_super(group_size);
 
   if (start) {
     GQ_CHECK_CUDA(cudaMemcpy2DAsync(wp, ldp * 4, start, n * 4, n * 4, m, cudaMemcpyDeviceToDevice, st));
@@ -397,7 +416,8 @@ int gq_gptq_sweep(const float* w, int64_t m, int64_t n, int64_t ldw, const float
   }
 
   SweepArgs a;
-  a.wp = wp; a.cp = cp; a.err = err; a.ubt = ubt;
+  a.wp = wp; a.cp = cp; a.ubt = ubt;
+  a.ld_err = super_w;
   a.m = m; a.n = n; a.ldp = ldp;
   a.n_groups = (int)(n / group_size);
   a.qp = make_qparams(w_bits, sym); a.sym = sym;
@@ -425,12 +445,15 @@ int gq_gptq_sweep(const float* w, int64_t m, int64_t n, int64_t ldw, const float
                                         cudaMemcpyDeviceToDevice, st));
       }
     }
+    const int64_t s0 = b0 - b0 % super_w;
+    const int64_t s1 = std::min<int64_t>(n, s0 + super_w);
     a.b0 = b0;
     a.bw = bw;
-    // U[b0:b1, b0:] transposed: the sweep reads the block's rows of U as
-    // contiguous runs, and the trailing GEMM gets both operands K-major
+    a.err = err + (b0 - s0);
+    // U[b0:b1, b0:s1] transposed: the sweep reads the block's rows of U as
+    // contiguous runs, and the near GEMM gets both operands K-major
     // (tensor-core path)
-    GQ_TRY(transpose2d(u + b0 * ldu + b0, bw, n - b0, ldu, ubt, SW_BLOCK, st));
+    GQ_TRY(transpose2d(u + b0 * ldu + b0, bw, s1 - b0, ldu, ubt, SW_BLOCK, st));
     switch (group_size) {
       case 4: sweep_rows_kernel<4><<<grid, 32, 0, st>>>(a); break;
       case 8: sweep_rows_kernel<8><<<grid, 32, 0, st>>>(a); break;
@@ -442,10 +465,16 @@ int gq_gptq_sweep(const float* w, int64_t m, int64_t n, int64_t ldw, const float
     }
     GQ_TRY(check_launch("sweep_rows"));
     const int64_t b1 = b0 + bw;
-    if (b1 < n) {
-      // wp[:, b1:] -= err @ U[b0:b1, b1:]
-      GQ_TRY(sgemm(0, 1, m, n - b1, bw, -1.f, err, SW_BLOCK, ubt + (int64_t)bw * SW_BLOCK,
+    if (b1 < s1) {
+      // near: wp[:, b1:s1] -= err_block @ U[b0:b1, b1:s1]
+      GQ_TRY(sgemm(0, 1, m, s1 - b1, bw, -1.f, a.err, super_w, ubt + (int64_t)bw * SW_BLOCK,
                    SW_BLOCK, 1.f, wp + b1, ldp, 0, st));
+    }
+    if (b1 == s1 && s1 < n) {
+      // far: wp[:, s1:] -= err @ U[s0:s1, s1:]
+      GQ_TRY(transpose2d(u + s0 * ldu + s1, s1 - s0, n - s1, ldu, ubt, super_w, st));
+      GQ_TRY(sgemm(0, 1, m, n - s1, s1 - s0, -1.f, err, super_w, ubt, super_w, 1.f, wp + s1, ldp,
+                   0, st));
     }
   }
   if (dequant || codes) {

@@ -190,7 +190,7 @@ def gptq_forward_step_reference(weight, perm, w_bits=4, group_size=128, sym=Fals
 
 
 def gptq_sweep(weight, u, perm, w_bits=4, group_size=128, sym=False, block=128,
-               dtype=np.float32, group0=None, noprop_cols=0, start=None):
+               dtype=np.float32, group0=None, noprop_cols=0, start=None, return_pre=False):
     """GPTQ column sweep with lazy block updates (Frantar et al., 2022).
 
     ``u`` is the upper factor in permuted coordinates.  Returns a dict with
@@ -201,7 +201,8 @@ def gptq_sweep(weight, u, perm, w_bits=4, group_size=128, sym=False, block=128,
     ``start`` (permuted order) replaces ``weight[:, perm]`` as the initial
     estimate; ``group0`` = (scale, zero) presets group 0's parameters and
     ``noprop_cols`` columns at the front propagate no error (both used by the
-    Qronos first step).
+    Qronos first step).  ``return_pre`` adds ``pre`` ([m, n], permuted
+    order): the unrounded ``w / scale + zero`` each code was rounded from.
     """
     w = np.asarray(weight)
     m, n = w.shape
@@ -216,6 +217,7 @@ def gptq_sweep(weight, u, perm, w_bits=4, group_size=128, sym=False, block=128,
     scales = np.zeros((m, n_groups), dtype)
     zeros = np.zeros((m, n_groups), dtype)
     qmin, qmax = oq.qrange(w_bits, sym)
+    pre_out = np.zeros((m, n), dtype) if return_pre else None
     scale = zero = None
     for b0 in range(0, n, block):
         b1 = min(b0 + block, n)
@@ -233,7 +235,10 @@ def gptq_sweep(weight, u, perm, w_bits=4, group_size=128, sym=False, block=128,
                 scales[:, gi] = scale[:, 0]
                 zeros[:, gi] = zero[:, 0]
             col = wp[:, i]
-            qc = np.clip(np.round(col / scale[:, 0] + zero[:, 0]), qmin, qmax).astype(dtype)
+            pre = col / scale[:, 0] + zero[:, 0]
+            if return_pre:
+                pre_out[:, i] = pre
+            qc = np.clip(np.round(pre), qmin, qmax).astype(dtype)
             dq = ((qc - zero[:, 0]) * scale[:, 0]).astype(dtype)
             q_out[:, i] = qc
             dq_out[:, i] = dq
@@ -246,13 +251,16 @@ def gptq_sweep(weight, u, perm, w_bits=4, group_size=128, sym=False, block=128,
             wp[:, b1:] -= err_blk @ u[b0:b1, b1:]
     inv_perm = np.argsort(perm, kind="stable")
     g_idx = (inv_perm // g).astype(np.int32)
-    return {
+    out = {
         "dequant": dq_out[:, inv_perm],
         "q": q_out[:, inv_perm],
         "scales": scales,
         "zeros": zeros,
         "g_idx": g_idx,
     }
+    if return_pre:
+        out["pre"] = pre_out
+    return out
 
 
 def reconstruction_error(w, w_hat, h) -> float:
