@@ -125,7 +125,263 @@ __device__ __forceinline__ void sweep_group_params(const SweepArgs& a, int64_t r
   }
 }
 
-// One 128-column block of the sweep for 32 rows: lane l owns row 32 * blockIdx.x + l.
+// One 128-column block of the sweep for 32 rows: lane l of every warp works on
+// row 32 * blockIdx.x + l.  Columns are taken in sub-blocks of 32.  Warp 0
+// runs the serial part: the sub-block's columns one by one in registers, each
+// column's scaled error applied at once to the later columns of the
+// sub-block (U tile broadcast from shared memory).  The sub-block's 32 errors
+// must then reach the block's remaining columns, which live in a shared-memory
+// row buffer (one column of 32 rows per ws row):
+//   critical: all four warps update the next sub-block's columns (the whole
+//             next group when a 64-column group starts there), then warp 0
+//             goes on;
+//   look-ahead: while warp 0 works on that sub-block, warps 1-3 update the
+//             columns beyond it, store the previous sub-block's dequantized
+//             values, errors and codes, and stage the U tiles warp 0 and the
+//             next critical step read.
+// Every column still receives the updates of all earlier columns in
+// increasing order, one fmaf each, so the result does not depend on the
+// split.  G: group size when it divides 128 (4..128), 0 when groups span
+// blocks.
+constexpr int SR_THREADS = 128;
+constexpr int SR_CP = 2 * SW_SUB + 4;  // pitch of the critical U tile (up to 64 columns)
+
+template <int G>
+__global__ void __launch_bounds__(SR_THREADS) sweep_rows_kernel(SweepArgs a) {
+  constexpr int GD = (G > 0) ? G : 1;  // divisor-safe group size for the G = 0 instance
+  __shared__ float ws[SW_BLOCK * SW_WP];                  // ws[j][lane]: column j of the rows
+  __shared__ __align__(16) float tile[2][SW_SUB * SW_TP];  // U inside sub-block s, [k][t]
+  __shared__ __align__(16) float ucrit[SW_SUB * SR_CP];    // U rows of sub-block s, critical columns
+  __shared__ float rinv[SW_BLOCK];
+  __shared__ float es[2][SW_SUB * SW_WP];                 // errors of sub-block s, [k][lane]
+  __shared__ uint32_t cs[2][(SW_SUB / 4) * 32];           // packed codes of sub-block s
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int bw = a.bw;
+  const float* __restrict__ ubt = a.ubt;  // ubt[j][i] = U[b0 + i][b0 + j]
+  const int64_t row = (int64_t)blockIdx.x * 32 + lane;
+  const bool valid = row < a.m;
+  float* wrow = valid ? a.wp + row * a.ldp + a.b0 : nullptr;
+  const int nsub = (bw + SW_SUB - 1) / SW_SUB;
+
+  // width of the critical update after sub-block s: the next sub-block, or
+  // the whole next group when a group wider than 32 columns starts there
+  auto crit_width = [&](int s) -> int {
+    const int c1 = SW_SUB * (s + 1);
+    if (c1 >= bw) return 0;
+    const int wdt = (G > SW_SUB && G <= SW_BLOCK && c1 % GD == 0) ? G : SW_SUB;
+    return min(wdt, bw - c1);
+  };
+  // U inside sub-block s: tile[s & 1][k][t] = U[b0 + c0 + k][b0 + c0 + t]
+  auto stage_tile = [&](int s, int t0, int nt) {
+    const int c0 = SW_SUB * s;
+    for (int e = t0; e < SW_SUB * (SW_SUB / 4); e += nt) {
+      const int t = e / (SW_SUB / 4), q = e % (SW_SUB / 4);
+      float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+      if (c0 + t < bw) v = __ldg(reinterpret_cast<const float4*>(ubt + (int64_t)(c0 + t) * SW_BLOCK + c0) + q);
+      float* dst = &tile[s & 1][(4 * q) * SW_TP + t];
+      dst[0] = v.x;
+      dst[SW_TP] = v.y;
+      dst[2 * SW_TP] = v.z;
+      dst[3 * SW_TP] = v.w;
+    }
+  };
+  // U rows of sub-block s for its critical columns: ucrit[k][t] = U[b0 + c0 + k][b0 + c1 + t]
+  auto stage_crit = [&](int s, int t0, int nt) {
+    const int c0 = SW_SUB * s, c1 = c0 + SW_SUB, wdt = crit_width(s);
+    for (int e = t0; e < wdt * (SW_SUB / 4); e += nt) {
+      const int t = e / (SW_SUB / 4), q = e % (SW_SUB / 4);
+      const float4 v = __ldg(reinterpret_cast<const float4*>(ubt + (int64_t)(c1 + t) * SW_BLOCK + c0) + q);
+      float* dst = &ucrit[(4 * q) * SR_CP + t];
+      dst[0] = v.x;
+      dst[SR_CP] = v.y;
+      dst[2 * SR_CP] = v.z;
+      dst[3 * SR_CP] = v.w;
+    }
+  };
+  // column j -= sum_k ev[k] U[b0 + c0 + k][b0 + j], k increasing (U from global, broadcast)
+  auto update_from_global = [&](const float (&ev)[SW_SUB], int c0, int j) {
+    const float4* u4 = reinterpret_cast<const float4*>(ubt + (int64_t)j * SW_BLOCK + c0);
+    float v = ws[j * SW_WP + lane];
+#pragma unroll
+    for (int kc = 0; kc < SW_SUB / 4; ++kc) {
+      const float4 u = __ldg(u4 + kc);
+      v = fmaf(-ev[4 * kc + 0], u.x, v);
+      v = fmaf(-ev[4 * kc + 1], u.y, v);
+      v = fmaf(-ev[4 * kc + 2], u.z, v);
+      v = fmaf(-ev[4 * kc + 3], u.w, v);
+    }
+    ws[j * SW_WP + lane] = v;
+  };
+  // sub-block s's results to global memory (dequantized values, errors, codes)
+  auto store_sub = [&](int s, int t0, int nt) {
+    if (!valid) return;
+    const int c0 = SW_SUB * s;
+    float* erow = a.err + row * a.ld_err + c0;
+    uint8_t* crow = a.cp + row * a.ldp + a.b0 + c0;
+    const bool full = c0 + SW_SUB <= bw;
+    for (int q = t0; q < SW_SUB / 4; q += nt) {
+      if (full) {
+        *reinterpret_cast<float4*>(wrow + c0 + 4 * q) =
+            make_float4(ws[(c0 + 4 * q) * SW_WP + lane], ws[(c0 + 4 * q + 1) * SW_WP + lane],
+                        ws[(c0 + 4 * q + 2) * SW_WP + lane], ws[(c0 + 4 * q + 3) * SW_WP + lane]);
+        const float* e = es[s & 1];
+        *reinterpret_cast<float4*>(erow + 4 * q) =
+            make_float4(e[(4 * q) * SW_WP + lane], e[(4 * q + 1) * SW_WP + lane],
+                        e[(4 * q + 2) * SW_WP + lane], e[(4 * q + 3) * SW_WP + lane]);
+        *reinterpret_cast<uint32_t*>(crow + 4 * q) = cs[s & 1][q * 32 + lane];
+      } else {
+        for (int t = 0; t < 4; ++t) {
+          const int k = 4 * q + t;
+          if (c0 + k < bw) {
+            wrow[c0 + k] = ws[(c0 + k) * SW_WP + lane];
+            erow[k] = es[s & 1][k * SW_WP + lane];
+            crow[k] = (uint8_t)(cs[s & 1][q * 32 + lane] >> (8 * t));
+          }
+        }
+      }
+    }
+  };
+
+  // ---- prologue (all warps): the row block, reciprocal pivots, the first tiles
+  for (int i = threadIdx.x; i < SW_BLOCK; i += SR_THREADS)
+    rinv[i] = (i < bw) ? 1.f / ubt[(int64_t)i * SW_BLOCK + i] : 0.f;
+  if (valid) {
+    // warp w loads columns [32 w, 32 w + 32): eight float4 loads in flight per lane
+    float4 v[SW_SUB / 4];
+#pragma unroll
+    for (int q = 0; q < SW_SUB / 4; ++q) {
+      const int j = SW_SUB * warp + 4 * q;
+      v[q] = (j < bw) ? *reinterpret_cast<const float4*>(wrow + j) : make_float4(0.f, 0.f, 0.f, 0.f);
+    }
+#pragma unroll
+    for (int q = 0; q < SW_SUB / 4; ++q) {
+      const int j = SW_SUB * warp + 4 * q;
+      ws[(j + 0) * SW_WP + lane] = v[q].x;
+      ws[(j + 1) * SW_WP + lane] = v[q].y;
+      ws[(j + 2) * SW_WP + lane] = v[q].z;
+      ws[(j + 3) * SW_WP + lane] = v[q].w;
+    }
+  } else {
+#pragma unroll
+    for (int k = 0; k < SW_SUB; ++k) ws[(SW_SUB * warp + k) * SW_WP + lane] = 0.f;
+  }
+  stage_tile(0, threadIdx.x, SR_THREADS);
+  float scale = 1.f, zero = 0.f;  // warp 0: the current group's parameters
+  if (G == 0 && valid) {
+    scale = a.big_scale[row];
+    zero = a.big_zero[row];
+  }
+  __syncthreads();
+
+  for (int s = 0; s < nsub; ++s) {
+    const int c0 = SW_SUB * s;
+    const int w_prev = (s > 0) ? crit_width(s - 1) : 0;
+    if (warp == 0) {
+      // ---- the sub-block's columns, in registers
+      const float* tl = tile[s & 1];
+      float w[SW_SUB], e[SW_SUB];
+      uint32_t cw[SW_SUB / 4];
+#pragma unroll
+      for (int k = 0; k < SW_SUB; ++k) w[k] = (c0 + k < bw) ? ws[(c0 + k) * SW_WP + lane] : 0.f;
+#pragma unroll
+      for (int q = 0; q < SW_SUB / 4; ++q) cw[q] = 0u;
+#pragma unroll
+      for (int k = 0; k < SW_SUB; ++k) {
+        const int i = c0 + k;
+        if (i >= bw) {
+          e[k] = 0.f;
+          continue;
+        }
+        // group parameters at the group's first column, from the current values
+        if (G > 0 && G <= SW_SUB && (k % GD) == 0) {
+          float mn = INFINITY, mx = -INFINITY, ma = 0.f;
+#pragma unroll
+          for (int t = k; t < k + GD && t < SW_SUB; ++t) {
+            mn = fminf(mn, w[t]);
+            mx = fmaxf(mx, w[t]);
+            ma = fmaxf(ma, fabsf(w[t]));
+          }
+          sweep_group_params(a, row, valid, (a.b0 + i) / GD, mn, mx, ma, scale, zero);
+        }
+        if (G > SW_SUB && k == 0 && (c0 % GD) == 0) {
+          float mn = INFINITY, mx = -INFINITY, ma = 0.f;
+#pragma unroll
+          for (int t = 0; t < SW_SUB; ++t) {
+            mn = fminf(mn, w[t]);
+            mx = fmaxf(mx, w[t]);
+            ma = fmaxf(ma, fabsf(w[t]));
+          }
+          for (int j = c0 + SW_SUB; j < c0 + G; ++j) {
+            const float v = ws[j * SW_WP + lane];
+            mn = fminf(mn, v);
+            mx = fmaxf(mx, v);
+            ma = fmaxf(ma, fabsf(v));
+          }
+          sweep_group_params(a, row, valid, (a.b0 + i) / GD, mn, mx, ma, scale, zero);
+        }
+        float dq;
+        const float q = quantize_one(w[k], scale, zero, a.qp, dq);
+        const bool prop = a.b0 + i >= a.noprop_cols;
+        e[k] = prop ? __fmul_rn(__fsub_rn(w[k], dq), rinv[i]) : 0.f;
+        w[k] = dq;
+        cw[k >> 2] |= ((uint32_t)(int)(q - a.qp.qmin) & 0xffu) << (8 * (k & 3));
+#pragma unroll
+        for (int q4 = 0; q4 < SW_SUB / 4; ++q4) {
+          if (4 * q4 + 3 > k) {
+            const float4 u4 = *reinterpret_cast<const float4*>(&tl[k * SW_TP + 4 * q4]);
+            const float uu[4] = {u4.x, u4.y, u4.z, u4.w};
+#pragma unroll
+            for (int t = 0; t < 4; ++t)
+              if (4 * q4 + t > k) w[4 * q4 + t] = fmaf(-e[k], uu[t], w[4 * q4 + t]);
+          }
+        }
+      }
+      // publish: dequantized values into the row buffer, errors and codes
+#pragma unroll
+      for (int k = 0; k < SW_SUB; ++k) {
+        if (c0 + k < bw) ws[(c0 + k) * SW_WP + lane] = w[k];
+        es[s & 1][k * SW_WP + lane] = e[k];
+      }
+#pragma unroll
+      for (int q = 0; q < SW_SUB / 4; ++q) cs[s & 1][q * 32 + lane] = cw[q];
+    } else {
+      // ---- look-ahead (warps 1-3)
+      const int lw = warp - 1, lt = threadIdx.x - 32;
+      if (s > 0) {
+        // sub-block s-1's errors reach the columns past its critical update
+        float ev[SW_SUB];
+#pragma unroll
+        for (int k = 0; k < SW_SUB; ++k) ev[k] = es[(s - 1) & 1][k * SW_WP + lane];
+        for (int j = SW_SUB * s + w_prev + lw; j < bw; j += SR_THREADS / 32 - 1)
+          update_from_global(ev, SW_SUB * (s - 1), j);
+        store_sub(s - 1, lw, SR_THREADS / 32 - 1);
+      }
+      if (s + 1 < nsub) stage_tile(s + 1, lt, SR_THREADS - 32);
+      stage_crit(s, lt, SR_THREADS - 32);
+    }
+    __syncthreads();
+    // ---- critical: sub-block s's errors reach the next critical columns (all warps)
+    const int wc = crit_width(s);
+    if (wc > 0) {
+      float ev[SW_SUB];
+#pragma unroll
+      for (int k = 0; k < SW_SUB; ++k) ev[k] = es[s & 1][k * SW_WP + lane];
+      for (int t = warp; t < wc; t += SR_THREADS / 32) {
+        const int j = c0 + SW_SUB + t;
+        float v = ws[j * SW_WP + lane];
+#pragma unroll
+        for (int k = 0; k < SW_SUB; ++k) v = fmaf(-ev[k], ucrit[k * SR_CP + t], v);
+        ws[j * SW_WP + lane] = v;
+      }
+    }
+    __syncthreads();
+  }
+  // the last sub-block's results (its look-ahead step never came)
+  store_sub(nsub - 1, warp, SR_THREADS / 32);
+}
+
+// Single-warp form of the block step, for grids too large to keep four-warp
+// CTAs resident in one wave: lane l owns row 32 * blockIdx.x + l.
 // Columns are taken in sub-blocks of 32 held in registers; inside a sub-block
 // each column's scaled error is applied at once to the later columns
 // (right-looking, U tile broadcast from shared memory), and after the
@@ -134,7 +390,7 @@ __device__ __forceinline__ void sweep_group_params(const SweepArgs& a, int64_t r
 // receives the updates of all earlier columns in increasing order, one fmaf
 // each.  G: group size when it divides 128 (4..128), 0 when groups span blocks.
 template <int G>
-__global__ void __launch_bounds__(32) sweep_rows_kernel(SweepArgs a) {
+__global__ void __launch_bounds__(32) sweep_rows1_kernel(SweepArgs a) {
   constexpr int GD = (G > 0) ? G : 1;  // divisor-safe group size for the G = 0 instance
   __shared__ float ws[SW_BLOCK * SW_WP];
   __shared__ __align__(16) float tile[SW_SUB * SW_TP];
@@ -426,6 +682,11 @@ int gq_gptq_sweep(const float* w, int64_t m, int64_t n, int64_t ldw, const float
   a.big_scale = bscale; a.big_zero = bzero;
   a.scales = scales; a.zeros = zeros;
   const unsigned grid = (unsigned)ceil_div(m, 32);
+  // the four-warp block step while its CTAs (four per SM) fit in one wave
+  int dev = 0, sms = 0;
+  GQ_CHECK_CUDA(cudaGetDevice(&dev));
+  GQ_CHECK_CUDA(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
+  const bool four_warps = grid <= (unsigned)(4 * sms);
   for (int64_t b0 = 0; b0 < n; b0 += SW_BLOCK) {
     const int bw = (int)std::min<int64_t>(SW_BLOCK, n - b0);
     if (group_size > SW_BLOCK && b0 % group_size == 0) {
@@ -454,14 +715,26 @@ int gq_gptq_sweep(const float* w, int64_t m, int64_t n, int64_t ldw, const float
     // contiguous runs, and the near GEMM gets both operands K-major
     // (tensor-core path)
     GQ_TRY(transpose2d(u + b0 * ldu + b0, bw, s1 - b0, ldu, ubt, SW_BLOCK, st));
-    switch (group_size) {
-      case 4: sweep_rows_kernel<4><<<grid, 32, 0, st>>>(a); break;
-      case 8: sweep_rows_kernel<8><<<grid, 32, 0, st>>>(a); break;
-      case 16: sweep_rows_kernel<16><<<grid, 32, 0, st>>>(a); break;
-      case 32: sweep_rows_kernel<32><<<grid, 32, 0, st>>>(a); break;
-      case 64: sweep_rows_kernel<64><<<grid, 32, 0, st>>>(a); break;
-      case 128: sweep_rows_kernel<128><<<grid, 32, 0, st>>>(a); break;
-      default: sweep_rows_kernel<0><<<grid, 32, 0, st>>>(a); break;
+    if (four_warps) {
+      switch (group_size) {
+        case 4: sweep_rows_kernel<4><<<grid, SR_THREADS, 0, st>>>(a); break;
+        case 8: sweep_rows_kernel<8><<<grid, SR_THREADS, 0, st>>>(a); break;
+        case 16: sweep_rows_kernel<16><<<grid, SR_THREADS, 0, st>>>(a); break;
+        case 32: sweep_rows_kernel<32><<<grid, SR_THREADS, 0, st>>>(a); break;
+        case 64: sweep_rows_kernel<64><<<grid, SR_THREADS, 0, st>>>(a); break;
+        case 128: sweep_rows_kernel<128><<<grid, SR_THREADS, 0, st>>>(a); break;
+        default: sweep_rows_kernel<0><<<grid, SR_THREADS, 0, st>>>(a); break;
+      }
+    } else {
+      switch (group_size) {
+        case 4: sweep_rows1_kernel<4><<<grid, 32, 0, st>>>(a); break;
+        case 8: sweep_rows1_kernel<8><<<grid, 32, 0, st>>>(a); break;
+        case 16: sweep_rows1_kernel<16><<<grid, 32, 0, st>>>(a); break;
+        case 32: sweep_rows1_kernel<32><<<grid, 32, 0, st>>>(a); break;
+        case 64: sweep_rows1_kernel<64><<<grid, 32, 0, st>>>(a); break;
+        case 128: sweep_rows1_kernel<128><<<grid, 32, 0, st>>>(a); break;
+        default: sweep_rows1_kernel<0><<<grid, 32, 0, st>>>(a); break;
+      }
     }
     GQ_TRY(check_launch("sweep_rows"));
     const int64_t b1 = b0 + bw;

@@ -230,3 +230,22 @@ def test_sweep_codes_match_float32_oracle_up_to_rounding_ties(m, n, bits, g):
     # and the flips are rare
     assert len(bad_rows) <= 0.05 * m, (len(bad_rows), int(diff.sum()))
     assert np.array_equal(res.g_idx.cpu().numpy(), ref["g_idx"])
+
+
+def test_sweep_single_warp_and_four_warp_block_steps_agree():
+    """Grids larger than one wave of four-warp CTAs take the single-warp block
+    step; rows are independent, so sweeping halves of the rows (four-warp
+    step) must reproduce the whole sweep bit for bit."""
+    sms = torch.cuda.get_device_properties(0).multi_processor_count
+    m, n = 32 * (4 * sms + 8), 512
+    rng = np.random.default_rng(5)
+    x = (rng.standard_normal((2 * n, n)) * rng.lognormal(0, 1, n)).astype(np.float32)
+    cfg = QuantConfig(w_bits=4, group_size=128, ordering_mode="diag_h", semantics="intended")
+    f = G.factor_hessian((x.T @ x).astype(np.float32), cfg)
+    w = torch.from_numpy((rng.standard_normal((m, n)) * 0.02).astype(np.float32)).cuda()
+    whole = G.gptq_sweep(w, f.u, f.perm, cfg)
+    h = m // 2
+    top, bot = G.gptq_sweep(w[:h], f.u, f.perm, cfg), G.gptq_sweep(w[h:], f.u, f.perm, cfg)
+    for key in ("dequant", "codes", "scales", "zeros"):
+        both = torch.cat([getattr(top, key), getattr(bot, key)])
+        assert torch.equal(getattr(whole, key), both), key
