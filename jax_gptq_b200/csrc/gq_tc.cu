@@ -5,11 +5,18 @@
 // Both operands are read in their native [tokens, features] layout: a TMA
 // box of 64 features x 64 tokens with 128-byte swizzle is exactly one
 // MN-major SW128 canonical block for the UMMA descriptor, so no transpose
-// pass is needed.  One CTA per SM, persistent over output tiles of 128 x 256:
-//   warp 0      TMA producer (one thread), 4-stage ring of 48 KB stages;
-//   warp 1      MMA issuer (one thread): 4 x tcgen05.mma (M128 N256 K16) per
-//               stage into one of two TMEM accumulators (2 x 256 columns),
-//               restarting the accumulation every CHUNK_KB stages (512 tokens);
+// pass is needed.  Two forms compute the same bits:
+//   pair (default): clusters of two CTAs, one 256 x 256 tile per cluster,
+//     tcgen05 cta_group::2 MMAs (M256 N256 K16) issued by the even CTA over
+//     both CTAs' shared memory; each CTA stages only its half of A and of B
+//     (32 KB per 64-token stage, six stages);
+//   single: one CTA per SM, tiles of 128 x 256 (48 KB per stage, four
+//     stages), used where no cluster of two fits.
+// In both, per CTA:
+//   warp 0      TMA producer (one thread);
+//   warp 1      MMA issuer (one thread; in the pair form only the even CTA's),
+//               restarting the accumulation every CHUNK_KB stages (512
+//               tokens), two TMEM accumulators of 256 columns;
 //   warps 2-9   epilogue: add each chunk's TMEM result into fp32 registers
 //               (128 columns per thread) and store the tile once; when
 //               accumulating, the register sum starts from C's contents.
@@ -22,7 +29,7 @@
 // Every mbarrier wait is bounded by a globaltimer deadline; a wait that
 // expires raises a shared abort flag (all roles leave their loops) and
 // records GQ_DEVERR_TIMEOUT in the device status word read by
-// gq_device_status().  No multicast loads are used, so the kernel is safe on
+// gq_device_status().  No load uses multicast, so the kernels are safe on
 // any number of GPUs.
 #include <cuda.h>
 
@@ -209,6 +216,8 @@ gemm_tn_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant_
   uint64_t* tempty = tfull + 2;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tempty + 2);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  // epilogue: warp 2's verdict on each accumulator wait, by chunk parity
+  volatile int* epi_go = abort_flag + 1;
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   if (threadIdx.x == 0) {
@@ -320,7 +329,13 @@ gemm_tn_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant_
     int acc = 0;
     uint32_t acc_phase = 0;
     bool ok = true;
-    for (int t = blockIdx.x; ok && t < p.num_tiles && !*abort_flag; t += gridDim.x) {
+    uint32_t chunk = 0;
+    // Only warp 2 polls the accumulator barrier; the other epilogue warps
+    // sleep at a named barrier instead of spinning (their issue slots belong
+    // to the MMA and TMA threads on the same schedulers).  Control flow stays
+    // uniform across the eight warps: every loop decision uses warp 2's
+    // verdict, published before the named barrier.
+    for (int t = blockIdx.x; ok && t < p.num_tiles; t += gridDim.x) {
       int bm, bn;
       tile_coords(p, t, bm, bn);
       const int64_t row = (int64_t)bm * BM + row_in_tile;
@@ -348,10 +363,14 @@ gemm_tn_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant_
           sum[j] = (p.accumulate && inside && col0 + j < p.N) ? cp[j] : 0.f;
       }
       for (int kc = 0; kc < nkb; kc += CHUNK_KB) {
-        if (!mbar_wait(&tfull[acc], acc_phase, abort_flag)) {
-          ok = false;
-          break;
+        if (warp == 2) {
+          const bool got = mbar_wait(&tfull[acc], acc_phase, abort_flag);
+          if (lane == 0) epi_go[chunk & 1] = got ? 1 : 0;
         }
+        asm volatile("bar.sync 1, %0;" ::"n"(EPI_THREADS) : "memory");
+        ok = epi_go[chunk & 1] != 0;
+        ++chunk;
+        if (!ok) break;
         fence_after();
 #pragma unroll
         for (int c = 0; c < HALF_COLS / 32; ++c) {
@@ -433,8 +452,8 @@ static int check_operand(const char* who, const void* x, int64_t tokens, int64_t
   return GQ_OK;
 }
 
-int launch(const void* xa, int64_t lda, const void* xb, int64_t ldb, int64_t K, int64_t M,
-           int64_t N, float* c, int64_t ldc, int accumulate, int symmetric, cudaStream_t st) {
+int launch_single(const void* xa, int64_t lda, const void* xb, int64_t ldb, int64_t K, int64_t M,
+                  int64_t N, float* c, int64_t ldc, int accumulate, int symmetric, cudaStream_t st) {
   if (K == 0) {
     if (!accumulate)
       GQ_CHECK_CUDA(cudaMemset2DAsync(c, ldc * 4, 0, N * 4, M, st));
@@ -473,6 +492,395 @@ int launch(const void* xa, int64_t lda, const void* xb, int64_t ldb, int64_t K, 
   return check_launch("tcgen05 gemm_tn");
 }
 
+}  // namespace tc
+
+// ---------------------------------------------------------------------------
+// CTA-pair form (tcgen05 cta_group::2): one cluster of two CTAs computes a
+// 256 x 256 tile.  CTA r of the pair loads rows [128 r, 128 r + 128) of the
+// tile's A panel and columns [128 r, 128 r + 128) of its B panel (32 KB per
+// 64-token stage instead of 48 KB), and each CTA's tensor memory holds its
+// 128 rows x 256 columns of the accumulator.  The even CTA issues the MMAs
+// (M = 256, N = 256, K = 16), which read both CTAs' shared memory at the same
+// offsets.  Protocol:
+//   full[s]   (even CTA): its producer's expect_tx for both halves; both
+//             producers' TMA loads complete_tx on it;
+//   empty[s]  (each CTA): one arrival from the MMA thread's commit, so each
+//             producer may refill its half of the stage;
+//   tfull[a]  (each CTA): committed by the MMA thread after a chunk;
+//   tempty[a] (even CTA): one arrival per epilogue warp of both CTAs.
+// Loads use no multicast; the even CTA's barriers are reached through mapa
+// addresses.  The arithmetic per element (512-token chunks summed in fp32
+// registers, in token order) is the one-CTA kernel's.
+namespace tc2 {
+using namespace tc;
+
+constexpr int PM = 256;   // tile rows (128 per CTA)
+constexpr int HM = 128;
+constexpr int PN = 256;   // tile columns (128 loaded per CTA)
+constexpr int STAGES2 = 6;
+constexpr int HALF_STAGE = 2 * BOX_BYTES;   // 128 features x 64 tokens
+constexpr int STAGE2 = 2 * HALF_STAGE;      // A half + B half
+constexpr int EPI_WARPS = EPI_THREADS / 32;
+constexpr int SMEM2 = STAGES2 * STAGE2 + 1024 /*align*/ + 256 /*barriers*/;
+constexpr uint32_t IDESC2 = (1u << 4) | (1u << 7) | (1u << 10) | (1u << 15) | (1u << 16) |
+                            ((uint32_t)(PN >> 3) << 17) | ((uint32_t)(PM >> 4) << 24);
+
+__device__ __forceinline__ uint32_t cluster_rank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+// shared::cluster address of the same shared-memory offset in CTA `rank`
+__device__ __forceinline__ uint32_t peer_addr(const void* p, uint32_t rank) {
+  uint32_t out;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(out) : "r"(smem_u32(p)), "r"(rank));
+  return out;
+}
+__device__ __forceinline__ void cluster_sync() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n barrier.cluster.wait.acquire.aligned;" ::
+                   : "memory");
+}
+__device__ __forceinline__ void tma_load_pair(const CUtensorMap* map, uint32_t bar_cluster,
+                                              void* dst, int x, int y) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%2, %3}], [%4];" ::"r"(smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(bar_cluster)
+      : "memory");
+}
+__device__ __forceinline__ void umma_bf16_pair(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc,
+                                               uint32_t accum) {
+  asm volatile(
+      "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
+      " tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p;\n}" ::"r"(d_tmem),
+      "l"(adesc), "l"(bdesc), "r"(IDESC2), "r"(accum));
+}
+// one arrival on the barrier at this shared-memory offset in both CTAs of the
+// pair once this thread's earlier MMAs are complete (a commit, not a load)
+__device__ __forceinline__ void umma_commit_both(const uint64_t* bar) {
+  asm volatile(
+      "tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64"
+      " [%0], %1;" ::"r"(smem_u32(bar)),
+      "h"((uint16_t)0x3)
+      : "memory");
+}
+__device__ __forceinline__ void remote_arrive(uint32_t bar_cluster) {
+  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(bar_cluster)
+               : "memory");
+}
+
+// Column tile bn computes row tiles 0 .. col_height2 - 1 (256 rows each).
+__device__ __forceinline__ int col_height2(const Params& p, int bn) {
+  return p.symmetric ? min(p.mb, bn + 1) : p.mb;
+}
+// Same grouped order as the one-CTA kernel, in 256 x 256 tiles.
+__device__ __forceinline__ void tile_coords2(const Params& p, int t, int& bm, int& bn) {
+  for (int g0 = 0; g0 < p.nb; g0 += GROUP_COLS) {
+    const int g1 = min(p.nb, g0 + GROUP_COLS);
+    int cnt = 0;
+    for (int j = g0; j < g1; ++j) cnt += col_height2(p, j);
+    if (t >= cnt) {
+      t -= cnt;
+      continue;
+    }
+    int first = g0;
+    for (int r = 0; r < col_height2(p, g1 - 1); ++r) {
+      while (first < g1 && col_height2(p, first) <= r) ++first;
+      const int n = g1 - first;
+      if (t < n) {
+        bm = r;
+        bn = first + t;
+        return;
+      }
+      t -= n;
+    }
+  }
+  bm = 0;
+  bn = 0;
+}
+
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
+gemm_tn_pair_kernel(const __grid_constant__ CUtensorMap map_a,
+                    const __grid_constant__ CUtensorMap map_b, Params p) {
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                             ~uintptr_t(1023));
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + STAGES2 * STAGE2);
+  uint64_t* empty = full + STAGES2;
+  uint64_t* tfull = empty + STAGES2;
+  uint64_t* tempty = tfull + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tempty + 2);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  volatile int* epi_go = abort_flag + 1;
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const uint32_t rank = cluster_rank();
+  const bool leader = rank == 0;
+  const int cid = blockIdx.x >> 1, nclusters = gridDim.x >> 1;
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES2; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(&tfull[a], 1);
+      mbar_init(&tempty[a], 2 * EPI_WARPS);
+    }
+    *abort_flag = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&map_a)) : "memory");
+    asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&map_b)) : "memory");
+  }
+  if (warp == 1) {
+    // collective over the pair: warp 1 of both CTAs, same destination offset
+    asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                     smem_u32(tmem_slot)),
+                 "r"(TMEM_COLS));
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;");
+  }
+  fence_before();
+  cluster_sync();  // barriers initialised and the allocation visible in both CTAs
+  fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+  const int nkb = (int)((p.K + BK - 1) / BK);
+  const uint32_t full0 = peer_addr(&full[0], 0);      // the even CTA's barriers
+  const uint32_t tempty0 = peer_addr(&tempty[0], 0);
+
+  if (warp == 0) {
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      for (int t = cid; t < p.num_tiles && !*abort_flag; t += nclusters) {
+        int bm, bn;
+        tile_coords2(p, t, bm, bn);
+        for (int kb = 0; kb < nkb; ++kb) {
+          if (!mbar_wait(&empty[stage], phase ^ 1, abort_flag)) break;
+          if (leader) mbar_expect_tx(&full[stage], 2 * STAGE2);
+          const int k0 = kb * BK;
+          uint8_t* a_dst = smem + stage * STAGE2;
+          uint8_t* b_dst = a_dst + HALF_STAGE;
+          const uint32_t bar = full0 + 8u * (uint32_t)stage;
+          const int r0 = bm * PM + (int)rank * HM, c0 = bn * PN + (int)rank * HM;
+          tma_load_pair(&map_a, bar, a_dst, r0, k0);
+          tma_load_pair(&map_a, bar, a_dst + BOX_BYTES, r0 + 64, k0);
+          tma_load_pair(&map_b, bar, b_dst, c0, k0);
+          tma_load_pair(&map_b, bar, b_dst + BOX_BYTES, c0 + 64, k0);
+          if (++stage == STAGES2) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+      }
+      // every stage released by the MMA: no commit arrival is still on its
+      // way to this CTA's barriers when the pair tears down
+      for (int i = 0; i < STAGES2 && !*abort_flag; ++i) {
+        if (!mbar_wait(&empty[stage], phase ^ 1, abort_flag)) break;
+        if (++stage == STAGES2) {
+          stage = 0;
+          phase ^= 1;
+        }
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0 && leader) {
+      int stage = 0, acc = 0;
+      uint32_t phase = 0, acc_phase = 0;
+      bool ok = true;
+      for (int t = cid; ok && t < p.num_tiles && !*abort_flag; t += nclusters) {
+        for (int kc = 0; kc < nkb && ok; kc += CHUNK_KB) {
+          if (!mbar_wait(&tempty[acc], acc_phase ^ 1, abort_flag)) {
+            ok = false;
+            break;
+          }
+          fence_after();
+          const uint32_t d_tmem = tmem_base + (uint32_t)(acc * PN);
+          const int kend = min(nkb, kc + CHUNK_KB);
+          for (int kb = kc; kb < kend; ++kb) {
+            if (!mbar_wait(&full[stage], phase, abort_flag)) {
+              ok = false;
+              break;
+            }
+            fence_after();
+            const uint32_t a_base = smem_u32(smem + stage * STAGE2);
+            const uint32_t b_base = a_base + HALF_STAGE;
+#pragma unroll
+            for (int kk = 0; kk < BK / 16; ++kk) {
+              const uint64_t ad = make_desc(a_base + kk * 2048, BOX_BYTES, 1024);
+              const uint64_t bd = make_desc(b_base + kk * 2048, BOX_BYTES, 1024);
+              umma_bf16_pair(d_tmem, ad, bd, (kb > kc || kk > 0) ? 1u : 0u);
+            }
+            umma_commit_both(&empty[stage]);
+            if (++stage == STAGES2) {
+              stage = 0;
+              phase ^= 1;
+            }
+          }
+          if (!ok) break;
+          umma_commit_both(&tfull[acc]);
+          if (++acc == 2) {
+            acc = 0;
+            acc_phase ^= 1;
+          }
+        }
+      }
+    }
+  } else {
+    // epilogue warps 2..9 of each CTA: this CTA's 128 rows, 256 columns
+    const int quarter = warp & 3;
+    const int half = (warp - 2) >> 2;
+    const int row_in_tile = quarter * 32 + lane;
+    const uint32_t lane_addr = (uint32_t)(quarter * 32) << 16;
+    int acc = 0;
+    uint32_t acc_phase = 0;
+    bool ok = true;
+    uint32_t chunk = 0;
+    for (int t = cid; ok && t < p.num_tiles; t += nclusters) {
+      int bm, bn;
+      tile_coords2(p, t, bm, bn);
+      const int64_t row = (int64_t)bm * PM + (int64_t)rank * HM + row_in_tile;
+      const int64_t col0 = (int64_t)bn * PN + half * HALF_COLS;
+      const bool inside = row < p.M && col0 < p.N;
+      float* cp = p.c + row * p.ldc + col0;
+      const bool vec = inside && (col0 + HALF_COLS <= p.N) &&
+                       ((reinterpret_cast<uintptr_t>(cp) & 15) == 0);
+      float sum[HALF_COLS];
+      if (p.accumulate && vec) {
+#pragma unroll
+        for (int j = 0; j < HALF_COLS; j += 4) {
+          const float4 o = *reinterpret_cast<const float4*>(cp + j);
+          sum[j] = o.x;
+          sum[j + 1] = o.y;
+          sum[j + 2] = o.z;
+          sum[j + 3] = o.w;
+        }
+      } else {
+#pragma unroll
+        for (int j = 0; j < HALF_COLS; ++j)
+          sum[j] = (p.accumulate && inside && col0 + j < p.N) ? cp[j] : 0.f;
+      }
+      for (int kc = 0; kc < nkb; kc += CHUNK_KB) {
+        if (warp == 2) {
+          const bool got = mbar_wait(&tfull[acc], acc_phase, abort_flag);
+          if (lane == 0) epi_go[chunk & 1] = got ? 1 : 0;
+        }
+        asm volatile("bar.sync 1, %0;" ::"n"(EPI_THREADS) : "memory");
+        ok = epi_go[chunk & 1] != 0;
+        ++chunk;
+        if (!ok) break;
+        fence_after();
+#pragma unroll
+        for (int c = 0; c < HALF_COLS / 32; ++c) {
+          uint32_t r[32];
+          tmem_ld32(tmem_base + lane_addr + (uint32_t)(acc * PN + half * HALF_COLS + c * 32), r);
+#pragma unroll
+          for (int j = 0; j < 32; ++j) sum[c * 32 + j] += __uint_as_float(r[j]);
+        }
+        fence_before();
+        __syncwarp();
+        if (lane == 0) remote_arrive(tempty0 + 8u * (uint32_t)acc);
+        if (++acc == 2) {
+          acc = 0;
+          acc_phase ^= 1;
+        }
+      }
+      if (!ok) break;
+      if (vec) {
+#pragma unroll
+        for (int j = 0; j < HALF_COLS; j += 4)
+          *reinterpret_cast<float4*>(cp + j) = make_float4(sum[j], sum[j + 1], sum[j + 2], sum[j + 3]);
+      } else if (inside) {
+#pragma unroll
+        for (int j = 0; j < HALF_COLS; ++j)
+          if (col0 + j < p.N) cp[j] = sum[j];
+      }
+    }
+  }
+
+  // both CTAs done with the pair's shared memory and tensor memory
+  fence_before();
+  cluster_sync();
+  if (warp == 1) {
+    fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(tmem_base),
+                 "r"(TMEM_COLS));
+  }
+  cluster_sync();
+}
+
+
+int pair_setup(int* max_clusters) {
+  static int attr_device = -1, clusters = 0;
+  int dev = 0;
+  GQ_CHECK_CUDA(cudaGetDevice(&dev));
+  if (attr_device != dev) {
+    GQ_CHECK_CUDA(cudaFuncSetAttribute(gemm_tn_pair_kernel,
+                                       cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM2));
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(2, 1, 1);
+    cfg.blockDim = dim3(THREADS, 1, 1);
+    cfg.dynamicSmemBytes = SMEM2;
+    cudaLaunchAttribute attr;
+    attr.id = cudaLaunchAttributeClusterDimension;
+    attr.val.clusterDim.x = 2;
+    attr.val.clusterDim.y = 1;
+    attr.val.clusterDim.z = 1;
+    cfg.attrs = &attr;
+    cfg.numAttrs = 1;
+    GQ_CHECK_CUDA(cudaOccupancyMaxActiveClusters(&clusters, gemm_tn_pair_kernel, &cfg));
+    GQ_REQUIRE(clusters >= 1, "tcgen05 pair kernel: no cluster of two CTAs fits on this device");
+    attr_device = dev;
+  }
+  *max_clusters = clusters;
+  return GQ_OK;
+}
+
+// C (+)= A^T B with CTA pairs; same contract as tc::launch.
+int launch_pair(const void* xa, int64_t lda, const void* xb, int64_t ldb, int64_t K, int64_t M,
+                int64_t N, float* c, int64_t ldc, int accumulate, int symmetric, cudaStream_t st) {
+  if (K == 0) {
+    if (!accumulate) GQ_CHECK_CUDA(cudaMemset2DAsync(c, ldc * 4, 0, N * 4, M, st));
+    return GQ_OK;
+  }
+  CUtensorMap ma, mbm;
+  GQ_TRY(make_map(&ma, xa, K, M, lda));
+  GQ_TRY(make_map(&mbm, xb, K, N, ldb));
+  Params p;
+  p.c = c;
+  p.ldc = ldc;
+  p.M = M;
+  p.N = N;
+  p.K = K;
+  p.symmetric = symmetric;
+  p.accumulate = accumulate;
+  p.mb = (int)ceil_div(M, PM);
+  p.nb = (int)ceil_div(N, PN);
+  if (symmetric) {
+    int64_t cnt = 0;
+    for (int j = 0; j < p.nb; ++j) cnt += std::min(p.mb, j + 1);
+    p.num_tiles = (int)cnt;
+  } else {
+    p.num_tiles = p.mb * p.nb;
+  }
+  int max_clusters = 0;
+  GQ_TRY(pair_setup(&max_clusters));
+  const int clusters = std::max(1, std::min(std::min(p.num_tiles, cta_budget() / 2), max_clusters));
+  gemm_tn_pair_kernel<<<2 * clusters, THREADS, SMEM2, st>>>(ma, mbm, p);
+  return check_launch("tcgen05 gemm_tn pair");
+}
+
+}  // namespace tc2
+
+namespace tc {
+// CTA pairs where a cluster of two fits (bit-identical results), else one CTA
+// per tile.
+int launch(const void* xa, int64_t lda, const void* xb, int64_t ldb, int64_t K, int64_t M,
+           int64_t N, float* c, int64_t ldc, int accumulate, int symmetric, cudaStream_t st) {
+  int max_clusters = 0;
+  if (tc2::pair_setup(&max_clusters) == GQ_OK && max_clusters >= 1)
+    return tc2::launch_pair(xa, lda, xb, ldb, K, M, N, c, ldc, accumulate, symmetric, st);
+  (void)cudaGetLastError();  // the failed occupancy query is not this launch's error
+  return launch_single(xa, lda, xb, ldb, K, M, N, c, ldc, accumulate, symmetric, st);
+}
 }  // namespace tc
 
 int symmetrize_upper(float* h, int64_t d, int64_t ldh, cudaStream_t st);
