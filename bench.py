@@ -444,12 +444,13 @@ def run_ours(args, world, rank, local):
     traffic = args.syrk_traffic
     if traffic is None and top_d == 11008:
         # DRAM bytes of one d = 11008 launch from an ncu capture at 32768 tokens
-        # (7.668 GB read: X once per wave of the 1892 symmetric tiles; 0.245 GB
-        # of H written), scaled to this launch's tokens
-        traffic = 7.668e9 * args.tokens / 32768 + 0.245e9
+        # (6.146 GB read: each wave of the 946 pair tiles streams the X columns
+        # of its tile group; 0.245 GB of H written), scaled to this launch's tokens
+        traffic = 6.146e9 * args.tokens / 32768 + 0.245e9
     peak = peaks.get("bf16_tflops_sustained", peaks.get("bf16_tflops"))
     roofline = {"bound": "tensor",
-                "kernel": f"gq_tc gemm_tn_kernel (H = X^T X, symmetric tiles), d = {top_d}",
+                "kernel": f"gq_tc gemm_tn_pair_kernel (H = X^T X, symmetric 256 x 256 tiles "
+                          f"on CTA pairs), d = {top_d}",
                 "achieved": top_tflops, "peak": peak, "unit": "TFLOP/s", "frac": top_tflops / peak,
                 "peak_kind": f"{peak_kind} bf16 sustained (kernel timed inside a long step)",
                 "algorithmic": f"tokens*d*(d+1) = {syrk_flop[top]:.4g} flops per launch",
