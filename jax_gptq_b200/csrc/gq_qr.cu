@@ -3,17 +3,19 @@
 // Working copy: the matrix transposed into column-major order, at[c][r]
 // (ld = m), so pivot columns, swaps, Householder vectors and column norms are
 // contiguous.  Per panel of P columns starting at k:
-//   * one single-CTA "step" kernel per pivot: choose the pivot from the norm
-//     metadata, swap whole columns, form the reflector, append it to the
-//     compact WY pair (yt = Y^T, P x (m-k); T, P x P) and produce the vector
+//   * one "step" kernel per pivot, on a cluster of eight CTAs that split the
+//     column's rows: choose the pivot from the norm metadata, swap whole
+//     columns, form the reflector, append it to the compact WY pair
+//     (yt = Y^T, P x (m-k); T, P x P) and produce the vector
 //     left = (y_r T^T) Y^T that exposes row r of the transformed trailing
 //     block;
 //   * one all-SM "exposed row" kernel: e_c = B[r][c] - left . B[:, c] for the
 //     deferred (stale) trailing columns, and the norm downdate
 //     norms_c = max(norms_c - e_c^2, 0) -- the BLAS-2 pass that reads the
 //     whole trailing block every step;
-//   * at the panel end the compact-WY update B <- B - Y (T^T (Y^T B)) (three
-//     fp32 GEMMs) and an exact norm refresh from rows >= panel end.
+//   * at the panel end the compact-WY update B <- B - Y (T^T (Y^T B)) (two
+//     tensor-core fp32 GEMMs around a small T application) and an exact norm
+//     refresh from rows >= panel end.
 //
 // semantics = 0 ("reference") reproduces _factor_panel_compiled
 // (:1479-1589) and the driver (:1627-1722) exactly, including:
@@ -46,8 +48,6 @@ int sgemm(int ta, int tb, int64_t M, int64_t N, int64_t K, float alpha, const fl
 namespace qr {
 
 constexpr float ZERO_TOL_SQ = 1e-24f;  // ZERO_TOL ** 2 (:52-53)
-constexpr int STEP_THREADS = 1024;
-constexpr int STEP_WARPS = STEP_THREADS / 32;
 constexpr int MAX_P = 256;             // widest panel (reference semantics honour panel_size)
 constexpr int INTENDED_P = 64;         // panel width used by the intended (exact) factorization
 
@@ -160,26 +160,90 @@ struct StepArgs {
   int semantics;   // 0 reference, 1 intended
 };
 
-// One pivot step (single CTA).  Dynamic shared memory: v and col, (m-k) floats each.
-__global__ void __launch_bounds__(STEP_THREADS) qr_step_kernel(StepArgs a) {
+// ---------------------------------------------------------------------------
+// The pivot step on a cluster of CL CTAs.  The step's L-long vectors (the
+// pivot column, the reflector v, the rows of Y^T) are split into CL row
+// slices, one per CTA, so the four passes over Y^T a step makes (Y^T col,
+// Y z, Y^T v, left = s Y^T) read L2 through CL SMs instead of one.  Dot
+// products are formed per slice and summed across the cluster through
+// distributed shared memory in rank order, so every CTA holds the same sums;
+// the small P-sized work (pivot choice, T, the exposed-row weights) is done
+// redundantly in every CTA and written once.  Compared with doing the step
+// in one CTA, only the grouping of the L-long sums differs.
+constexpr int CL = 8;            // CTAs per cluster (portable size)
+constexpr int CT = 512;          // threads per CTA
+constexpr int CTW = CT / 32;
+
+__device__ __forceinline__ uint32_t smem_addr(const void* p) {
+  return (uint32_t)__cvta_generic_to_shared(p);
+}
+__device__ __forceinline__ float ld_cluster(const float* local, uint32_t rank) {
+  uint32_t a;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(a) : "r"(smem_addr(local)), "r"(rank));
+  float v;
+  asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(a) : "memory");
+  return v;
+}
+__device__ __forceinline__ void cluster_barrier() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n barrier.cluster.wait.acquire.aligned;" ::
+                   : "memory");
+}
+__device__ __forceinline__ int64_t i64min(int64_t x, int64_t y) { return x < y ? x : y; }
+__device__ __forceinline__ int64_t i64max(int64_t x, int64_t y) { return x > y ? x : y; }
+__device__ __forceinline__ uint32_t cta_rank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+
+// Double-buffered partial vectors: each CTA writes its partials into
+// part[buf], the cluster synchronizes, and every CTA sums the CL partial
+// vectors in rank order into out.  A buffer is written again only two
+// reductions later, after every CTA has passed the barrier that follows its
+// reads.  buf is a per-thread copy, flipped in step by every thread.
+__device__ void cluster_sum(float (*part)[MAX_P + 8], int& buf, int count, float* out) {
+  cluster_barrier();
+  const float* src = part[buf];
+  for (int t = threadIdx.x; t < count; t += blockDim.x) {
+    float s = ld_cluster(src + t, 0);
+    for (uint32_t q = 1; q < CL; ++q) s = __fadd_rn(s, ld_cluster(src + t, q));
+    out[t] = s;
+  }
+  __syncthreads();
+  buf ^= 1;
+}
+
+__global__ void __cluster_dims__(CL, 1, 1) __launch_bounds__(CT)
+qr_step_cluster_kernel(StepArgs a) {
   extern __shared__ __align__(16) float sm[];
-  __shared__ float redv[STEP_WARPS];
-  __shared__ int redi[STEP_WARPS];
-  __shared__ float sw[MAX_P + 1];   // T-column work / z vectors
+  __shared__ float redv[CTW];
+  __shared__ int redi[CTW];
+  __shared__ float sw[MAX_P + 1];
   __shared__ float sw2[MAX_P + 1];
+  __shared__ float sums[MAX_P + 8];
+  __shared__ float part[2][MAX_P + 8];
   __shared__ int s_flag;
 
   Ctrl* ctrl = a.ctrl;
   if (ctrl->done) return;
+  if (a.semantics == 1 && ctrl->early_end) {
+    if (cta_rank() == 0 && threadIdx.x == 0) ctrl->done = 1;
+    return;
+  }
   const int64_t m = a.m, n = a.n, k = a.k, j = a.j, pe = a.pe;
   const int64_t L = m - k;
   const int lj = (int)(j - k);
   const int P = a.P;
-  float* v = sm;
-  float* col = sm + L;
+  const uint32_t rank = cta_rank();
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  // this CTA's rows [r0, r1) of the panel-local range [0, L)
+  const int64_t Ls = (L + CL - 1) / CL;
+  const int64_t r0 = i64min(L, (int64_t)rank * Ls), r1 = i64min(L, r0 + Ls);
+  float* v = sm;        // v[r - r0]
+  float* col = sm + Ls;  // col[r - r0]
+  int buf = 0;
 
-  // 1. "smallest": stop when no remaining norm exceeds ZERO_TOL^2 (:1562-1570)
+  // 1. "smallest": stop when no remaining norm exceeds ZERO_TOL^2 (every CTA alike)
   if (a.smallest) {
     int any = 0;
     for (int64_t c = j + tid; c < n; c += blockDim.x) any |= (a.norms[c] > ZERO_TOL_SQ);
@@ -188,11 +252,12 @@ __global__ void __launch_bounds__(STEP_THREADS) qr_step_kernel(StepArgs a) {
     if (any) atomicOr(&s_flag, 1);
     __syncthreads();
     if (!s_flag) {
-      if (tid == 0) ctrl->done = 1;
+      if (rank == 0 && tid == 0) ctrl->done = 1;
       return;
     }
   }
-  // 2. pivot (:202-219): first argmax / argmin over columns >= j
+  // 2. pivot: first argmax / argmin over columns >= j (every CTA alike)
+  int p;
   {
     const bool larger = !a.smallest;
     float bv = larger ? -INFINITY : INFINITY;
@@ -202,66 +267,91 @@ __global__ void __launch_bounds__(STEP_THREADS) qr_step_kernel(StepArgs a) {
       if (a.smallest && !(x > ZERO_TOL_SQ)) x = INFINITY;
       better(bv, bi, x, (int)c, larger);
     }
-    int p = block_arg(bv, bi, larger, redv, redi);
+    p = block_arg(bv, bi, larger, redv, redi);
     if (p == 0x7fffffff) p = (int)j;
-    // 3. swap whole columns j and p (:264-283)
-    if (p != j) {
-      float* cj = a.at + j * m;
-      float* cp = a.at + (int64_t)p * m;
-      for (int64_t r = tid; r < m; r += blockDim.x) {
-        float x = cj[r];
-        cj[r] = cp[r];
-        cp[r] = x;
-      }
-      if (tid == 0) {
-        int32_t tp = a.perm[j];
-        a.perm[j] = a.perm[p];
-        a.perm[p] = tp;
-        float tn = a.norms[j];
-        a.norms[j] = a.norms[p];
-        a.norms[p] = tn;
-        if (a.normref) {
-          float tr = a.normref[j];
-          a.normref[j] = a.normref[p];
-          a.normref[p] = tr;
-        }
+  }
+  // every CTA has read the norms before CTA 0 swaps two of them
+  cluster_barrier();
+  // 3. swap whole columns j and p: this CTA's slice of rows [k, m) and a share of [0, k)
+  if (p != j) {
+    float* cj = a.at + j * m;
+    float* cp = a.at + (int64_t)p * m;
+    for (int64_t r = k + r0 + tid; r < k + r1; r += blockDim.x) {
+      float x = cj[r];
+      cj[r] = cp[r];
+      cp[r] = x;
+    }
+    const int64_t ks = (k + CL - 1) / CL;
+    for (int64_t r = i64min(k, rank * ks) + tid; r < i64min(k, (rank + 1) * ks);
+         r += blockDim.x) {
+      float x = cj[r];
+      cj[r] = cp[r];
+      cp[r] = x;
+    }
+    if (rank == 0 && tid == 0) {
+      int32_t tp = a.perm[j];
+      a.perm[j] = a.perm[p];
+      a.perm[p] = tp;
+      float tn = a.norms[j];
+      a.norms[j] = a.norms[p];
+      a.norms[p] = tn;
+      if (a.normref) {
+        float tr = a.normref[j];
+        a.normref[j] = a.normref[p];
+        a.normref[p] = tr;
       }
     }
-    __syncthreads();
   }
+  __syncthreads();
 
-  // 4. the column the reflector is built from
+  // 4. the column the reflector is built from (this CTA's rows)
   const int64_t src = (a.semantics == 0) ? (j - k) : j;
-  for (int64_t r = tid; r < L; r += blockDim.x) col[r] = a.at[src * m + k + r];
+  for (int64_t r = r0 + tid; r < r1; r += blockDim.x) col[r - r0] = a.at[src * m + k + r];
   __syncthreads();
   if (a.semantics == 1 && lj > 0) {
     // bring the deferred pivot column up to date: col -= Y (T^T (Y^T col))
-    for (int i = warp; i < lj; i += STEP_WARPS) {
+    for (int i = warp; i < lj; i += CTW) {
       const float* yi = a.yt + (int64_t)i * L;
       float s = 0.f;
-      for (int64_t r = lane; r < L; r += 32) s = fmaf(yi[r], col[r], s);
+      for (int64_t r = r0 + lane; r < r1; r += 32) s = fmaf(yi[r], col[r - r0], s);
       s = warp_sum(s);
-      if (lane == 0) sw[i] = s;
+      if (lane == 0) part[buf][i] = s;
     }
-    __syncthreads();
+    cluster_sum(part, buf, lj, sums);
     if (tid < lj) {
       float z = 0.f;
-      for (int l = 0; l <= tid; ++l) z = fmaf(a.t[l * P + tid], sw[l], z);
+      for (int l = 0; l <= tid; ++l) z = fmaf(a.t[l * P + tid], sums[l], z);
       sw2[tid] = z;
     }
     __syncthreads();
-    for (int64_t r = tid; r < L; r += blockDim.x) {
+    for (int64_t r = r0 + tid; r < r1; r += blockDim.x) {
       float s = 0.f;
       for (int i = 0; i < lj; ++i) s = fmaf(a.yt[(int64_t)i * L + r], sw2[i], s);
-      col[r] = col[r] - s;
+      col[r - r0] = col[r - r0] - s;
     }
     __syncthreads();
   }
-  // Householder vector (:327-356): sigma over rows below lj
-  float part = 0.f;
-  for (int64_t r = lj + 1 + tid; r < L; r += blockDim.x) part = fmaf(col[r], col[r], part);
-  const float sigma = block_sum(part, redv);
-  const float x0 = col[lj];
+  // Householder vector: sigma over rows below lj; x0 = col[lj] from its owner
+  {
+    float mine = 0.f;
+    for (int64_t r = i64max(r0, lj + 1) + tid; r < r1; r += blockDim.x)
+      mine = fmaf(col[r - r0], col[r - r0], mine);
+    const float blk = block_sum(mine, redv);
+    if (tid == 0) {
+      part[buf][0] = blk;
+      part[buf][1] = (lj >= r0 && lj < r1) ? col[lj - r0] : 0.f;
+    }
+  }
+  cluster_barrier();
+  float sigma, x0;
+  {
+    const float* src_part = part[buf];
+    sigma = ld_cluster(src_part, 0);
+    for (uint32_t q = 1; q < CL; ++q) sigma = __fadd_rn(sigma, ld_cluster(src_part, q));
+    x0 = ld_cluster(src_part + 1, (uint32_t)(lj / Ls));
+  }
+  __syncthreads();
+  buf ^= 1;
   float tau_j, alpha, beta = 1.f;
   if (sigma == 0.f) {
     tau_j = 0.f;
@@ -272,80 +362,98 @@ __global__ void __launch_bounds__(STEP_THREADS) qr_step_kernel(StepArgs a) {
     beta = __fsub_rn(x0, alpha);
     tau_j = __fdiv_rn(-beta, alpha);
   }
-  for (int64_t r = tid; r < L; r += blockDim.x) {
+  for (int64_t r = r0 + tid; r < r1; r += blockDim.x) {
     float vr;
     if (r == lj) vr = 1.f;
     else if (r < lj || sigma == 0.f) vr = 0.f;
-    else vr = __fdiv_rn(col[r], beta);
-    v[r] = vr;
+    else vr = __fdiv_rn(col[r - r0], beta);
+    v[r - r0] = vr;
     a.yt[(int64_t)lj * L + r] = vr;
   }
   __syncthreads();
-  // 5. append to T (:674-726): T[:lj, lj] = T_prev (-tau Y_prev^T v); T[lj, lj] = tau
-  for (int i = warp; i < lj; i += STEP_WARPS) {
-    const float* yi = a.yt + (int64_t)i * L;
-    float s = 0.f;
-    for (int64_t r = lane; r < L; r += 32) s = fmaf(yi[r], v[r], s);
-    s = warp_sum(s);
-    if (lane == 0) sw[i] = -tau_j * s;
+  // 5. append to T: T[:lj, lj] = T_prev (-tau Y_prev^T v); T[lj, lj] = tau
+  if (lj > 0) {
+    for (int i = warp; i < lj; i += CTW) {
+      const float* yi = a.yt + (int64_t)i * L;
+      float s = 0.f;
+      for (int64_t r = r0 + lane; r < r1; r += 32) s = fmaf(yi[r], v[r - r0], s);
+      s = warp_sum(s);
+      if (lane == 0) part[buf][i] = s;
+    }
+    cluster_sum(part, buf, lj, sums);
+    if (tid < lj) sw[tid] = -tau_j * sums[tid];
+    __syncthreads();
+    if (tid < lj) {
+      float s = 0.f;
+      for (int l = tid; l < lj; ++l) s = fmaf(a.t[tid * P + l], sw[l], s);
+      sw2[tid] = s;
+    }
+    __syncthreads();
   }
-  __syncthreads();
-  if (tid < lj) {
-    float s = 0.f;
-    for (int l = tid; l < lj; ++l) s = fmaf(a.t[tid * P + l], sw[l], s);
-    sw2[tid] = s;
-  }
-  __syncthreads();
-  if (tid < lj) a.t[tid * P + lj] = sw2[tid];
-  if (tid == 0) {
-    a.t[lj * P + lj] = tau_j;
-    a.tau[lj] = tau_j;
+  if (rank == 0) {
+    if (tid < lj) a.t[tid * P + lj] = sw2[tid];
+    if (tid == 0) {
+      a.t[lj * P + lj] = tau_j;
+      a.tau[lj] = tau_j;
+    }
   }
   __syncthreads();
 
   if (a.semantics == 0) {
-    // 6. eager reflector on panel columns j..pe-1 (:786-815)
-    for (int64_t c = j + warp; c < pe; c += STEP_WARPS) {
-      float* cc = a.at + c * m + k;
+    // 6. eager reflector on panel columns j..pe-1
+    const int nc = (int)(pe - j);
+    for (int ci = warp; ci < nc; ci += CTW) {
+      const float* cc = a.at + (j + ci) * m + k;
       float s = 0.f;
-      for (int64_t r = lane; r < L; r += 32) s = fmaf(v[r], cc[r], s);
+      for (int64_t r = r0 + lane; r < r1; r += 32) s = fmaf(v[r - r0], cc[r], s);
       s = warp_sum(s);
-      const float wc = tau_j * s;
-      for (int64_t r = lane; r < L; r += 32) cc[r] = __fsub_rn(cc[r], __fmul_rn(v[r], wc));
+      if (lane == 0) part[buf][ci] = s;
+    }
+    cluster_sum(part, buf, nc, sums);
+    for (int ci = warp; ci < nc; ci += CTW) {
+      float* cc = a.at + (j + ci) * m + k;
+      const float wc = tau_j * sums[ci];
+      for (int64_t r = r0 + lane; r < r1; r += 32)
+        cc[r] = __fsub_rn(cc[r], __fmul_rn(v[r - r0], wc));
     }
     __syncthreads();
   }
   // pivot column: alpha on the diagonal, zeros below; in the intended
-  // factorization rows k..j-1 take the brought-up-to-date values (its R entries)
-  for (int64_t r = tid; r < L; r += blockDim.x) {
+  // factorization rows k..j-1 take the brought-up-to-date values
+  for (int64_t r = r0 + tid; r < r1; r += blockDim.x) {
     if (r >= lj) a.at[j * m + k + r] = (r == lj) ? alpha : 0.f;
-    else if (a.semantics == 1) a.at[j * m + k + r] = col[r];
+    else if (a.semantics == 1) a.at[j * m + k + r] = col[r - r0];
   }
-  __syncthreads();
+  // the reflector row, T and the updated panel columns visible to every CTA
+  cluster_barrier();
 
   const int64_t nxt = j + 1;
   if (a.semantics == 0 && nxt < n && nxt < pe) {
-    // 7a. panel-column norm metadata (:1048-1092)
+    // 7a. panel-column norm metadata: exact every 8 steps, else downdated
     const bool refresh = ((nxt - k) % 8) == 0;
-    for (int64_t c = nxt + warp; c < pe; c += STEP_WARPS) {
-      const float* cc = a.at + c * m;
-      float cur = a.norms[c];
-      if (refresh) {
+    const int nc = (int)(pe - nxt);
+    if (refresh) {
+      for (int ci = warp; ci < nc; ci += CTW) {
+        const float* cc = a.at + (nxt + ci) * m + k;
         float s = 0.f;
-        for (int64_t r = nxt + lane; r < m; r += 32) s = fmaf(cc[r], cc[r], s);
+        for (int64_t r = i64max(r0, nxt - k) + lane; r < r1; r += 32)
+          s = fmaf(cc[r], cc[r], s);
         s = warp_sum(s);
-        cur = s;
-      } else {
-        float row = cc[j];
-        cur = fmaxf(__fsub_rn(cur, __fmul_rn(row, row)), 0.f);
+        if (lane == 0) part[buf][ci] = s;
       }
-      if (lane == 0) a.norms[c] = cur;
+      cluster_sum(part, buf, nc, sums);
+      if (rank == 0)
+        for (int ci = tid; ci < nc; ci += blockDim.x) a.norms[nxt + ci] = sums[ci];
+    } else if (rank == 0) {
+      for (int ci = tid; ci < nc; ci += blockDim.x) {
+        const float row = a.at[(nxt + ci) * m + j];
+        a.norms[nxt + ci] = fmaxf(__fsub_rn(a.norms[nxt + ci], __fmul_rn(row, row)), 0.f);
+      }
     }
   }
   // 7b. the vector exposing one row of the transformed deferred block
   const bool exposes = (a.semantics == 0) ? (nxt < n && pe < n) : (nxt < n);
   if (exposes) {
-    // reference: the global step index is used as the panel-local row (clamped)
     int64_t rs = lj;
     if (a.semantics == 0) rs = (j < 0) ? 0 : ((j > L - 1) ? L - 1 : j);
     if (tid < P) {
@@ -354,14 +462,16 @@ __global__ void __launch_bounds__(STEP_THREADS) qr_step_kernel(StepArgs a) {
       sw[tid] = s;  // row_weights = y_r T^T
     }
     __syncthreads();
-    for (int64_t r = tid; r < L; r += blockDim.x) {
+    for (int64_t r = r0 + tid; r < r1; r += blockDim.x) {
       float s = 0.f;
       for (int i = 0; i < P; ++i) s = fmaf(sw[i], a.yt[(int64_t)i * L + r], s);
       a.left[r] = s;
     }
-    if (tid == 0) ctrl->row_sel = (int)rs;
+    if (rank == 0 && tid == 0) ctrl->row_sel = (int)rs;
   }
-  if (tid == 0) ctrl->active = ctrl->active + 1;
+  if (rank == 0 && tid == 0) ctrl->active = ctrl->active + 1;
+  // no CTA leaves while another may still read its shared memory
+  cluster_barrier();
 }
 
 // Exposed-row downdate over deferred columns [c0, n): warp per column.
@@ -401,11 +511,6 @@ __global__ void exposed_row_kernel(const float* __restrict__ at, int64_t m, int6
   }
 }
 
-// After a step: intended panels stop once a downdate lost precision.
-__global__ void end_check_kernel(Ctrl* ctrl) {
-  if (ctrl->early_end) ctrl->done = 1;
-}
-
 __global__ void reset_ctrl_kernel(Ctrl* ctrl) {
   ctrl->active = 0;
   ctrl->done = 0;
@@ -436,6 +541,7 @@ struct Work {
   float* left;
   float* z;
   float* z2;
+  float* y;
   Ctrl* ctrl;
 };
 
@@ -450,21 +556,9 @@ int64_t ws_bytes(int64_t m, int64_t n, int P) {
   b += align256(n * 4) * 2;          // norms, normref
   b += align256(m * 4);              // left
   b += align256(n * (int64_t)P * 4) * 2;  // z, z2
+  b += align256(m * (int64_t)P * 4);      // y
   b += align256(sizeof(Ctrl));
   return b;
-}
-
-// The step kernel's shared-memory opt-in, once per device.
-int step_kernel_setup() {
-  static int attr_device = -1;
-  int dev = 0;
-  GQ_CHECK_CUDA(cudaGetDevice(&dev));
-  if (attr_device != dev) {
-    GQ_CHECK_CUDA(cudaFuncSetAttribute(qr_step_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                       200 * 1024));
-    attr_device = dev;
-  }
-  return GQ_OK;
 }
 
 Work carve(void* ws, int64_t m, int64_t n, int P) {
@@ -479,23 +573,40 @@ Work carve(void* ws, int64_t m, int64_t n, int P) {
   w.left = reinterpret_cast<float*>(p); p += align256(m * 4);
   w.z = reinterpret_cast<float*>(p); p += align256(n * (int64_t)P * 4);
   w.z2 = reinterpret_cast<float*>(p); p += align256(n * (int64_t)P * 4);
+  w.y = reinterpret_cast<float*>(p); p += align256(m * (int64_t)P * 4);
   w.ctrl = reinterpret_cast<Ctrl*>(p);
   return w;
 }
 
 // B <- B - Y (T^T (Y^T B)) for deferred columns [c0, n), rows k..m-1 (width w).
+// zt2[c][i] = sum_{l <= i} T[l][i] z[l][c]   (z: w x nc, ld nc; zt2: nc x w, ld P)
+__global__ void apply_t_kernel(const float* __restrict__ z, int64_t nc, int w,
+                               const float* __restrict__ t, int P, float* __restrict__ zt2) {
+  const int64_t c = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
+  if (c >= nc) return;
+  for (int i = 0; i < w; ++i) {
+    float s = 0.f;
+    for (int l = 0; l <= i; ++l) s = fmaf(z[(int64_t)l * nc + c], t[l * P + i], s);
+    zt2[c * P + i] = s;
+  }
+}
+
+// B <- B - Y (T^T (Y^T B)) on the deferred columns, as two K-major products
+// (tensor cores where the shapes allow) around a small T application:
+//   Z = Y^T B (w x nc), Zt2 = (T^T Z)^T (nc x w), Bt -= Zt2 Y^T with Y = yt^T.
 int apply_panel(Work& W, int64_t m, int64_t n, int64_t k, int w, int P, int64_t c0,
                 cudaStream_t st) {
   if (c0 >= n || w <= 0) return GQ_OK;
   const int64_t L = m - k, nc = n - c0;
   float* bt = W.at + c0 * m + k;  // nc x L, ld m
-  // Zt = Bt Y  (Y = yt^T):  nc x w
-  GQ_TRY(sgemm(0, 1, nc, w, L, 1.f, bt, m, W.yt, L, 0.f, W.z, P, 0, st));
-  // Zt' = Zt T  (z' = T^T z)
-  GQ_TRY(sgemm(0, 0, nc, w, w, 1.f, W.z, P, W.t, P, 0.f, W.z2, P, 0, st));
-  // Bt -= Zt' yt
-  GQ_TRY(sgemm(0, 0, nc, L, w, -1.f, W.z2, P, W.yt, L, 1.f, bt, m, 0, st));
-  return GQ_OK;
+  GQ_TRY(sgemm(0, 1, w, nc, L, 1.f, W.yt, L, bt, m, 0.f, W.z, nc, 0, st));
+  apply_t_kernel<<<(unsigned)ceil_div(nc, 128), 128, 0, st>>>(W.z, nc, w, W.t, P, W.z2);
+  GQ_TRY(check_launch("apply_t"));
+  // y = yt^T: L x w, ld P
+  transpose_kernel<<<dim3((unsigned)ceil_div(L, 32), (unsigned)ceil_div(w, 32)), dim3(32, 8), 0,
+                     st>>>(W.yt, w, L, L, W.y, P);
+  GQ_TRY(check_launch("transpose_y"));
+  return sgemm(0, 1, nc, L, w, -1.f, W.z2, P, W.y, P, 1.f, bt, m, 0, st);
 }
 
 int norms_from(Work& W, int64_t m, int64_t n, int64_t r0, bool keep_ref, cudaStream_t st) {
@@ -515,7 +626,6 @@ int factor_panel(Work& W, int64_t m, int64_t n, int64_t k, int P, int smallest, 
   GQ_CHECK_CUDA(cudaMemsetAsync(W.tau, 0, (size_t)P * 4, st));
   reset_ctrl_kernel<<<1, 1, 0, st>>>(W.ctrl);
   GQ_TRY(check_launch("reset_ctrl"));
-  const size_t smem = (size_t)L * 8;
   const int gemv_blocks = std::max(1, sm_count() * 4);
   const float tol3z = 0.000244140625f;  // sqrt(2^-24): LAPACK's xLAQPS recompute threshold
   for (int64_t j = k; j < pe; ++j) {
@@ -524,7 +634,7 @@ int factor_panel(Work& W, int64_t m, int64_t n, int64_t k, int P, int smallest, 
     a.yt = W.yt; a.t = W.t; a.tau = W.tau; a.norms = W.norms; a.perm = perm; a.left = W.left;
     a.normref = W.normref;
     a.ctrl = W.ctrl; a.smallest = smallest; a.semantics = semantics;
-    qr_step_kernel<<<1, STEP_THREADS, smem, st>>>(a);
+    qr_step_cluster_kernel<<<CL, CT, 2 * (size_t)((L + CL - 1) / CL) * 4, st>>>(a);
     GQ_TRY(check_launch("qr_step"));
     const int64_t c0 = (semantics == 0) ? pe : j + 1;
     const bool exposes = (semantics == 0) ? (j + 1 < n && pe < n) : (j + 1 < n);
@@ -533,10 +643,6 @@ int factor_panel(Work& W, int64_t m, int64_t n, int64_t k, int P, int smallest, 
                                                        semantics == 1 ? W.normref : nullptr,
                                                        W.ctrl, tol3z);
       GQ_TRY(check_launch("exposed_row"));
-    }
-    if (semantics == 1) {
-      end_check_kernel<<<1, 1, 0, st>>>(W.ctrl);
-      GQ_TRY(check_launch("end_check"));
     }
   }
   Ctrl h;
@@ -581,7 +687,6 @@ int gq_qrcp(float* a, int64_t m, int64_t n, int64_t lda, int panel_size, int piv
   GQ_REQUIRE(v_out == nullptr || ldv >= limit, "gq_qrcp: ldv too small");
   cudaStream_t st = as_stream(stream);
   qr::Work W = qr::carve(workspace, m, n, P);
-  GQ_TRY(qr::step_kernel_setup());
   dim3 tb(32, 8);
   qr::transpose_kernel<<<dim3((unsigned)ceil_div(n, 32), (unsigned)ceil_div(m, 32)), tb, 0, st>>>(
       a, m, n, lda, W.at, m);
@@ -643,7 +748,6 @@ int gq_qr_factor_panel(float* a, int64_t m, int64_t n, int64_t lda, int32_t* per
   GQ_REQUIRE(workspace_bytes >= gq_qrcp_workspace_size(m, n, P), "gq_qr_factor_panel: workspace too small");
   cudaStream_t st = as_stream(stream);
   qr::Work W = qr::carve(workspace, m, n, P);
-  GQ_TRY(qr::step_kernel_setup());
   dim3 tb(32, 8);
   qr::transpose_kernel<<<dim3((unsigned)ceil_div(n, 32), (unsigned)ceil_div(m, 32)), tb, 0, st>>>(
       a, m, n, lda, W.at, m);
