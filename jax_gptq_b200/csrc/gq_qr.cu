@@ -215,6 +215,10 @@ __device__ void cluster_sum(float (*part)[MAX_P + 8], int& buf, int count, float
 
 __global__ void __cluster_dims__(CL, 1, 1) __launch_bounds__(CT)
 qr_step_cluster_kernel(StepArgs a) {
+  // launched as a programmatic dependent of the previous kernel: wait for it
+  // to complete, then let the next kernel be scheduled behind this one
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+  asm volatile("griddepcontrol.launch_dependents;");
   extern __shared__ __align__(16) float sm[];
   __shared__ float redv[CTW];
   __shared__ int redi[CTW];
@@ -479,6 +483,8 @@ __global__ void exposed_row_kernel(const float* __restrict__ at, int64_t m, int6
                                    int64_t c0, const float* __restrict__ left,
                                    float* __restrict__ norms, const float* __restrict__ normref,
                                    Ctrl* ctrl, float tol) {
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+  asm volatile("griddepcontrol.launch_dependents;");
   if (ctrl->done) return;
   const int lane = threadIdx.x & 31;
   const int64_t L = m - k;
@@ -579,16 +585,16 @@ Work carve(void* ws, int64_t m, int64_t n, int P) {
 }
 
 // B <- B - Y (T^T (Y^T B)) for deferred columns [c0, n), rows k..m-1 (width w).
-// zt2[c][i] = sum_{l <= i} T[l][i] z[l][c]   (z: w x nc, ld nc; zt2: nc x w, ld P)
+// zt2[c][i] = sum_{l <= i} T[l][i] z[l][c]   (z: w x nc, ld nc; zt2: nc x w, ld P);
+// one thread per (c, i), i = blockIdx.y
 __global__ void apply_t_kernel(const float* __restrict__ z, int64_t nc, int w,
                                const float* __restrict__ t, int P, float* __restrict__ zt2) {
   const int64_t c = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
+  const int i = blockIdx.y;
   if (c >= nc) return;
-  for (int i = 0; i < w; ++i) {
-    float s = 0.f;
-    for (int l = 0; l <= i; ++l) s = fmaf(z[(int64_t)l * nc + c], t[l * P + i], s);
-    zt2[c * P + i] = s;
-  }
+  float s = 0.f;
+  for (int l = 0; l <= i; ++l) s = fmaf(z[(int64_t)l * nc + c], t[l * P + i], s);
+  zt2[c * P + i] = s;
 }
 
 // B <- B - Y (T^T (Y^T B)) on the deferred columns, as two K-major products
@@ -600,7 +606,8 @@ int apply_panel(Work& W, int64_t m, int64_t n, int64_t k, int w, int P, int64_t 
   const int64_t L = m - k, nc = n - c0;
   float* bt = W.at + c0 * m + k;  // nc x L, ld m
   GQ_TRY(sgemm(0, 1, w, nc, L, 1.f, W.yt, L, bt, m, 0.f, W.z, nc, 0, st));
-  apply_t_kernel<<<(unsigned)ceil_div(nc, 128), 128, 0, st>>>(W.z, nc, w, W.t, P, W.z2);
+  apply_t_kernel<<<dim3((unsigned)ceil_div(nc, 128), (unsigned)w), 128, 0, st>>>(W.z, nc, w, W.t,
+                                                                                P, W.z2);
   GQ_TRY(check_launch("apply_t"));
   // y = yt^T: L x w, ld P
   transpose_kernel<<<dim3((unsigned)ceil_div(L, 32), (unsigned)ceil_div(w, 32)), dim3(32, 8), 0,
@@ -634,14 +641,30 @@ int factor_panel(Work& W, int64_t m, int64_t n, int64_t k, int P, int smallest, 
     a.yt = W.yt; a.t = W.t; a.tau = W.tau; a.norms = W.norms; a.perm = perm; a.left = W.left;
     a.normref = W.normref;
     a.ctrl = W.ctrl; a.smallest = smallest; a.semantics = semantics;
-    qr_step_cluster_kernel<<<CL, CT, 2 * (size_t)((L + CL - 1) / CL) * 4, st>>>(a);
+    // both kernels start with griddepcontrol.wait, so each may be launched
+    // while its predecessor is still running (programmatic dependent launch)
+    cudaLaunchAttribute pdl;
+    pdl.id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    pdl.val.programmaticStreamSerializationAllowed = 1;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(CL);
+    cfg.blockDim = dim3(CT);
+    cfg.dynamicSmemBytes = 2 * (size_t)((L + CL - 1) / CL) * 4;
+    cfg.stream = st;
+    cfg.attrs = &pdl;
+    cfg.numAttrs = 1;
+    GQ_CHECK_CUDA(cudaLaunchKernelEx(&cfg, qr_step_cluster_kernel, a));
     GQ_TRY(check_launch("qr_step"));
     const int64_t c0 = (semantics == 0) ? pe : j + 1;
     const bool exposes = (semantics == 0) ? (j + 1 < n && pe < n) : (j + 1 < n);
     if (exposes) {
-      exposed_row_kernel<<<gemv_blocks, 256, 0, st>>>(W.at, m, n, k, c0, W.left, W.norms,
-                                                       semantics == 1 ? W.normref : nullptr,
-                                                       W.ctrl, tol3z);
+      cfg.gridDim = dim3(gemv_blocks);
+      cfg.blockDim = dim3(256);
+      cfg.dynamicSmemBytes = 0;
+      const float* leftc = W.left;
+      const float* ref = semantics == 1 ? W.normref : nullptr;
+      GQ_CHECK_CUDA(cudaLaunchKernelEx(&cfg, exposed_row_kernel, (const float*)W.at, m, n, k, c0,
+                                       leftc, W.norms, ref, W.ctrl, tol3z));
       GQ_TRY(check_launch("exposed_row"));
     }
   }
