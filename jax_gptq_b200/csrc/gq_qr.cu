@@ -274,8 +274,10 @@ qr_step_cluster_kernel(StepArgs a) {
     p = block_arg(bv, bi, larger, redv, redi);
     if (p == 0x7fffffff) p = (int)j;
   }
-  // every CTA has read the norms before CTA 0 swaps two of them
-  cluster_barrier();
+  // every CTA has read the norms before CTA 0 swaps two of them (the
+  // intended factorization reads no norm later in the step, so there the
+  // scalar swap waits until the end and needs no barrier here)
+  if (a.semantics == 0) cluster_barrier();
   // 3. swap whole columns j and p: this CTA's slice of rows [k, m) and a share of [0, k)
   if (p != j) {
     float* cj = a.at + j * m;
@@ -292,7 +294,9 @@ qr_step_cluster_kernel(StepArgs a) {
       cj[r] = cp[r];
       cp[r] = x;
     }
-    if (rank == 0 && tid == 0) {
+  }
+  auto swap_scalars = [&]() {
+    if (p != j && rank == 0 && tid == 0) {
       int32_t tp = a.perm[j];
       a.perm[j] = a.perm[p];
       a.perm[p] = tp;
@@ -305,7 +309,8 @@ qr_step_cluster_kernel(StepArgs a) {
         a.normref[p] = tr;
       }
     }
-  }
+  };
+  if (a.semantics == 0) swap_scalars();
   __syncthreads();
 
   // 4. the column the reflector is built from (this CTA's rows)
@@ -428,8 +433,11 @@ qr_step_cluster_kernel(StepArgs a) {
     if (r >= lj) a.at[j * m + k + r] = (r == lj) ? alpha : 0.f;
     else if (a.semantics == 1) a.at[j * m + k + r] = col[r - r0];
   }
-  // the reflector row, T and the updated panel columns visible to every CTA
-  cluster_barrier();
+  // reference semantics read other CTAs' rows of the updated panel columns
+  // (norm metadata) and an arbitrary row of Y: make them visible; the
+  // intended exposed row is row lj, whose Y entries this step are v[lj] = 1
+  // and whose new T column every CTA holds in sw2
+  if (a.semantics == 0) cluster_barrier();
 
   const int64_t nxt = j + 1;
   if (a.semantics == 0 && nxt < n && nxt < pe) {
@@ -462,7 +470,18 @@ qr_step_cluster_kernel(StepArgs a) {
     if (a.semantics == 0) rs = (j < 0) ? 0 : ((j > L - 1) ? L - 1 : j);
     if (tid < P) {
       float s = 0.f;
-      for (int l = 0; l < P; ++l) s = fmaf(a.yt[(int64_t)l * L + rs], a.t[tid * P + l], s);
+      if (a.semantics == 0) {
+        for (int l = 0; l < P; ++l) s = fmaf(a.yt[(int64_t)l * L + rs], a.t[tid * P + l], s);
+      } else {
+        // rows of Y beyond lj are zero; Y[lj][lj] = 1 and T[:, lj] is sw2 / tau here
+        for (int l = 0; l <= lj; ++l) {
+          const float y = (l == lj) ? 1.f : a.yt[(int64_t)l * L + rs];
+          const float tv = (l < lj) ? a.t[tid * P + l]
+                                    : ((tid < lj) ? sw2[tid] : ((tid == lj) ? tau_j : 0.f));
+          s = fmaf(y, tv, s);
+        }
+        for (int l = lj + 1; l < P; ++l) s = fmaf(0.f, 0.f, s);
+      }
       sw[tid] = s;  // row_weights = y_r T^T
     }
     __syncthreads();
@@ -476,6 +495,7 @@ qr_step_cluster_kernel(StepArgs a) {
   if (rank == 0 && tid == 0) ctrl->active = ctrl->active + 1;
   // no CTA leaves while another may still read its shared memory
   cluster_barrier();
+  if (a.semantics == 1) swap_scalars();
 }
 
 // Exposed-row downdate over deferred columns [c0, n): warp per column.
