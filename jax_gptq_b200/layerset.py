@@ -357,17 +357,27 @@ def _copy_streams():
     return _COPY_STREAMS[dev]
 
 
+# Activations cross PCIe in chunks of this many tokens; each chunk's H
+# contribution is accumulated as soon as it lands (bit-identical to one
+# launch over all tokens), so H is ready right after the last chunk.
+HOST_TOKEN_CHUNK = 32768
+
+
 def quantize_layer_gptq_host(weights_host: dict, inputs_host: dict, cfg: QuantConfig,
                              shapes=LLAMA2_7B):
     """GPTQ layer set from host buffers to host results.
 
     Activations (bf16) and weights (float32) are copied from (pinned) host
-    memory on a copy stream in the order the computation needs them -- the
-    weights of linears sharing an input straight into one row-stacked device
-    buffer -- so the transfer of the next input group overlaps the tensor-core
-    work on the current one; codes, scales and zeros stream back on a second
-    copy stream.  Returns ``({name: (codes, scales, zeros, g_idx, perm)},
-    {"h2d": bytes, "d2h": bytes})`` with host tensors.
+    memory on a copy stream, largest input group first, activations in
+    ``HOST_TOKEN_CHUNK``-token chunks whose H contribution is accumulated
+    while the next chunk is in flight, then the group's weights straight into
+    one row-stacked device buffer.  Each group's factor and sweep overlap the
+    later groups' transfers, so what is left after the last byte arrives is
+    one small group's factor and sweep.  Codes, scales and zeros stream back
+    on a second copy stream.  The results equal the device-resident
+    :func:`quantize_layer_gptq` bit for bit.  Returns ``({name: (codes,
+    scales, zeros, g_idx, perm)}, {"h2d": bytes, "d2h": bytes})`` with host
+    tensors.
     """
     compute = torch.cuda.current_stream()
     h2d, d2h = _copy_streams()
@@ -375,15 +385,21 @@ def quantize_layer_gptq_host(weights_host: dict, inputs_host: dict, cfg: QuantCo
     start.record(compute)
     h2d.wait_event(start)
     nbytes = {"h2d": 0, "d2h": 0}
+    order = sorted(inputs_host, key=lambda g: -inputs_host[g].shape[1])
     dev_x, dev_w, ready_x, ready_w = {}, {}, {}, {}
     with torch.cuda.stream(h2d):
-        for grp, src in inputs_host.items():
+        for grp in order:
+            src = inputs_host[grp]
             dst = torch.empty(src.shape, dtype=src.dtype, device="cuda")
-            dst.copy_(src, non_blocking=True)
-            ev = torch.cuda.Event()
-            ev.record(h2d)
+            evs = []
+            for t0 in range(0, src.shape[0], HOST_TOKEN_CHUNK):
+                t1 = min(src.shape[0], t0 + HOST_TOKEN_CHUNK)
+                dst[t0:t1].copy_(src[t0:t1], non_blocking=True)
+                ev = torch.cuda.Event()
+                ev.record(h2d)
+                evs.append((t0, t1, ev))
             nbytes["h2d"] += src.numel() * src.element_size()
-            dev_x[grp], ready_x[grp] = dst, ev
+            dev_x[grp], ready_x[grp] = dst, evs
             members = _members(shapes, grp)
             n = weights_host[members[0][0]].shape[1]
             wdev = torch.empty((sum(m for _, m in members), n), dtype=torch.float32, device="cuda")
@@ -397,13 +413,14 @@ def quantize_layer_gptq_host(weights_host: dict, inputs_host: dict, cfg: QuantCo
             ev.record(h2d)
             dev_w[grp], ready_w[grp] = wdev, ev
     out = {}
-    for grp in inputs_host:
-        compute.wait_event(ready_x[grp])
+    for grp in order:
         x = dev_x[grp]
         x.record_stream(compute)
         d = x.shape[1]
         h = torch.empty((d, d), dtype=torch.float32, device="cuda")
-        stats.syrk_into(h, x, accumulate=False)
+        for i, (t0, t1, ev) in enumerate(ready_x[grp]):
+            compute.wait_event(ev)
+            stats.syrk_into(h, x[t0:t1], accumulate=i > 0)
         f = factor_hessian(h, cfg)
         del h
         compute.wait_event(ready_w[grp])

@@ -80,3 +80,31 @@ def test_failed_first_attempt_is_redone():
     assert out["bad"].dequant.equal(ref.dequant)
     fg = factor_hessian(good, cfg)
     assert out["good"].dequant.equal(gptq_sweep(w, fg.u, fg.perm, cfg).dequant)
+
+
+def test_host_buffer_driver_equals_device_driver():
+    """Host buffers in, host results out (chunked transfers, H accumulated per
+    chunk, largest group first): the same bits as the device-resident path."""
+    shapes = SHAPES
+    cfg = QuantConfig(w_bits=4, group_size=128, ordering_mode="diag_h", semantics="intended")
+    weights = LS.synth_weights(shapes, 0.02, 3)
+    inputs = {g: LS.synth_activations(3000, d, 40 + i)[0]
+              for i, (g, d) in enumerate(LS.group_dims(shapes).items())}
+    old = LS.HOST_TOKEN_CHUNK
+    LS.HOST_TOKEN_CHUNK = 1024
+    try:
+        w_host = {k: v.cpu().pin_memory() for k, v in weights.items()}
+        x_host = {k: v.cpu().pin_memory() for k, v in inputs.items()}
+        got, nbytes = LS.quantize_layer_gptq_host(w_host, x_host, cfg, shapes)
+    finally:
+        LS.HOST_TOKEN_CHUNK = old
+    torch.cuda.synchronize()
+    ref, _ = LS.quantize_layer_gptq(weights, inputs, cfg, shapes, concurrent=False)
+    assert set(got) == set(ref)
+    for name, (codes, scales, zeros, g_idx, perm) in got.items():
+        r = ref[name]
+        assert torch.equal(codes, r.codes.cpu()), name
+        assert torch.equal(scales, r.scales.cpu()), name
+        assert torch.equal(zeros, r.zeros.cpu()), name
+        assert torch.equal(perm, r.perm.cpu()), name
+    assert nbytes["h2d"] > 0 and nbytes["d2h"] > 0
