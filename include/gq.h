@@ -40,6 +40,14 @@ typedef enum {
  * reference (single stream). */
 int gq_set_cta_budget(int n);
 
+/* Form of the bf16 statistics kernels (gq_syrk_bf16, gq_gemm_tn_bf16)
+ * launched afterwards by the calling host thread: 1 (default) = clusters of
+ * two CTAs sharing 256 x 256 tiles (tcgen05 cta_group::2), 0 = one CTA per
+ * 128 x 256 tile.  Both give the same bits; the pair form moves a third less
+ * data from L2 per flop.  Without a cluster of two available the one-CTA
+ * form runs regardless. */
+int gq_set_pair_kernels(int enable);
+
 /* Library version (major*10000 + minor*100 + patch). */
 int gq_version(void);
 

@@ -41,6 +41,11 @@ int cta_budget() {
   return (g_cta_budget > 0 && g_cta_budget < n) ? g_cta_budget : n;
 }
 
+// Statistics kernels on CTA pairs (1) or one CTA per tile (0), this host thread.
+static thread_local int g_pair_kernels = 1;
+
+bool pair_kernels() { return g_pair_kernels != 0; }
+
 // Copy the upper triangle (j > i) of h into the lower triangle.  Tiled
 // through shared memory so both the read and the write are coalesced.
 __global__ void symmetrize_upper_kernel(float* __restrict__ h, int64_t d, int64_t ldh) {
@@ -113,5 +118,11 @@ int gq_symmetrize_upper(float* h, int64_t d, int64_t ldh, void* stream) {
 extern "C" int gq_set_cta_budget(int n) {
   GQ_REQUIRE(n >= 0, "gq_set_cta_budget: negative budget");
   gq::g_cta_budget = n;
+  return GQ_OK;
+}
+
+extern "C" int gq_set_pair_kernels(int enable) {
+  GQ_REQUIRE(enable == 0 || enable == 1, "gq_set_pair_kernels: enable must be 0 or 1");
+  gq::g_pair_kernels = enable;
   return GQ_OK;
 }

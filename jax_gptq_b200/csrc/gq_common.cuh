@@ -98,5 +98,7 @@ int sm_count();
 // Grid size for persistent kernels: sm_count(), or less when this host thread
 // set a budget with gq_set_cta_budget.
 int cta_budget();
+// Whether the bf16 statistics kernels run on CTA pairs; set with gq_set_pair_kernels.
+bool pair_kernels();
 
 }  // namespace gq

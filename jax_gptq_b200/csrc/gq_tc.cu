@@ -876,7 +876,7 @@ namespace tc {
 int launch(const void* xa, int64_t lda, const void* xb, int64_t ldb, int64_t K, int64_t M,
            int64_t N, float* c, int64_t ldc, int accumulate, int symmetric, cudaStream_t st) {
   int max_clusters = 0;
-  if (tc2::pair_setup(&max_clusters) == GQ_OK && max_clusters >= 1)
+  if (pair_kernels() && tc2::pair_setup(&max_clusters) == GQ_OK && max_clusters >= 1)
     return tc2::launch_pair(xa, lda, xb, ldb, K, M, N, c, ldc, accumulate, symmetric, st);
   (void)cudaGetLastError();  // the failed occupancy query is not this launch's error
   return launch_single(xa, lda, xb, ldb, K, M, N, c, ldc, accumulate, symmetric, st);

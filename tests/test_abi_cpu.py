@@ -90,3 +90,10 @@ def test_comm_handle_argument_errors_without_a_gpu():
     small = ctypes.create_string_buffer(16)
     assert lib.gq_nccl_unique_id(small, 16) == _lib.GQ_EINVAL
     assert lib.gq_handle_create_nccl(0, small, 2, 2, ctypes.byref(h)) == _lib.GQ_EINVAL
+
+
+def test_pair_kernel_switch_validates_its_argument():
+    lib = _lib.lib()
+    assert lib.gq_set_pair_kernels(0) == 0
+    assert lib.gq_set_pair_kernels(1) == 0
+    assert lib.gq_set_pair_kernels(2) != 0

@@ -136,3 +136,28 @@ def test_token_chunk_must_be_a_multiple_of_512():
     h = torch.empty((64, 64), device="cuda")
     with pytest.raises(ValueError):
         stats.syrk_into(h, x, accumulate=False, token_chunk=1000)
+
+
+@pytest.mark.parametrize("tokens,d,sym", [(4096, 1000, True), (2048, 520, True), (3000, 392, False)])
+def test_pair_and_single_cta_statistics_agree(tokens, d, sym):
+    """CTA-pair (cta_group::2, 256 x 256 tiles) and one-CTA (128 x 256) forms of
+    the bf16 statistics kernels give the same bits."""
+    from jax_gptq_b200 import stats
+    rng = np.random.default_rng(tokens + d)
+    xq = _bf16(rng, (tokens, d))[0].cuda()
+    xf = _bf16(rng, (tokens, d))[0].cuda()
+    out = []
+    lib = _lib.lib()
+    try:
+        for pair in (1, 0):
+            assert lib.gq_set_pair_kernels(pair) == 0
+            c = torch.empty((d, d), device="cuda")
+            if sym:
+                stats.syrk_into(c, xq, accumulate=False)
+            else:
+                stats.gemm_tn_into(c, xf, xq, accumulate=False)
+            out.append(c)
+    finally:
+        lib.gq_set_pair_kernels(1)
+    assert _status() == 0
+    assert torch.equal(out[0], out[1])
