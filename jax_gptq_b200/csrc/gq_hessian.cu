@@ -234,35 +234,33 @@ __device__ __forceinline__ void bprod(const float* __restrict__ A, const float* 
 // 2 x 32 floats; rdiag, 32 floats.
 // Column j of the trailing matrix is published in cb as soon as it is final
 // (one pivot ahead) and read back as float4 broadcasts, so each lane forms
-// the whole column of L itself, l_kj = a_kj / l_jj.  The diagonal is
-// replicated in every lane and updated with the same fmaf sequence as its own
-// row, so the pivot chain is rsqrt -> multiply -> fmaf per column, with no
-// shuffle or shared-memory round trip on it.
+// the whole column of L itself, l_kj = a_kj / l_jj, and takes the pivot from
+// it; the read-back of the next column is issued before the current pivot's
+// bulk updates, which hide its latency.
 // Returns true (uniform) if a pivot was not > 0 or not finite; that pivot is
 // replaced by 1.
 __device__ bool sub_factor(float (&r)[SUB], float* xd, float* lt, float* cb, float* rdiag) {
-  const unsigned FULL = 0xffffffffu;
   const int lane = threadIdx.x & 31;
-  float dg[SUB];
-#pragma unroll
-  for (int k = 0; k < SUB; ++k) dg[k] = __shfl_sync(FULL, r[k], k);
   cb[lane] = r[0];
   __syncwarp();
-  bool bad = false;
+  // column j of the trailing block, published one pivot ahead; the pivot is
+  // its entry j (lane j's own r[j], which every lane reads here)
+  float cv[SUB];
+  {
+    const float4* c4 = reinterpret_cast<const float4*>(cb);
 #pragma unroll
-  for (int j = 0; j < SUB; ++j) {
-    // column j (rows below the pivot), published during the previous pivot
-    float cv[SUB];
-    const float4* c4 = reinterpret_cast<const float4*>(cb + (j & 1) * SUB);
-#pragma unroll
-    for (int g = (j + 1) / 4; g < SUB / 4; ++g) {
+    for (int g = 0; g < SUB / 4; ++g) {
       const float4 v = c4[g];
       cv[4 * g + 0] = v.x;
       cv[4 * g + 1] = v.y;
       cv[4 * g + 2] = v.z;
       cv[4 * g + 3] = v.w;
     }
-    float djj = dg[j];
+  }
+  bool bad = false;
+#pragma unroll
+  for (int j = 0; j < SUB; ++j) {
+    float djj = cv[j];
     if (!(djj > 0.f) || !isfinite(djj)) {
       bad = true;
       djj = 1.f;
@@ -274,19 +272,26 @@ __device__ bool sub_factor(float (&r)[SUB], float* xd, float* lt, float* cb, flo
     const float lij = (lane < j) ? 0.f : ((lane == j) ? djj * rl : r[j] * rl);
     r[j] = lij;
     if (j + 1 < SUB) {
-      // the next pivot first, then publish column j + 1 (final in every lane)
-      const float l1 = cv[j + 1] * rl;
-      dg[j + 1] = fmaf(-l1, l1, dg[j + 1]);
-      r[j + 1] = fmaf(-lij, l1, r[j + 1]);
+      // the next column first: update, publish, and start reading it back so
+      // the load overlaps this pivot's remaining updates
+      r[j + 1] = fmaf(-lij, cv[j + 1] * rl, r[j + 1]);
       // double-buffered: this buffer's previous readers are past the last __syncwarp
       cb[((j + 1) & 1) * SUB + lane] = r[j + 1];
       __syncwarp();
+      float nx[SUB];
+      const float4* c4 = reinterpret_cast<const float4*>(cb + ((j + 1) & 1) * SUB);
 #pragma unroll
-      for (int k = j + 2; k < SUB; ++k) {
-        const float lkj = cv[k] * rl;
-        dg[k] = fmaf(-lkj, lkj, dg[k]);
-        r[k] = fmaf(-lij, lkj, r[k]);
+      for (int g = (j + 1) / 4; g < SUB / 4; ++g) {
+        const float4 v = c4[g];
+        nx[4 * g + 0] = v.x;
+        nx[4 * g + 1] = v.y;
+        nx[4 * g + 2] = v.z;
+        nx[4 * g + 3] = v.w;
       }
+#pragma unroll
+      for (int k = j + 2; k < SUB; ++k) r[k] = fmaf(-lij, cv[k] * rl, r[k]);
+#pragma unroll
+      for (int k = j + 1; k < SUB; ++k) cv[k] = nx[k];
     }
   }
   // L transposed, so that a column of L is one run of float4 broadcasts
