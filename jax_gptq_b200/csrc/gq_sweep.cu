@@ -5,18 +5,20 @@
 // Data layout (workspace): wp [m, ldp] float32 -- the working weights in
 // permuted column order (ldp = n rounded up to 4), overwritten block by block
 // with the dequantized values; cp [m, ldp] uint8 -- codes in permuted order;
-// err [m, 128] float32 -- the scaled errors of the current block.
+// err [m, 512] float32 -- the scaled errors of the current super-block.
 //
 // The lazy updates are two-level: blocks of 128 columns inside super-blocks
 // of 512.  Per block [b0, b1) of super-block [s0, s1):
 //   1. the band U[b0:b1, b0:s1] is transposed into ubt (column j of the band
 //      is a contiguous 128-float row);
-//   2. sweep_rows_kernel: one lane per weight row, one warp per CTA; the
-//      lane quantizes its row's columns one by one (32-column sub-blocks in
-//      registers, the rest of the block in a shared-memory row buffer, the U
-//      rows of each sub-block's trailing update copied in by cp.async while
-//      the sub-block's columns are quantized) and writes codes, dequantized
-//      values and scaled errors (w - dq) / U_ii into its 128 columns of err;
+//   2. the block step, one lane per weight row: the lane quantizes its row's
+//      columns one by one (32-column sub-blocks in registers, the rest of the
+//      block in a shared-memory row buffer) and writes codes, dequantized
+//      values and scaled errors (w - dq) / U_ii into its 128 columns of err.
+//      sweep_rows_kernel runs it on four warps per 32 rows (one for the
+//      column chain, three applying finished sub-blocks' errors ahead of it);
+//      sweep_rows1_kernel, on one warp, serves grids too large for one wave
+//      of those CTAs;
 //   3. near update: wp[:, b1:s1] -= err[:, b0-s0:b1-s0] @ U[b0:b1, b1:s1].
 // After the super-block, one far update with K = 512:
 //   wp[:, s1:] -= err @ U[s0:s1, s1:]   (U[s0:s1, s1:] transposed first).
@@ -90,7 +92,7 @@ struct SweepArgs {
   uint8_t* cp;          // [m, ldp]
   float* err;           // [m, ld_err]: this block's scaled errors
   int64_t ld_err;
-  const float* ubt;     // [n - b0, 128]: ubt[j][i] = U[b0 + i][b0 + j]
+  const float* ubt;     // [s1 - b0, 128]: ubt[j][i] = U[b0 + i][b0 + j]
   int64_t m, n, ldp;
   int64_t b0;           // first column of this block
   int bw;               // block width (<= 128)
