@@ -54,16 +54,25 @@ def qronos_reference(weight, weight_orig, h, g, w_bits=4, group_size=128, sym=Fa
 
 
 def qronos_intended(weight, weight_orig, h, g, w_bits=4, group_size=128, sym=False,
-                    ordering_mode="none", damp_percent=0.01, block=128, dtype=np.float64):
+                    ordering_mode="none", damp_percent=0.01, block=128, dtype=np.float64,
+                    factor=None, return_pre=False):
+    """``factor = (u, perm, hd)`` replaces the oracle's own factor of ``h``
+    (to compare the update and sweep arithmetic alone); ``return_pre`` adds
+    the sweep's unrounded values (see :func:`oracle.gptq.gptq_sweep`)."""
     weight = np.asarray(weight)
     weight_orig = np.asarray(weight_orig)
     h = np.asarray(h)
     g = np.asarray(g)
     check_qronos_args(weight, weight_orig, h, g)
     m, n = weight.shape
-    u, perm, attempt = og.process_hessian_intended(h, ordering_mode, damp_percent, dtype)
-    damp = (10 ** max(attempt, 0)) * damp_percent
-    hd = og.damped_permuted(h, perm, damp, dtype)
+    if factor is None:
+        u, perm, attempt = og.process_hessian_intended(h, ordering_mode, damp_percent, dtype)
+        damp = (10 ** max(attempt, 0)) * damp_percent
+        hd = og.damped_permuted(h, perm, damp, dtype)
+    else:
+        u, perm, hd = (np.asarray(factor[0], dtype), np.asarray(factor[1]),
+                       np.asarray(factor[2], dtype))
+        attempt = 0
     gp = np.asarray(g, dtype)[perm][:, perm]
     wp = np.asarray(weight, dtype)[:, perm]
     wop = np.asarray(weight_orig, dtype)[:, perm]
@@ -79,7 +88,7 @@ def qronos_intended(weight, weight_orig, h, g, w_bits=4, group_size=128, sym=Fal
     future = np.linalg.solve(hd[1:, 1:], b.T).T if n > 1 else np.zeros((m, 0), dtype)
     start = np.concatenate([v1[:, None], future], axis=1)
     out = og.gptq_sweep(weight, u, perm, w_bits, group_size, sym, block, dtype,
-                        group0=(s0, z0), noprop_cols=1, start=start)
+                        group0=(s0, z0), noprop_cols=1, start=start, return_pre=return_pre)
     out["perm"] = perm
     out["attempt"] = attempt
     return out
