@@ -157,6 +157,13 @@ int gq_act_order_perm(const float* h, int64_t d, int64_t ldh, int ordering,
  * untouched) when all five attempts fail; *attempt_out receives the
  * exponent used.  hd_out (nullable) receives the damped, permuted Hessian
  * of the successful attempt.
+ *
+ * Part of the factor's work runs on a library-owned side stream (one per
+ * device and caller stream, created on the first call with the caller
+ * stream's priority) that forks from and joins back into `stream` through
+ * events, so everything is complete in `stream` order when the call's work
+ * is.  Make that first call outside stream capture; later calls may be
+ * captured.
  */
 int64_t gq_hessian_factor_workspace_size(int64_t d);
 int gq_hessian_factor(const float* h, int64_t d, int64_t ldh, const int32_t* perm,

@@ -17,6 +17,9 @@
 
 #include <algorithm>
 #include <cmath>
+#include <map>
+#include <mutex>
+#include <utility>
 
 namespace gq {
 
@@ -604,7 +607,35 @@ int transpose2d(const float* src, int64_t rows, int64_t cols, int64_t lds, float
 // product operands' zero triangles skipped tile by tile.  Every GEMM has both
 // operands K-major (tensor-core path): X11^T is formed by a transpose and the
 // last product is taken as X21 = -X22 Tt^T with Tt = X11^T L21^T.
-// scratch: n1 * n floats suffice (n1 <= n / 2 + NB).
+//
+// Tt depends only on X11 and L21, so it is formed on a side stream (same
+// priority as the caller's) while the caller's stream runs the Schur update
+// and rec(A22); the last product waits for it.  The critical path per split
+// is then L21, the update, rec(A22) and X21.  All splits share the one side
+// stream: each split's Tt is queued behind those of the splits that forked
+// before it, which are smaller or finished long before it is needed, and a
+// single extra stream per caller keeps the streams of a concurrent layer set
+// within the device's hardware work queues (streams that share a queue wait
+// on one another's pending dependencies).
+//
+// Scratch per split, in this order: L21 (n2 x n1), Tt (n1 x n2), X11^T
+// (n1 x n1), then rec(A22)'s scratch; rec(A11) runs before any of them is
+// written and reuses the same base.  inv_chol_scratch_floats(n) is the total.
+constexpr int MAX_FORK_DEPTH = 24;
+
+int64_t split_n1(int64_t n) {
+  int64_t n1 = ((n / 2 + NB - 1) / NB) * NB;
+  if (n1 >= n) n1 = n - NB;
+  return n1;
+}
+
+int64_t inv_chol_scratch_floats(int64_t n) {
+  if (n <= NB) return 0;
+  const int64_t n1 = split_n1(n), n2 = n - n1;
+  return std::max(inv_chol_scratch_floats(n1),
+                  2 * n1 * n2 + n1 * n1 + inv_chol_scratch_floats(n2));
+}
+
 constexpr int MAX_ROW_BYTES = 220 * 1024;  // the row-staged permute holds one row of h
 
 int diag_kernel_setup() {
@@ -623,35 +654,82 @@ int diag_kernel_setup() {
   return GQ_OK;
 }
 
-int inv_chol_rec(float* a, int64_t n, int64_t lda, float* scratch, int* status, cudaStream_t st) {
+// The side stream and events of the recursion's forks, one set per (device,
+// caller stream), created on first use with the caller stream's priority and
+// kept for the life of the process.  Calls that share a caller stream must
+// not run concurrently on different host threads (as for any stream).
+struct Forks {
+  cudaStream_t side;
+  cudaEvent_t fork[MAX_FORK_DEPTH];
+  cudaEvent_t join[MAX_FORK_DEPTH];
+};
+
+int forks_for(cudaStream_t st, Forks** out) {
+  static std::mutex mu;
+  static std::map<std::pair<int, cudaStream_t>, Forks*> table;
+  int dev = 0;
+  GQ_CHECK_CUDA(cudaGetDevice(&dev));
+  std::lock_guard<std::mutex> lock(mu);
+  auto it = table.find({dev, st});
+  if (it != table.end()) {
+    *out = it->second;
+    return GQ_OK;
+  }
+  int prio = 0;
+  GQ_CHECK_CUDA(cudaStreamGetPriority(st, &prio));
+  Forks* f = new Forks();
+  GQ_CHECK_CUDA(cudaStreamCreateWithPriority(&f->side, cudaStreamNonBlocking, prio));
+  for (int i = 0; i < MAX_FORK_DEPTH; ++i) {
+    GQ_CHECK_CUDA(cudaEventCreateWithFlags(&f->fork[i], cudaEventDisableTiming));
+    GQ_CHECK_CUDA(cudaEventCreateWithFlags(&f->join[i], cudaEventDisableTiming));
+  }
+  table[{dev, st}] = f;
+  *out = f;
+  return GQ_OK;
+}
+
+int inv_chol_rec(float* a, int64_t n, int64_t lda, float* scratch, int* status, cudaStream_t st,
+                 Forks* forks, int depth) {
   if (n <= NB) {
     potrf_diag_kernel<<<1, DIAG_THREADS, DIAG_SMEM, st>>>(a, lda, (int)n, status);
     return check_launch("potrf_diag");
   }
-  int64_t n1 = ((n / 2 + NB - 1) / NB) * NB;
-  if (n1 >= n) n1 = n - NB;
-  const int64_t n2 = n - n1;
+  GQ_REQUIRE(depth < MAX_FORK_DEPTH, "inv_chol_rec: recursion deeper than %d", MAX_FORK_DEPTH);
+  const int64_t n1 = split_n1(n), n2 = n - n1;
   float* a11 = a;
   float* a21 = a + n1 * lda;
   float* a22 = a21 + n1;
-  GQ_TRY(inv_chol_rec(a11, n1, lda, scratch, status, st));
-  float* l21 = scratch;  // n2 x n1
+  float* l21 = scratch;            // n2 x n1
+  float* tt = l21 + n2 * n1;       // n1 x n2: Tt = X11^T L21^T
+  float* xt = tt + n1 * n2;        // n1 x n1: X11^T
+  float* rest = xt + n1 * n1;      // rec(A22)'s scratch
+  GQ_TRY(inv_chol_rec(a11, n1, lda, scratch, status, st, forks, depth + 1));
   GQ_TRY(sgemm_tri(0, 1, n2, n1, n1, 1.f, a21, lda, a11, lda, 0.f, l21, n1, 3, st));
+  cudaStream_t side = forks->side;
+  GQ_CHECK_CUDA(cudaEventRecord(forks->fork[depth], st));
+  GQ_CHECK_CUDA(cudaStreamWaitEvent(side, forks->fork[depth], 0));
+  GQ_TRY(transpose2d(a11, n1, n1, lda, xt, n1, side));
+  GQ_TRY(sgemm_tri(0, 1, n1, n2, n1, 1.f, xt, n1, l21, n1, 0.f, tt, n2, 1, side));
+  GQ_CHECK_CUDA(cudaEventRecord(forks->join[depth], side));
   GQ_TRY(sgemm(0, 1, n2, n2, n1, -1.f, l21, n1, l21, n1, 1.f, a22, lda, 1, st));
-  GQ_CHECK_CUDA(cudaMemcpy2DAsync(a21, lda * sizeof(float), l21, n1 * sizeof(float),
-                                  n1 * sizeof(float), n2, cudaMemcpyDeviceToDevice, st));
-  float* tt = scratch;            // n1 x n2: Tt = X11^T L21^T
-  float* xt = scratch + n1 * n2;  // n1 x n1: X11^T
-  GQ_TRY(transpose2d(a11, n1, n1, lda, xt, n1, st));
-  GQ_TRY(sgemm_tri(0, 1, n1, n2, n1, 1.f, xt, n1, a21, lda, 0.f, tt, n2, 1, st));
-  GQ_TRY(inv_chol_rec(a22, n2, lda, scratch + n1 * n2, status, st));
+  GQ_TRY(inv_chol_rec(a22, n2, lda, rest, status, st, forks, depth + 1));
+  GQ_CHECK_CUDA(cudaStreamWaitEvent(st, forks->join[depth], 0));
   GQ_TRY(sgemm_tri(0, 1, n2, n1, n2, -1.f, a22, lda, tt, n2, 0.f, a21, lda, 2, st));
   return GQ_OK;
 }
 
+int inv_chol(float* a, int64_t n, int64_t lda, float* scratch, int* status, cudaStream_t st) {
+  Forks* forks = nullptr;
+  if (n > NB) GQ_TRY(forks_for(st, &forks));
+  return inv_chol_rec(a, n, lda, scratch, status, st, forks, 0);
+}
+
+// Workspace: the damped, permuted copy (d x d), then the recursion's scratch
+// from a 256-byte boundary, then the damping mean and the status word.
+int64_t hessian_scratch_offset(int64_t d) { return (d * d + 63) / 64 * 64; }
+
 int64_t hessian_ws_floats(int64_t d) {
-  int64_t half = d / 2 + NB;
-  return d * d + half * (d + NB) + 64;
+  return hessian_scratch_offset(d) + inv_chol_scratch_floats(d) + 64;
 }
 
 }  // namespace gq
@@ -687,10 +765,9 @@ int gq_hessian_factor_attempt(const float* h, int64_t d, int64_t ldh, const int3
              gq::MAX_ROW_BYTES / (int)sizeof(float));
   cudaStream_t st = gq::as_stream(stream);
   float* ws = reinterpret_cast<float*>(workspace);
-  float* ht = ws;                                  // d*d
-  float* scratch = ht + d * d;                     // (d/2+NB) x (d+NB)
-  int64_t half = d / 2 + gq::NB;
-  float* mean = scratch + half * (d + gq::NB);     // 1 float
+  float* ht = ws;                                   // d*d
+  float* scratch = ht + gq::hessian_scratch_offset(d);     // inv_chol_scratch_floats(d)
+  float* mean = scratch + gq::inv_chol_scratch_floats(d);  // 1 float
   GQ_TRY(gq::diag_kernel_setup());
   gq::diag_mean_kernel<<<1, 1024, 0, st>>>(h, d, ldh, mean);
   GQ_TRY(gq::check_launch("diag_mean"));
@@ -707,7 +784,7 @@ int gq_hessian_factor_attempt(const float* h, int64_t d, int64_t ldh, const int3
     GQ_TRY(gq::check_launch("damp_permute"));
   }
   // L^-1 in place (lower triangle; the strict upper part is zero), then U = J L^-1 J
-  GQ_TRY(gq::inv_chol_rec(ht, d, d, scratch, status, st));
+  GQ_TRY(gq::inv_chol(ht, d, d, scratch, status, st));
   gq::reverse_copy_kernel<<<rows_grid, 256, 0, st>>>(ht, d, d, u, ldu);
   return gq::check_launch("reverse_copy");
 }
@@ -723,9 +800,8 @@ int gq_hessian_factor(const float* h, int64_t d, int64_t ldh, const int32_t* per
   GQ_REQUIRE(damp_percent >= 0.0, "gq_hessian_factor: negative damp_percent");
   cudaStream_t st = gq::as_stream(stream);
   float* ws = reinterpret_cast<float*>(workspace);
-  int64_t half = d / 2 + gq::NB;
-  float* mean = ws + d * d + half * (d + gq::NB);  // 1 float
-  int* status = reinterpret_cast<int*>(mean + 16);  // 1 int
+  float* mean = ws + gq::hessian_scratch_offset(d) + gq::inv_chol_scratch_floats(d);
+  int* status = reinterpret_cast<int*>(mean + 16);           // 1 int
   for (int attempt = 0; attempt < 5; ++attempt) {
     GQ_TRY(gq_hessian_factor_attempt(h, d, ldh, perm, damp_percent, attempt, u, ldu, hd_out,
                                      workspace, workspace_bytes, status, stream));

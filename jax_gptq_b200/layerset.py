@@ -174,12 +174,21 @@ def _side_streams(n: int) -> list:
     return pool[:n]
 
 
+def _chain_sizes(inputs: dict, shapes) -> dict:
+    """Per input group, the key that orders the chains, longest first: the
+    feature count (the factor's cost, cubic), then the stacked row count (the
+    sweep's).  The last group's chain is the only one that overlaps no
+    statistics, so it should be the shortest."""
+    return {grp: (x.shape[1], sum(m for _, m in _members(shapes, grp)))
+            for grp, x in inputs.items()}
+
+
 def _stack(weights: dict, members) -> torch.Tensor:
     return weights[members[0][0]] if len(members) == 1 else \
         torch.cat([weights[name] for name, _ in members], dim=0)
 
 
-def _run_groups_concurrently(sizes: dict, form, work, redo) -> dict:
+def _run_groups_concurrently(sizes: dict, form, work, redo, prepare=None, late=None) -> dict:
     """Run each input group's chain on its own side stream.
 
     ``sizes[grp]`` orders the groups (largest first).  ``form(grp, chunk)
@@ -192,6 +201,12 @@ def _run_groups_concurrently(sizes: dict, form, work, redo) -> dict:
     after it leaves ``RESERVED_SMS`` SMs free, so its latency-bound steps
     overlap the remaining statistics and the other chains.
 
+    With ``prepare`` and ``late`` the chain is split around statistics that
+    only its second half reads (Qronos' cross term): ``prepare(grp, h) ->
+    state`` (the factor) is queued on the side stream first, then
+    ``late(grp, chunk)`` forms the late statistics on the current stream,
+    and ``work(grp, state)`` follows on the side stream once they are ready.
+
     ``status`` is the device word of the group's first damping attempt; the
     statuses are read once at the end, and a group whose damped Hessian was
     not positive definite is recomputed by ``redo(grp, h)`` (the retrying,
@@ -199,7 +214,7 @@ def _run_groups_concurrently(sizes: dict, form, work, redo) -> dict:
     tensors are marked as used by the current stream, which waits for every
     side stream before returning."""
     main = torch.cuda.current_stream()
-    order = sorted(sizes, key=lambda g: -sizes[g])
+    order = sorted(sizes, key=lambda g: sizes[g], reverse=True)
     streams = _side_streams(len(order))
     sms = torch.cuda.get_device_properties(main.device).multi_processor_count
     lib = _lib.lib()
@@ -209,8 +224,18 @@ def _run_groups_concurrently(sizes: dict, form, work, redo) -> dict:
         try:
             hs[grp] = form(grp, None if idx == 0 else STATS_TOKEN_CHUNK)
             s.wait_stream(main)
+            if prepare is None:
+                with torch.cuda.stream(s):
+                    pending[grp] = work(grp, hs[grp])
+                continue
             with torch.cuda.stream(s):
-                pending[grp] = work(grp, hs[grp])
+                state = prepare(grp, hs[grp])
+            # the chain is now running: leave it its SMs
+            lib.gq_set_cta_budget(max(1, sms - RESERVED_SMS))
+            late(grp, STATS_TOKEN_CHUNK)
+            s.wait_stream(main)
+            with torch.cuda.stream(s):
+                pending[grp] = work(grp, state)
         finally:
             lib.gq_set_cta_budget(0)
     for s in streams:
@@ -258,8 +283,8 @@ def quantize_layer_gptq(weights: dict, inputs: dict, cfg: QuantConfig, shapes=LL
         return gptq_sweep(_stack(weights, _members(shapes, grp)), f.u, f.perm, cfg)
 
     results: dict[str, SweepResult] = {}
-    sizes = {grp: x.shape[1] for grp, x in inputs.items()}
-    for grp, res in _run_groups_concurrently(sizes, form, work, redo).items():
+    for grp, res in _run_groups_concurrently(_chain_sizes(inputs, shapes), form, work,
+                                             redo).items():
         results.update(_split_rows(res, _members(shapes, grp)))
     return results, LayerTimes()
 
@@ -300,14 +325,23 @@ def quantize_layer_qronos(weights: dict, inputs_float: dict, inputs_quant: dict,
         xq = inputs_quant[grp]
         d = xq.shape[1]
         h = torch.empty((d, d), dtype=torch.float32, device=xq.device)
-        g = torch.empty((d, d), dtype=torch.float32, device=xq.device)
         stats.syrk_into(h, xq, accumulate=False, token_chunk=chunk)
-        stats.gemm_tn_into(g, inputs_float[grp], xq, accumulate=False, token_chunk=chunk)
-        gs[grp] = g
         return h
 
-    def work(grp, h):
-        f, status = factor_hessian_attempt0(h, cfg, want_hd=True)
+    def late(grp, chunk):
+        # the cross term is read only by the sweep, so it is formed while the
+        # group's factor runs
+        xq = inputs_quant[grp]
+        d = xq.shape[1]
+        g = torch.empty((d, d), dtype=torch.float32, device=xq.device)
+        stats.gemm_tn_into(g, inputs_float[grp], xq, accumulate=False, token_chunk=chunk)
+        gs[grp] = g
+
+    def prepare(grp, h):
+        return factor_hessian_attempt0(h, cfg, want_hd=True)
+
+    def work(grp, state):
+        f, status = state
         w = _stack(weights, _members(shapes, grp))
         return status, qronos_quantize(w, w, None, gs[grp], cfg, factor=f)
 
@@ -317,8 +351,8 @@ def quantize_layer_qronos(weights: dict, inputs_float: dict, inputs_quant: dict,
         return qronos_quantize(w, w, None, gs[grp], cfg, factor=f)
 
     results = {}
-    sizes = {grp: x.shape[1] for grp, x in inputs_quant.items()}
-    for grp, res in _run_groups_concurrently(sizes, form, work, redo).items():
+    for grp, res in _run_groups_concurrently(_chain_sizes(inputs_quant, shapes), form, work, redo,
+                                             prepare, late).items():
         results.update(_split_rows(res, _members(shapes, grp)))
     return results, LayerTimes()
 
