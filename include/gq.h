@@ -185,6 +185,27 @@ int gq_hessian_factor_attempt(const float* h, int64_t d, int64_t ldh, const int3
                               float* hd_out, void* workspace, int64_t workspace_bytes,
                               int* status, void* stream);
 
+/* No counterpart in the reference: attempt 0 of the factor, formed straight
+ * from the bf16 activations x[tokens, d] (ld ldx), with the same u and perm,
+ * bit for bit, as gq_syrk_bf16 -> gq_act_order_perm(ordering) ->
+ * gq_hessian_factor_attempt(attempt 0).  The Hessian is accumulated on
+ * stats_stream in the factor's (act-order, reversed) feature order, leading
+ * block first, and the factor runs on chain_stream: its first half starts as
+ * soon as the leading block is formed, while the rest of H accumulates with
+ * reserve_sms SMs left free.  The full H is never materialised (redo a
+ * failed attempt, status != 0, from gq_syrk_bf16 and gq_hessian_factor).
+ * x may be reused once stats_stream passes this call's work; u, perm and
+ * status are complete in chain_stream order.  Requires d and ldx multiples
+ * of 8, x 16-byte aligned, a 256-byte aligned workspace of
+ * gq_factor_from_x_workspace_size(tokens, d) bytes, and d * 6 bytes of
+ * shared memory for the column gather (d <= 37000 or so). */
+int64_t gq_factor_from_x_workspace_size(int64_t tokens, int64_t d);
+int gq_factor_from_x_attempt(const uint16_t* x, int64_t tokens, int64_t d, int64_t ldx,
+                             int ordering, double damp_percent, int reserve_sms,
+                             float* u, int64_t ldu, int32_t* perm,
+                             void* workspace, int64_t workspace_bytes, int* status,
+                             void* stats_stream, void* chain_stream);
+
 /* ------------------------------------------------------------------------
  * GPTQ column sweep (the computation gptq_ref.py:136-155 stands in for).
  * With u = I it reproduces gptq_forward_step bit-exactly.

@@ -56,6 +56,9 @@ SIGNATURES = {
     "gq_symmetrize_upper": (c_int, [_P, c_int64, c_int64, _P]),
     "gq_act_order_perm": (c_int, [_P, c_int64, c_int64, c_int, _P, _P]),
     "gq_hessian_factor_workspace_size": (c_int64, [c_int64]),
+    "gq_factor_from_x_workspace_size": (c_int64, [c_int64, c_int64]),
+    "gq_factor_from_x_attempt": (c_int, [_P, c_int64, c_int64, c_int64, c_int, c_double, c_int,
+                                         _P, c_int64, _P, _P, c_int64, _P, _P, _P]),
     "gq_hessian_factor": (c_int, [_P, c_int64, c_int64, _P, c_double, _P, c_int64, _P, _P, c_int64,
                                   ctypes.POINTER(c_int), _P]),
     "gq_hessian_factor_attempt": (c_int, [_P, c_int64, c_int64, _P, c_double, c_int, _P, c_int64,

@@ -688,6 +688,9 @@ int forks_for(cudaStream_t st, Forks** out) {
   return GQ_OK;
 }
 
+int inv_chol_after_a11(float* a, int64_t n, int64_t lda, float* scratch, int* status,
+                       cudaStream_t st, Forks* forks, int depth);
+
 int inv_chol_rec(float* a, int64_t n, int64_t lda, float* scratch, int* status, cudaStream_t st,
                  Forks* forks, int depth) {
   if (n <= NB) {
@@ -695,6 +698,14 @@ int inv_chol_rec(float* a, int64_t n, int64_t lda, float* scratch, int* status, 
     return check_launch("potrf_diag");
   }
   GQ_REQUIRE(depth < MAX_FORK_DEPTH, "inv_chol_rec: recursion deeper than %d", MAX_FORK_DEPTH);
+  GQ_TRY(inv_chol_rec(a, split_n1(n), lda, scratch, status, st, forks, depth + 1));
+  return inv_chol_after_a11(a, n, lda, scratch, status, st, forks, depth);
+}
+
+// The split's work after rec(A11): L21, the Schur update, rec(A22) and X21
+// (Tt on the side stream).
+int inv_chol_after_a11(float* a, int64_t n, int64_t lda, float* scratch, int* status,
+                       cudaStream_t st, Forks* forks, int depth) {
   const int64_t n1 = split_n1(n), n2 = n - n1;
   float* a11 = a;
   float* a21 = a + n1 * lda;
@@ -703,7 +714,6 @@ int inv_chol_rec(float* a, int64_t n, int64_t lda, float* scratch, int* status, 
   float* tt = l21 + n2 * n1;       // n1 x n2: Tt = X11^T L21^T
   float* xt = tt + n1 * n2;        // n1 x n1: X11^T
   float* rest = xt + n1 * n1;      // rec(A22)'s scratch
-  GQ_TRY(inv_chol_rec(a11, n1, lda, scratch, status, st, forks, depth + 1));
   GQ_TRY(sgemm_tri(0, 1, n2, n1, n1, 1.f, a21, lda, a11, lda, 0.f, l21, n1, 3, st));
   cudaStream_t side = forks->side;
   GQ_CHECK_CUDA(cudaEventRecord(forks->fork[depth], st));
@@ -731,6 +741,97 @@ int64_t hessian_scratch_offset(int64_t d) { return (d * d + 63) / 64 * 64; }
 int64_t hessian_ws_floats(int64_t d) {
   return hessian_scratch_offset(d) + inv_chol_scratch_floats(d) + 64;
 }
+
+
+// ---------------------------------------------------------------------------
+// Factor straight from the activations (gq_factor_from_x_attempt).
+//
+// The factor's first split only needs the leading block A11 of the damped,
+// permuted, reversed Hessian.  Its features are known once the diagonal of H
+// is (act order sorts it), so the columns of X are gathered into that order
+// and H is formed block by block: A11 first, then A21 and A22 while rec(A11)
+// already runs on the chain stream.  Every element equals the one the
+// one-shot path computes (the same tensor-core tile arithmetic on the same
+// token order; a product and its mirror are the same bf16 x bf16 products),
+// and the diagonal, the mean and the permutation come from the diagonal tiles
+// of the original-order H, so u and perm are bit-identical to
+// gq_syrk_bf16 -> gq_act_order_perm -> gq_hessian_factor_attempt.
+
+// xr[t][i] = x[t][perm[d - 1 - i]] (bf16 bits); d % 8 == 0, rows 16-byte aligned.
+__global__ void gather_cols_reversed_kernel(const uint16_t* __restrict__ x, int64_t tokens,
+                                            int64_t d, int64_t ldx,
+                                            const int32_t* __restrict__ perm,
+                                            uint16_t* __restrict__ xr) {
+  extern __shared__ __align__(16) uint8_t gsm[];
+  int32_t* q = reinterpret_cast<int32_t*>(gsm);
+  uint16_t* row = reinterpret_cast<uint16_t*>(gsm + ((d * 4 + 15) / 16) * 16);
+  for (int64_t i = threadIdx.x; i < d; i += blockDim.x) q[i] = perm[d - 1 - i];
+  for (int64_t t = blockIdx.x; t < tokens; t += gridDim.x) {
+    __syncthreads();
+    const uint16_t* src = x + t * ldx;
+    for (int64_t c = (int64_t)threadIdx.x * 8; c < d; c += (int64_t)blockDim.x * 8)
+      *reinterpret_cast<uint4*>(row + c) = *reinterpret_cast<const uint4*>(src + c);
+    __syncthreads();
+    uint16_t* dst = xr + t * d;
+    for (int64_t i = (int64_t)threadIdx.x * 8; i < d; i += (int64_t)blockDim.x * 8) {
+      uint32_t w[4];
+#pragma unroll
+      for (int e = 0; e < 4; ++e)
+        w[e] = (uint32_t)row[q[i + 2 * e]] | ((uint32_t)row[q[i + 2 * e + 1]] << 16);
+      *reinterpret_cast<uint4*>(dst + i) = make_uint4(w[0], w[1], w[2], w[3]);
+    }
+  }
+}
+
+// Diagonal block a[0:n, 0:n] (ld lda) whose upper triangle holds H: the lower
+// triangle receives the mirror, the diagonal + damp * mean, the strict upper
+// triangle zeros -- what damp_permute_rows_kernel<true> writes.  Block (bi, bj)
+// with bj <= bi owns the 32 x 32 tiles (bi, bj) and (bj, bi).
+__global__ void lower_damped_from_upper_kernel(float* __restrict__ a, int64_t n, int64_t lda,
+                                               const float* __restrict__ mean, float damp) {
+  __shared__ float tile[32][33];
+  const int64_t bi = blockIdx.y, bj = blockIdx.x;
+  if (bj > bi) return;
+  const int tx = threadIdx.x, ty = threadIdx.y;  // 32 x 8
+  const float dv = damp * mean[0];
+  for (int r = ty; r < 32; r += 8) {  // upper tile (bj, bi)
+    const int64_t i = bj * 32 + r, j = bi * 32 + tx;
+    tile[r][tx] = (i < n && j < n) ? a[i * lda + j] : 0.f;
+  }
+  __syncthreads();
+  for (int r = ty; r < 32; r += 8) {
+    const int64_t i = bi * 32 + r, j = bj * 32 + tx;  // (i, j) in tile (bi, bj)
+    if (i < n && j < n) {
+      float v = 0.f;
+      if (j < i) v = tile[tx][r];            // mirror of (j, i)
+      else if (j == i) v = tile[r][tx] + dv;  // (bi == bj here)
+      a[i * lda + j] = v;
+    }
+    if (bi > bj) {  // the upper tile's element (bj*32 + r, bi*32 + tx) -> 0
+      const int64_t ui = bj * 32 + r, uj = bi * 32 + tx;
+      if (ui < n && uj < n) a[ui * lda + uj] = 0.f;
+    }
+  }
+}
+
+namespace tc {
+int launch(const void* xa, int64_t lda, const void* xb, int64_t ldb, int64_t K, int64_t M,
+           int64_t N, float* c, int64_t ldc, int accumulate, int symmetric, cudaStream_t st,
+           int diag_only);
+}
+
+int lower_damped_from_upper(float* a, int64_t n, int64_t lda, const float* mean, float damp,
+                            cudaStream_t st) {
+  if (n == 0) return GQ_OK;
+  const int64_t nt = ceil_div(n, 32);
+  lower_damped_from_upper_kernel<<<dim3((unsigned)nt, (unsigned)nt), dim3(32, 8), 0, st>>>(
+      a, n, lda, mean, damp);
+  return check_launch("lower_damped_from_upper");
+}
+
+// Workspace of the from-activations factor: the hessian factor's layout
+// (working matrix, recursion scratch, mean), then the gathered activations.
+int64_t factor_x_gather_offset(int64_t d) { return (hessian_ws_floats(d) * 4 + 255) / 256 * 256; }
 
 }  // namespace gq
 
@@ -786,6 +887,94 @@ int gq_hessian_factor_attempt(const float* h, int64_t d, int64_t ldh, const int3
   // L^-1 in place (lower triangle; the strict upper part is zero), then U = J L^-1 J
   GQ_TRY(gq::inv_chol(ht, d, d, scratch, status, st));
   gq::reverse_copy_kernel<<<rows_grid, 256, 0, st>>>(ht, d, d, u, ldu);
+  return gq::check_launch("reverse_copy");
+}
+
+int64_t gq_factor_from_x_workspace_size(int64_t tokens, int64_t d) {
+  return gq::factor_x_gather_offset(d) + tokens * d * 2;
+}
+
+int gq_factor_from_x_attempt(const uint16_t* x, int64_t tokens, int64_t d, int64_t ldx,
+                             int ordering, double damp_percent, int reserve_sms, float* u,
+                             int64_t ldu, int32_t* perm, void* workspace, int64_t workspace_bytes,
+                             int* status, void* stats_stream, void* chain_stream) {
+  GQ_REQUIRE(x != nullptr && u != nullptr && perm != nullptr && status != nullptr,
+             "gq_factor_from_x_attempt: NULL x, u, perm or status");
+  GQ_REQUIRE(tokens > 0 && d > 0 && ldx >= d && ldu >= d, "gq_factor_from_x_attempt: bad shape");
+  GQ_REQUIRE(d % 8 == 0 && ldx % 8 == 0 && (reinterpret_cast<uintptr_t>(x) & 15) == 0,
+             "gq_factor_from_x_attempt: d and ldx must be multiples of 8 and x 16-byte aligned");
+  GQ_REQUIRE(ordering == 0 || ordering == 1, "gq_factor_from_x_attempt: ordering must be 0 or 1");
+  GQ_REQUIRE(damp_percent >= 0.0, "gq_factor_from_x_attempt: negative damp_percent");
+  GQ_REQUIRE(reserve_sms >= 0, "gq_factor_from_x_attempt: negative reserve_sms");
+  GQ_REQUIRE(workspace != nullptr && (reinterpret_cast<uintptr_t>(workspace) & 255) == 0 &&
+                 workspace_bytes >= gq_factor_from_x_workspace_size(tokens, d),
+             "gq_factor_from_x_attempt: workspace must be 256-byte aligned and hold %lld bytes",
+             (long long)gq_factor_from_x_workspace_size(tokens, d));
+  const size_t gather_smem = (size_t)((d * 4 + 15) / 16) * 16 + (size_t)d * 2;
+  GQ_REQUIRE(gather_smem <= (size_t)gq::MAX_ROW_BYTES, "gq_factor_from_x_attempt: d = %lld too large",
+             (long long)d);
+  cudaStream_t ss = gq::as_stream(stats_stream), cs = gq::as_stream(chain_stream);
+  float* ws = reinterpret_cast<float*>(workspace);
+  float* ht = ws;
+  float* scratch = ht + gq::hessian_scratch_offset(d);
+  float* mean = scratch + gq::inv_chol_scratch_floats(d);
+  uint16_t* xr = reinterpret_cast<uint16_t*>(reinterpret_cast<uint8_t*>(workspace) +
+                                             gq::factor_x_gather_offset(d));
+  GQ_TRY(gq::diag_kernel_setup());
+  static int gather_attr_device = -1;
+  int dev = 0;
+  GQ_CHECK_CUDA(cudaGetDevice(&dev));
+  if (gather_attr_device != dev) {
+    GQ_CHECK_CUDA(cudaFuncSetAttribute(gq::gather_cols_reversed_kernel,
+                                       cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       gq::MAX_ROW_BYTES));
+    gather_attr_device = dev;
+  }
+  cudaEvent_t ev_a11 = nullptr, ev_all = nullptr;
+  {
+    gq::Forks* f = nullptr;
+    GQ_TRY(gq::forks_for(cs, &f));
+    ev_a11 = f->fork[gq::MAX_FORK_DEPTH - 1];  // depths this deep are never reached
+    ev_all = f->join[gq::MAX_FORK_DEPTH - 1];
+  }
+  // statistics stream: diagonal tiles of H in original order -> perm, mean;
+  // gathered columns; A11, then A21 and A22 with reserve_sms left to the chain
+  GQ_TRY(gq::tc::launch(x, ldx, x, ldx, tokens, d, d, ht, d, 0, 1, ss, 1));
+  GQ_TRY(gq::act_order_perm(ht, d, d, ordering, perm, ss));
+  gq::diag_mean_kernel<<<1, 1024, 0, ss>>>(ht, d, d, mean);
+  GQ_TRY(gq::check_launch("diag_mean"));
+  const unsigned rows_grid = (unsigned)std::min<int64_t>(tokens, 148 * 8);
+  gq::gather_cols_reversed_kernel<<<rows_grid, 256, gather_smem, ss>>>(x, tokens, d, ldx, perm,
+                                                                       xr);
+  GQ_TRY(gq::check_launch("gather_cols_reversed"));
+  const float damp = (float)damp_percent;
+  const int64_t n1 = d > gq::NB ? gq::split_n1(d) : d, n2 = d - n1;
+  GQ_TRY(gq::tc::launch(xr, d, xr, d, tokens, n1, n1, ht, d, 0, 1, ss, 0));
+  GQ_TRY(gq::lower_damped_from_upper(ht, n1, d, mean, damp, ss));
+  if (n2 > 0) GQ_CHECK_CUDA(cudaMemset2DAsync(ht + n1, d * 4, 0, n2 * 4, n1, ss));
+  GQ_CHECK_CUDA(cudaMemsetAsync(status, 0, sizeof(int), ss));
+  GQ_CHECK_CUDA(cudaEventRecord(ev_a11, ss));
+  if (n2 > 0) {
+    const int prev = gq::cta_budget();
+    const int keep = std::max(1, std::min(prev, gq::sm_count() - reserve_sms));
+    gq_set_cta_budget(keep);
+    int rc = gq::tc::launch(xr + n1, d, xr, d, tokens, n2, n1, ht + n1 * d, d, 0, 0, ss, 0);
+    if (rc == GQ_OK) rc = gq::tc::launch(xr + n1, d, xr + n1, d, tokens, n2, n2, ht + n1 * d + n1,
+                                         d, 0, 1, ss, 0);
+    gq_set_cta_budget(prev == gq::sm_count() ? 0 : prev);
+    GQ_TRY(rc);
+    GQ_TRY(gq::lower_damped_from_upper(ht + n1 * d + n1, n2, d, mean, damp, ss));
+  }
+  GQ_CHECK_CUDA(cudaEventRecord(ev_all, ss));
+  // chain stream: rec(A11) as soon as A11 is formed, the rest once H is
+  gq::Forks* forks = nullptr;
+  GQ_TRY(gq::forks_for(cs, &forks));
+  GQ_CHECK_CUDA(cudaStreamWaitEvent(cs, ev_a11, 0));
+  GQ_TRY(gq::inv_chol_rec(ht, n1, d, scratch, status, cs, forks, 1));
+  GQ_CHECK_CUDA(cudaStreamWaitEvent(cs, ev_all, 0));
+  if (n2 > 0) GQ_TRY(gq::inv_chol_after_a11(ht, d, d, scratch, status, cs, forks, 0));
+  gq::reverse_copy_kernel<<<(unsigned)std::min<int64_t>(d, 148 * 16), 256, 0, cs>>>(ht, d, d, u,
+                                                                                     ldu);
   return gq::check_launch("reverse_copy");
 }
 

@@ -66,6 +66,7 @@ struct Params {
   int num_tiles;
   int mb;  // row tiles
   int nb;  // column tiles
+  int diag_only;  // symmetric: only the tiles holding diagonal elements
 };
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
@@ -177,6 +178,11 @@ __device__ __forceinline__ int col_height(const Params& p, int bn) {
 // reads under half of X from DRAM and L2 serves the rest.
 constexpr int GROUP_COLS = 8;
 __device__ __forceinline__ void tile_coords(const Params& p, int t, int& bm, int& bn) {
+  if (p.diag_only) {  // 128-row tile t holds its diagonal in 256-column tile t / 2
+    bm = t;
+    bn = t >> 1;
+    return;
+  }
   for (int g0 = 0; g0 < p.nb; g0 += GROUP_COLS) {
     const int g1 = min(p.nb, g0 + GROUP_COLS);
     int cnt = 0;
@@ -453,7 +459,8 @@ static int check_operand(const char* who, const void* x, int64_t tokens, int64_t
 }
 
 int launch_single(const void* xa, int64_t lda, const void* xb, int64_t ldb, int64_t K, int64_t M,
-                  int64_t N, float* c, int64_t ldc, int accumulate, int symmetric, cudaStream_t st) {
+                  int64_t N, float* c, int64_t ldc, int accumulate, int symmetric, cudaStream_t st,
+                  int diag_only) {
   if (K == 0) {
     if (!accumulate)
       GQ_CHECK_CUDA(cudaMemset2DAsync(c, ldc * 4, 0, N * 4, M, st));
@@ -472,7 +479,10 @@ int launch_single(const void* xa, int64_t lda, const void* xb, int64_t ldb, int6
   p.accumulate = accumulate;
   p.mb = (int)ceil_div(M, BM);
   p.nb = (int)ceil_div(N, BN);
-  if (symmetric) {
+  p.diag_only = symmetric && diag_only;
+  if (p.diag_only) {
+    p.num_tiles = p.mb;
+  } else if (symmetric) {
     int64_t cnt = 0;
     for (int j = 0; j < p.nb; ++j) cnt += std::min(p.mb, 2 * j + 2);
     p.num_tiles = (int)cnt;
@@ -575,6 +585,10 @@ __device__ __forceinline__ int col_height2(const Params& p, int bn) {
 }
 // Same grouped order as the one-CTA kernel, in 256 x 256 tiles.
 __device__ __forceinline__ void tile_coords2(const Params& p, int t, int& bm, int& bn) {
+  if (p.diag_only) {
+    bm = bn = t;
+    return;
+  }
   for (int g0 = 0; g0 < p.nb; g0 += GROUP_COLS) {
     const int g1 = min(p.nb, g0 + GROUP_COLS);
     int cnt = 0;
@@ -836,7 +850,8 @@ int pair_setup(int* max_clusters) {
 
 // C (+)= A^T B with CTA pairs; same contract as tc::launch.
 int launch_pair(const void* xa, int64_t lda, const void* xb, int64_t ldb, int64_t K, int64_t M,
-                int64_t N, float* c, int64_t ldc, int accumulate, int symmetric, cudaStream_t st) {
+                int64_t N, float* c, int64_t ldc, int accumulate, int symmetric, cudaStream_t st,
+                int diag_only) {
   if (K == 0) {
     if (!accumulate) GQ_CHECK_CUDA(cudaMemset2DAsync(c, ldc * 4, 0, N * 4, M, st));
     return GQ_OK;
@@ -854,7 +869,10 @@ int launch_pair(const void* xa, int64_t lda, const void* xb, int64_t ldb, int64_
   p.accumulate = accumulate;
   p.mb = (int)ceil_div(M, PM);
   p.nb = (int)ceil_div(N, PN);
-  if (symmetric) {
+  p.diag_only = symmetric && diag_only;
+  if (p.diag_only) {
+    p.num_tiles = std::min(p.mb, p.nb);
+  } else if (symmetric) {
     int64_t cnt = 0;
     for (int j = 0; j < p.nb; ++j) cnt += std::min(p.mb, j + 1);
     p.num_tiles = (int)cnt;
@@ -872,14 +890,17 @@ int launch_pair(const void* xa, int64_t lda, const void* xb, int64_t ldb, int64_
 
 namespace tc {
 // CTA pairs where a cluster of two fits (bit-identical results), else one CTA
-// per tile.
+// per tile.  diag_only (symmetric): only the tiles that hold diagonal
+// elements, each computed exactly as in the full launch.
 int launch(const void* xa, int64_t lda, const void* xb, int64_t ldb, int64_t K, int64_t M,
-           int64_t N, float* c, int64_t ldc, int accumulate, int symmetric, cudaStream_t st) {
+           int64_t N, float* c, int64_t ldc, int accumulate, int symmetric, cudaStream_t st,
+           int diag_only) {
   int max_clusters = 0;
   if (pair_kernels() && tc2::pair_setup(&max_clusters) == GQ_OK && max_clusters >= 1)
-    return tc2::launch_pair(xa, lda, xb, ldb, K, M, N, c, ldc, accumulate, symmetric, st);
+    return tc2::launch_pair(xa, lda, xb, ldb, K, M, N, c, ldc, accumulate, symmetric, st,
+                            diag_only);
   (void)cudaGetLastError();  // the failed occupancy query is not this launch's error
-  return launch_single(xa, lda, xb, ldb, K, M, N, c, ldc, accumulate, symmetric, st);
+  return launch_single(xa, lda, xb, ldb, K, M, N, c, ldc, accumulate, symmetric, st, diag_only);
 }
 }  // namespace tc
 
@@ -898,7 +919,7 @@ int gq_syrk_bf16(const uint16_t* x, int64_t tokens, int64_t d, int64_t ldx, floa
   GQ_TRY(gq::tc::check_operand("gq_syrk_bf16", x, tokens, d, ldx));
   GQ_REQUIRE(h != nullptr && ldh >= d, "gq_syrk_bf16: bad output");
   cudaStream_t st = gq::as_stream(stream);
-  GQ_TRY(gq::tc::launch(x, ldx, x, ldx, tokens, d, d, h, ldh, accumulate, 1, st));
+  GQ_TRY(gq::tc::launch(x, ldx, x, ldx, tokens, d, d, h, ldh, accumulate, 1, st, 0));
   return gq::symmetrize_upper(h, d, ldh, st);
 }
 
@@ -909,7 +930,7 @@ int gq_gemm_tn_bf16(const uint16_t* xa, int64_t lda, const uint16_t* xb, int64_t
   GQ_TRY(gq::tc::check_operand("gq_gemm_tn_bf16", xb, tokens, db, ldb));
   GQ_REQUIRE(g != nullptr && ldg >= db, "gq_gemm_tn_bf16: bad output");
   return gq::tc::launch(xa, lda, xb, ldb, tokens, da, db, g, ldg, accumulate, 0,
-                        gq::as_stream(stream));
+                        gq::as_stream(stream), 0);
 }
 
 int gq_device_status(int* status_out, int reset, void* stream) {

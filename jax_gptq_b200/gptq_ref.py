@@ -128,6 +128,38 @@ def factor_hessian_attempt0(h_dev: torch.Tensor, cfg: QuantConfig, want_hd: bool
     return HessianFactor(u, perm, 0, hd), status
 
 
+def factor_from_activations_attempt0(x: torch.Tensor, cfg: QuantConfig,
+                                     chain_stream: torch.cuda.Stream, reserve_sms: int):
+    """Attempt 0 of :func:`factor_hessian` for ``h = x^T x`` formed from the
+    bf16 activations ``x`` (``gq_factor_from_x_attempt``): the statistics run
+    on the current stream, the factor on ``chain_stream``, whose first half
+    starts while the rest of ``h`` is still accumulating.  Same factor, bit
+    for bit, as ``factor_hessian_attempt0(x^T x)``.
+
+    Returns ``(factor, status)`` like :func:`factor_hessian_attempt0`; the
+    result tensors belong to ``chain_stream``."""
+    if cfg.solver_mode != "chol" or cfg.ordering_mode not in {"none", "diag_h"}:
+        raise ValueError("factor_from_activations_attempt0 supports solver_mode='chol' with "
+                         "ordering_mode 'none' or 'diag_h'")
+    tokens, d = x.shape
+    main = torch.cuda.current_stream()
+    lib = _lib.lib()
+    ws = A.workspace(lib.gq_factor_from_x_workspace_size(tokens, d))
+    with torch.cuda.stream(chain_stream):
+        u = A.empty((d, d))
+        perm = A.empty((d,), torch.int32)
+        status = torch.empty((1,), dtype=torch.int32, device="cuda")
+    # perm and status are written on the statistics stream first
+    perm.record_stream(main)
+    status.record_stream(main)
+    ws.record_stream(chain_stream)
+    _lib.call("gq_factor_from_x_attempt", A.ptr(x), tokens, d, x.stride(0),
+              1 if cfg.ordering_mode == "diag_h" else 0, float(cfg.damp_percent), int(reserve_sms),
+              A.ptr(u), d, A.ptr(perm), A.ptr(ws), ws.numel(), A.ptr(status),
+              main.cuda_stream, chain_stream.cuda_stream)
+    return HessianFactor(u, perm, 0, None), status
+
+
 def _process_hessian_eigh(h, cfg: QuantConfig, panel_size: int):
     """gptq_ref.py:95-133 on the device.
 

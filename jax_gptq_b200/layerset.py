@@ -23,8 +23,8 @@ import torch
 
 from . import _lib, stats
 from .config import QuantConfig
-from .gptq_ref import (HessianFactor, SweepResult, factor_hessian, factor_hessian_attempt0,
-                       gptq_sweep)
+from .gptq_ref import (HessianFactor, SweepResult, factor_from_activations_attempt0,
+                       factor_hessian, factor_hessian_attempt0, gptq_sweep)
 from .qronos_ref import qronos_quantize
 
 # (name, out_features, in_features, input group)
@@ -174,6 +174,23 @@ def _side_streams(n: int) -> list:
     return pool[:n]
 
 
+# Form the largest group's factor straight from its activations
+# (factor_from_activations_attempt0): the factor's first half then overlaps
+# the rest of that group's Hessian.  Off by default: in the concurrent layer
+# step the other groups' statistics and chains already keep the GPU busy
+# while the largest chain runs, so the shorter chain did not shorten the step
+# (measured on the 7B layer set), and the gathered copy of the activations
+# costs tokens x d x 2 bytes.  It pays where a group's statistics overlap
+# nothing else.
+FACTOR_FROM_ACTIVATIONS = False
+
+
+def _fused_factor_ok(x: torch.Tensor, cfg: QuantConfig) -> bool:
+    return (x.dtype == torch.bfloat16 and x.dim() == 2 and x.stride(1) == 1
+            and x.shape[1] % 8 == 0 and x.stride(0) % 8 == 0 and x.data_ptr() % 16 == 0
+            and cfg.solver_mode == "chol" and cfg.ordering_mode in ("none", "diag_h"))
+
+
 def _chain_sizes(inputs: dict, shapes) -> dict:
     """Per input group, the key that orders the chains, longest first: the
     feature count (the factor's cost, cubic), then the stacked row count (the
@@ -188,7 +205,8 @@ def _stack(weights: dict, members) -> torch.Tensor:
         torch.cat([weights[name] for name, _ in members], dim=0)
 
 
-def _run_groups_concurrently(sizes: dict, form, work, redo, prepare=None, late=None) -> dict:
+def _run_groups_concurrently(sizes: dict, form, work, redo, prepare=None, late=None,
+                             fused=None) -> dict:
     """Run each input group's chain on its own side stream.
 
     ``sizes[grp]`` orders the groups (largest first).  ``form(grp, chunk)
@@ -206,6 +224,11 @@ def _run_groups_concurrently(sizes: dict, form, work, redo, prepare=None, late=N
     state`` (the factor) is queued on the side stream first, then
     ``late(grp, chunk)`` forms the late statistics on the current stream,
     and ``work(grp, state)`` follows on the side stream once they are ready.
+    With ``fused`` (and ``prepare``), the first group's statistics and
+    factor are enqueued together by ``fused(grp, side_stream) -> state``
+    (statistics on the current stream, the factor on the side stream, which
+    can then start before the statistics are complete); ``redo`` then gets
+    ``h = None`` for that group.
 
     ``status`` is the device word of the group's first damping attempt; the
     statuses are read once at the end, and a group whose damped Hessian was
@@ -222,18 +245,23 @@ def _run_groups_concurrently(sizes: dict, form, work, redo, prepare=None, late=N
     for idx, (grp, s) in enumerate(zip(order, streams)):
         lib.gq_set_cta_budget(0 if idx == 0 else max(1, sms - RESERVED_SMS))
         try:
-            hs[grp] = form(grp, None if idx == 0 else STATS_TOKEN_CHUNK)
-            s.wait_stream(main)
-            if prepare is None:
+            if idx == 0 and fused is not None:
+                hs[grp] = None
+                state = fused(grp, s)
+            else:
+                hs[grp] = form(grp, None if idx == 0 else STATS_TOKEN_CHUNK)
+                s.wait_stream(main)
+                if prepare is None:
+                    with torch.cuda.stream(s):
+                        pending[grp] = work(grp, hs[grp])
+                    continue
                 with torch.cuda.stream(s):
-                    pending[grp] = work(grp, hs[grp])
-                continue
-            with torch.cuda.stream(s):
-                state = prepare(grp, hs[grp])
-            # the chain is now running: leave it its SMs
-            lib.gq_set_cta_budget(max(1, sms - RESERVED_SMS))
-            late(grp, STATS_TOKEN_CHUNK)
-            s.wait_stream(main)
+                    state = prepare(grp, hs[grp])
+            if late is not None:
+                # the chain is now running: leave it its SMs
+                lib.gq_set_cta_budget(max(1, sms - RESERVED_SMS))
+                late(grp, STATS_TOKEN_CHUNK)
+                s.wait_stream(main)
             with torch.cuda.stream(s):
                 pending[grp] = work(grp, state)
         finally:
@@ -274,17 +302,26 @@ def quantize_layer_gptq(weights: dict, inputs: dict, cfg: QuantConfig, shapes=LL
         stats.syrk_into(h, x, accumulate=False, token_chunk=chunk)
         return h
 
-    def work(grp, h):
-        f, status = factor_hessian_attempt0(h, cfg)
+    def prepare(grp, h):
+        return factor_hessian_attempt0(h, cfg)
+
+    def fused(grp, side):
+        return factor_from_activations_attempt0(inputs[grp], cfg, side, RESERVED_SMS)
+
+    def work(grp, state):
+        f, status = state
         return status, gptq_sweep(_stack(weights, _members(shapes, grp)), f.u, f.perm, cfg)
 
     def redo(grp, h):
-        f = factor_hessian(h, cfg)
+        f = factor_hessian(form(grp, None) if h is None else h, cfg)
         return gptq_sweep(_stack(weights, _members(shapes, grp)), f.u, f.perm, cfg)
 
+    sizes = _chain_sizes(inputs, shapes)
+    first = max(sizes, key=lambda g: sizes[g])
+    use_fused = FACTOR_FROM_ACTIVATIONS and _fused_factor_ok(inputs[first], cfg)
     results: dict[str, SweepResult] = {}
-    for grp, res in _run_groups_concurrently(_chain_sizes(inputs, shapes), form, work,
-                                             redo).items():
+    for grp, res in _run_groups_concurrently(sizes, form, work, redo, prepare,
+                                             fused=fused if use_fused else None).items():
         results.update(_split_rows(res, _members(shapes, grp)))
     return results, LayerTimes()
 

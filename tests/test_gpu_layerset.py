@@ -108,3 +108,82 @@ def test_host_buffer_driver_equals_device_driver():
         assert torch.equal(zeros, r.zeros.cpu()), name
         assert torch.equal(perm, r.perm.cpu()), name
     assert nbytes["h2d"] > 0 and nbytes["d2h"] > 0
+
+
+def _two_step_and_fused(x, cfg):
+    from jax_gptq_b200 import stats
+    from jax_gptq_b200.gptq_ref import factor_from_activations_attempt0
+    d = x.shape[1]
+    h = torch.empty((d, d), device="cuda")
+    stats.syrk_into(h, x, accumulate=False)
+    f0, st0 = factor_hessian_attempt0(h, cfg)
+    side = torch.cuda.Stream()
+    f1, st1 = factor_from_activations_attempt0(x, cfg, side, LS.RESERVED_SMS)
+    torch.cuda.current_stream().wait_stream(side)
+    torch.cuda.synchronize()
+    return (f0, st0.item()), (f1, st1.item())
+
+
+@pytest.mark.parametrize("tokens,d,ordering", [
+    (3000, 136, "diag_h"), (2048, 520, "diag_h"), (2048, 520, "none"), (4096, 1024, "diag_h"),
+    (5000, 2304, "diag_h"), (1000, 64, "diag_h")])
+def test_factor_from_activations_matches_two_step_path(tokens, d, ordering):
+    """The factor formed straight from X (H in act-order blocks, leading block
+    first, rec(A11) overlapping the rest) equals SYRK -> act order -> factor
+    bit for bit: every element of the permuted H is the same tile arithmetic."""
+    x = LS.synth_activations(tokens, d, tokens + d)[0]
+    cfg = QuantConfig(ordering_mode=ordering, semantics="intended")
+    (f0, st0), (f1, st1) = _two_step_and_fused(x, cfg)
+    assert st0 == 0 and st1 == 0
+    assert torch.equal(f0.perm, f1.perm)
+    assert torch.equal(f0.u, f1.u)
+
+
+def test_factor_from_activations_single_cta_statistics():
+    from jax_gptq_b200 import _lib
+    x = LS.synth_activations(2048, 776, 3)[0]
+    cfg = QuantConfig(ordering_mode="diag_h", semantics="intended")
+    lib = _lib.lib()
+    try:
+        assert lib.gq_set_pair_kernels(0) == 0
+        (f0, st0), (f1, st1) = _two_step_and_fused(x, cfg)
+    finally:
+        lib.gq_set_pair_kernels(1)
+    assert st0 == 0 and st1 == 0
+    assert torch.equal(f0.u, f1.u) and torch.equal(f0.perm, f1.perm)
+
+
+def test_factor_from_activations_reports_a_failed_attempt():
+    x = LS.synth_activations(2048, 384, 4)[0]
+    x[:, 17] = 0  # a dead feature: zero pivot without damping
+    cfg = QuantConfig(ordering_mode="diag_h", semantics="intended", damp_percent=0.0)
+    (_, st0), (_, st1) = _two_step_and_fused(x, cfg)
+    assert st0 != 0 and st1 != 0
+
+
+@pytest.fixture
+def fused_first_group(monkeypatch):
+    monkeypatch.setattr(LS, "FACTOR_FROM_ACTIVATIONS", True)
+
+
+def test_concurrent_gptq_with_fused_first_group_equals_sequential(fused_first_group):
+    weights, inputs = _setup(3)
+    cfg = QuantConfig(w_bits=4, group_size=128, ordering_mode="diag_h", semantics="intended")
+    seq, _ = LS.quantize_layer_gptq(weights, inputs, cfg, SHAPES, concurrent=False)
+    con, _ = LS.quantize_layer_gptq(weights, inputs, cfg, SHAPES)
+    torch.cuda.synchronize()
+    _assert_same(con, seq)
+
+
+def test_concurrent_gptq_redoes_a_failed_fused_group(fused_first_group):
+    """The largest group (fused statistics + factor) fails its first attempt;
+    the driver recomputes its H and takes the retrying path, as the sequential
+    driver does."""
+    weights, inputs = _setup(2)
+    inputs["c"][:, 3] = 0
+    cfg = QuantConfig(w_bits=4, group_size=128, ordering_mode="diag_h", semantics="intended",
+                      damp_percent=0.0)
+    seq, _ = LS.quantize_layer_gptq(weights, inputs, cfg, SHAPES, concurrent=False)
+    con, _ = LS.quantize_layer_gptq(weights, inputs, cfg, SHAPES)
+    torch.cuda.synchronize()
+    _assert_same(con, seq)
