@@ -439,13 +439,15 @@ def quantize_layer_gptq_host(weights_host: dict, inputs_host: dict, cfg: QuantCo
     """GPTQ layer set from host buffers to host results.
 
     Activations (bf16) and weights (float32) are copied from (pinned) host
-    memory on a copy stream, largest input group first, activations in
-    ``HOST_TOKEN_CHUNK``-token chunks whose H contribution is accumulated
-    while the next chunk is in flight, then the group's weights straight into
-    one row-stacked device buffer.  Each group's factor and sweep overlap the
-    later groups' transfers, so what is left after the last byte arrives is
-    one small group's factor and sweep.  Codes, scales and zeros stream back
-    on a second copy stream.  The results equal the device-resident
+    memory on a copy stream, longest chain first (the order of
+    :func:`quantize_layer_gptq`), activations in ``HOST_TOKEN_CHUNK``-token
+    chunks whose H contribution is accumulated while the next chunk is in
+    flight, then the group's weights straight into one row-stacked device
+    buffer (for the last group, its weights first).  Each group's factor and
+    sweep overlap the later groups' transfers, so what is left after the last
+    byte arrives is the shortest chain: one small group's last H chunk,
+    factor and sweep.  Codes, scales and zeros stream back on a second copy
+    stream.  The results equal the device-resident
     :func:`quantize_layer_gptq` bit for bit.  Returns ``({name: (codes,
     scales, zeros, g_idx, perm)}, {"h2d": bytes, "d2h": bytes})`` with host
     tensors.
@@ -456,33 +458,45 @@ def quantize_layer_gptq_host(weights_host: dict, inputs_host: dict, cfg: QuantCo
     start.record(compute)
     h2d.wait_event(start)
     nbytes = {"h2d": 0, "d2h": 0}
-    order = sorted(inputs_host, key=lambda g: -inputs_host[g].shape[1])
+    sizes = _chain_sizes(inputs_host, shapes)
+    order = sorted(sizes, key=lambda g: sizes[g], reverse=True)
     dev_x, dev_w, ready_x, ready_w = {}, {}, {}, {}
-    with torch.cuda.stream(h2d):
-        for grp in order:
-            src = inputs_host[grp]
-            dst = torch.empty(src.shape, dtype=src.dtype, device="cuda")
-            evs = []
-            for t0 in range(0, src.shape[0], HOST_TOKEN_CHUNK):
-                t1 = min(src.shape[0], t0 + HOST_TOKEN_CHUNK)
-                dst[t0:t1].copy_(src[t0:t1], non_blocking=True)
-                ev = torch.cuda.Event()
-                ev.record(h2d)
-                evs.append((t0, t1, ev))
-            nbytes["h2d"] += src.numel() * src.element_size()
-            dev_x[grp], ready_x[grp] = dst, evs
-            members = _members(shapes, grp)
-            n = weights_host[members[0][0]].shape[1]
-            wdev = torch.empty((sum(m for _, m in members), n), dtype=torch.float32, device="cuda")
-            r0 = 0
-            for name, m in members:
-                wsrc = weights_host[name]
-                wdev[r0:r0 + m].copy_(wsrc, non_blocking=True)
-                nbytes["h2d"] += wsrc.numel() * wsrc.element_size()
-                r0 += m
+
+    def copy_x(grp):
+        src = inputs_host[grp]
+        dst = torch.empty(src.shape, dtype=src.dtype, device="cuda")
+        evs = []
+        for t0 in range(0, src.shape[0], HOST_TOKEN_CHUNK):
+            t1 = min(src.shape[0], t0 + HOST_TOKEN_CHUNK)
+            dst[t0:t1].copy_(src[t0:t1], non_blocking=True)
             ev = torch.cuda.Event()
             ev.record(h2d)
-            dev_w[grp], ready_w[grp] = wdev, ev
+            evs.append((t0, t1, ev))
+        nbytes["h2d"] += src.numel() * src.element_size()
+        dev_x[grp], ready_x[grp] = dst, evs
+
+    def copy_w(grp):
+        members = _members(shapes, grp)
+        n = weights_host[members[0][0]].shape[1]
+        wdev = torch.empty((sum(m for _, m in members), n), dtype=torch.float32, device="cuda")
+        r0 = 0
+        for name, m in members:
+            wsrc = weights_host[name]
+            wdev[r0:r0 + m].copy_(wsrc, non_blocking=True)
+            nbytes["h2d"] += wsrc.numel() * wsrc.element_size()
+            r0 += m
+        ev = torch.cuda.Event()
+        ev.record(h2d)
+        dev_w[grp], ready_w[grp] = wdev, ev
+
+    with torch.cuda.stream(h2d):
+        for grp in order:
+            if grp == order[-1]:
+                copy_w(grp)
+                copy_x(grp)
+            else:
+                copy_x(grp)
+                copy_w(grp)
     out = {}
     for grp in order:
         x = dev_x[grp]
