@@ -97,3 +97,30 @@ def test_pair_kernel_switch_validates_its_argument():
     assert lib.gq_set_pair_kernels(0) == 0
     assert lib.gq_set_pair_kernels(1) == 0
     assert lib.gq_set_pair_kernels(2) != 0
+
+
+def test_factor_from_activations_validates_before_launching():
+    lib = _lib.lib()
+    p = ctypes.c_void_p(256)
+    need = lib.gq_factor_from_x_workspace_size(1024, 512)
+    assert need >= 512 * 512 * 4 + 1024 * 512 * 2
+    args = dict(x=p, tokens=1024, d=512, ldx=512, ordering=1, damp=0.01, reserve=12, u=p, ldu=512,
+                perm=p, ws=p, ws_bytes=need, status=p)
+
+    def call(**kw):
+        a = dict(args, **kw)
+        return lib.gq_factor_from_x_attempt(a["x"], a["tokens"], a["d"], a["ldx"], a["ordering"],
+                                            a["damp"], a["reserve"], a["u"], a["ldu"], a["perm"],
+                                            a["ws"], a["ws_bytes"], a["status"], None, None)
+
+    assert call(d=516, ldx=516, ldu=516) == _lib.GQ_EINVAL       # d not a multiple of 8
+    assert b"multiples of 8" in lib.gq_last_error()
+    assert call(ordering=2) == _lib.GQ_EINVAL
+    assert call(ws_bytes=need - 1) == _lib.GQ_EINVAL
+    assert call(ws=ctypes.c_void_p(272)) == _lib.GQ_EINVAL        # not 256-byte aligned
+    assert call(x=ctypes.c_void_p(264)) == _lib.GQ_EINVAL         # x not 16-byte aligned
+    assert call(damp=-1.0) == _lib.GQ_EINVAL
+    assert call(reserve=-1) == _lib.GQ_EINVAL
+    assert call(d=40000, ldx=40000, ldu=40000,
+                ws_bytes=lib.gq_factor_from_x_workspace_size(1024, 40000)) == _lib.GQ_EINVAL
+    assert b"too large" in lib.gq_last_error()
