@@ -662,6 +662,8 @@ struct Forks {
   cudaStream_t side;
   cudaEvent_t fork[MAX_FORK_DEPTH];
   cudaEvent_t join[MAX_FORK_DEPTH];
+  // gq_factor_from_x_attempt: A11 formed, all of H formed (statistics stream)
+  cudaEvent_t a11_ready, h_ready;
 };
 
 int forks_for(cudaStream_t st, Forks** out) {
@@ -683,6 +685,8 @@ int forks_for(cudaStream_t st, Forks** out) {
     GQ_CHECK_CUDA(cudaEventCreateWithFlags(&f->fork[i], cudaEventDisableTiming));
     GQ_CHECK_CUDA(cudaEventCreateWithFlags(&f->join[i], cudaEventDisableTiming));
   }
+  GQ_CHECK_CUDA(cudaEventCreateWithFlags(&f->a11_ready, cudaEventDisableTiming));
+  GQ_CHECK_CUDA(cudaEventCreateWithFlags(&f->h_ready, cudaEventDisableTiming));
   table[{dev, st}] = f;
   *out = f;
   return GQ_OK;
@@ -930,13 +934,9 @@ int gq_factor_from_x_attempt(const uint16_t* x, int64_t tokens, int64_t d, int64
                                        gq::MAX_ROW_BYTES));
     gather_attr_device = dev;
   }
-  cudaEvent_t ev_a11 = nullptr, ev_all = nullptr;
-  {
-    gq::Forks* f = nullptr;
-    GQ_TRY(gq::forks_for(cs, &f));
-    ev_a11 = f->fork[gq::MAX_FORK_DEPTH - 1];  // depths this deep are never reached
-    ev_all = f->join[gq::MAX_FORK_DEPTH - 1];
-  }
+  gq::Forks* forks = nullptr;
+  GQ_TRY(gq::forks_for(cs, &forks));
+  cudaEvent_t ev_a11 = forks->a11_ready, ev_all = forks->h_ready;
   // statistics stream: diagonal tiles of H in original order -> perm, mean;
   // gathered columns; A11, then A21 and A22 with reserve_sms left to the chain
   GQ_TRY(gq::tc::launch(x, ldx, x, ldx, tokens, d, d, ht, d, 0, 1, ss, 1));
@@ -967,8 +967,6 @@ int gq_factor_from_x_attempt(const uint16_t* x, int64_t tokens, int64_t d, int64
   }
   GQ_CHECK_CUDA(cudaEventRecord(ev_all, ss));
   // chain stream: rec(A11) as soon as A11 is formed, the rest once H is
-  gq::Forks* forks = nullptr;
-  GQ_TRY(gq::forks_for(cs, &forks));
   GQ_CHECK_CUDA(cudaStreamWaitEvent(cs, ev_a11, 0));
   GQ_TRY(gq::inv_chol_rec(ht, n1, d, scratch, status, cs, forks, 1));
   GQ_CHECK_CUDA(cudaStreamWaitEvent(cs, ev_all, 0));
