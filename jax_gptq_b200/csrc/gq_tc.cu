@@ -222,7 +222,7 @@ gemm_tn_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant_
   uint64_t* tempty = tfull + 2;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tempty + 2);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
-  // epilogue: warp 2's verdict on each accumulator wait, by chunk parity
+  // epilogue: warp 2's outcome of each accumulator wait, by chunk parity
   volatile int* epi_go = abort_flag + 1;
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -340,7 +340,7 @@ gemm_tn_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant_
     // sleep at a named barrier instead of spinning (their issue slots belong
     // to the MMA and TMA threads on the same schedulers).  Control flow stays
     // uniform across the eight warps: every loop decision uses warp 2's
-    // verdict, published before the named barrier.
+    // outcome, published before the named barrier.
     for (int t = blockIdx.x; ok && t < p.num_tiles; t += gridDim.x) {
       int bm, bn;
       tile_coords(p, t, bm, bn);
