@@ -88,7 +88,7 @@ class ClockSampler:
             self.fh = open(self.path, "w")
             self.proc = subprocess.Popen(
                 ["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.QUERY}",
-                 "--format=csv,noheader,nounits", "-lms", "200"], stdout=self.fh,
+                 "--format=csv,noheader,nounits", "-lms", "50"], stdout=self.fh,
                 stderr=subprocess.DEVNULL)
         except Exception:
             self.proc = None
