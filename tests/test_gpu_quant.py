@@ -281,3 +281,33 @@ def test_qronos_codes_match_float32_oracle_up_to_rounding_ties():
     dist = np.abs(pre - np.floor(pre) - 0.5)
     assert np.all(dist <= 2e-3), (dist.max(), len(bad_rows))
     assert len(bad_rows) <= 0.1 * m, (len(bad_rows), int(diff.sum()))
+
+
+def test_factor_attempt_replays_from_a_cuda_graph():
+    """The factor's side-stream fork joins a stream capture through its events:
+    after one call on the capture stream (which creates that stream's side
+    stream), the attempt captured in a CUDA graph and replayed gives the eager
+    factor bit for bit."""
+    rng = np.random.default_rng(21)
+    d = 1152
+    x = torch.from_numpy(rng.standard_normal((2 * d, d)).astype(np.float32)).cuda()
+    h = x.T @ x
+    cfg = QuantConfig(ordering_mode="diag_h", semantics="intended")
+    s = torch.cuda.Stream()
+    s.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(s):
+        eager, st = G.factor_hessian_attempt0(h, cfg)
+        eager_u = eager.u.clone()
+    torch.cuda.current_stream().wait_stream(s)
+    torch.cuda.synchronize()
+    assert st.item() == 0
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g, stream=s):
+        cap, cst = G.factor_hessian_attempt0(h, cfg)
+    cap.u.zero_()
+    torch.cuda.synchronize()
+    g.replay()
+    torch.cuda.synchronize()
+    assert cst.item() == 0
+    assert torch.equal(cap.u, eager_u)
+    assert torch.equal(cap.perm, eager.perm)
