@@ -80,7 +80,9 @@ class ClockSampler:
     def __init__(self, gpu_index: int):
         self.gpu = gpu_index
         self.proc = None
-        self.path = os.path.join(ROOT, "gpurun_out", f"clocks_gpu{gpu_index}.csv")
+        # raw samples (one CSV per GPU); the JSON line carries their summary
+        out = os.environ.get("GQ_CLOCKS_DIR", os.path.join(ROOT, "bench_clocks"))
+        self.path = os.path.join(out, f"clocks_gpu{gpu_index}.csv")
 
     def start(self):
         try:
