@@ -291,8 +291,10 @@ __device__ bool sub_factor(float (&r)[SUB], float* xd, float* lt, float* cb, flo
         nx[4 * g + 2] = v.z;
         nx[4 * g + 3] = v.w;
       }
+      // off the pivot chain: l_ij l_kj = (l_ij rl) a_kj, one FMA per entry
+      const float lr = lij * rl;
 #pragma unroll
-      for (int k = j + 2; k < SUB; ++k) r[k] = fmaf(-lij, cv[k] * rl, r[k]);
+      for (int k = j + 2; k < SUB; ++k) r[k] = fmaf(-lr, cv[k], r[k]);
 #pragma unroll
       for (int k = j + 1; k < SUB; ++k) cv[k] = nx[k];
     }
