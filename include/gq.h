@@ -243,7 +243,10 @@ int gq_gptq_sweep(const float* w, int64_t m, int64_t n, int64_t ldw, const float
  * roughly 6 million weights) return GQ_EINVAL.  All calls on a device share the
  * buffer: calls that may overlap on the GPU race and must be ordered.  The
  * first call on each device looks up the buffer's address; make it before any
- * stream capture begins.
+ * stream capture begins.  The address is cached per (device, CUDA context);
+ * a call made from another context (after cudaDeviceReset, or a context the
+ * caller created) looks it up again, so that first call after the change
+ * must also come before any capture.
  */
 #define GQ_SWEEP_STATIC_SCRATCH_BYTES (32ll * 1024 * 1024)
 int gq_gptq_sweep_static(const float* w, int64_t m, int64_t n, int64_t ldw, const float* start,

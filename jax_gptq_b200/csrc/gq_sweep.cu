@@ -616,8 +616,24 @@ inline int64_t sweep_ubt_offset(int64_t m, int64_t n) {
 }
 
 // ubt holds a band [<= 512, 128] or the far block U[s0:s1, s1:]^T [n - s1, 512].
+// Only meaningful for shapes that pass sweep_shape_ok (no int64 overflow).
 int64_t sweep_ws_bytes(int64_t m, int64_t n) {
   return sweep_ubt_offset(m, n) + n * SW_SUPER * 4 + 256;
+}
+
+// Largest n whose row (float value + code per column) fits the shared-memory
+// row buffer of the gather / scatter kernels.
+constexpr int64_t kSweepMaxCols = (220 * 1024 - 64) / 5;
+
+// Rejects shapes whose workspace size would not fit in int64: the workspace
+// is below m * (5 * round4(n) + 4 * 512 + 8) + n * 2048 + 768 bytes.
+int sweep_shape_ok(const char* who, int64_t m, int64_t n) {
+  GQ_REQUIRE(m >= 0 && n >= 0, "%s: negative shape %lld x %lld", who, (long long)m, (long long)n);
+  GQ_REQUIRE(n <= kSweepMaxCols, "%s: n=%lld exceeds the row buffer (at most %lld columns)", who,
+             (long long)n, (long long)kSweepMaxCols);
+  const int64_t per_row = 8 * round4(n) + 8 * SW_SUPER + 64;
+  GQ_REQUIRE(m <= (INT64_MAX / 2) / per_row, "%s: m=%lld rows is too large", who, (long long)m);
+  return GQ_OK;
 }
 
 int transpose2d(const float* src, int64_t rows, int64_t cols, int64_t lds, float* dst, int64_t ldd,
@@ -646,13 +662,21 @@ int gq_gptq_sweep(const float* w, int64_t m, int64_t n, int64_t ldw, const float
              "gq_gptq_sweep: group0_scale and group0_zero must both be given or both NULL");
   GQ_REQUIRE((scales == nullptr) == (zeros == nullptr),
              "gq_gptq_sweep: scales and zeros must both be given or both NULL");
+  GQ_TRY(sweep_shape_ok("gq_gptq_sweep", m, n));
   GQ_REQUIRE(workspace_bytes >= sweep_ws_bytes(m, n), "gq_gptq_sweep: workspace too small");
   GQ_REQUIRE((reinterpret_cast<uintptr_t>(workspace) & 255) == 0,
              "gq_gptq_sweep: workspace must be 256-byte aligned");
-  GQ_REQUIRE(n * 5 + 64 <= 220 * 1024, "gq_gptq_sweep: n=%lld exceeds the row buffer",
-             (long long)n);
-  if (m == 0 || n == 0) return GQ_OK;
+  if (n == 0) return GQ_OK;
   cudaStream_t st = as_stream(stream);
+  if (m == 0) {
+    // no rows (e.g. an empty row shard): the group index of every column is
+    // still an output, and it depends only on the permutation
+    if (g_idx) {
+      g_idx_kernel<<<(unsigned)ceil_div(n, 256), 256, 0, st>>>(perm, n, group_size, g_idx);
+      GQ_TRY(check_launch("g_idx"));
+    }
+    return GQ_OK;
+  }
   const int64_t ldp = round4(n);
   char* ws = reinterpret_cast<char*>(workspace);
   float* wp = reinterpret_cast<float*>(ws);

@@ -24,7 +24,12 @@
 // Host code must not hand the array's name to a kernel: on the host it is a
 // stand-in symbol, not a device address.  The first call on each device (with
 // that device current) looks the real address up with cudaGetSymbolAddress
-// and caches it; make that first call before any stream capture begins.
+// and caches it together with the CUDA context it was resolved in; make that
+// first call before any stream capture begins.  A later call from a different
+// context on the same device (after cudaDeviceReset, or from a context the
+// caller created) resolves the address again instead of using a stale one.
+#include <cuda.h>
+
 #include "gq_common.cuh"
 
 #include <mutex>
@@ -32,6 +37,7 @@
 namespace gq {
 
 int64_t sweep_ws_bytes(int64_t m, int64_t n);
+int sweep_shape_ok(const char* who, int64_t m, int64_t n);
 
 constexpr int64_t kStaticSweepScratchBytes = 32ll * 1024 * 1024;
 static_assert(kStaticSweepScratchBytes == GQ_SWEEP_STATIC_SCRATCH_BYTES,
@@ -41,20 +47,44 @@ static __device__ __align__(256) unsigned char g_sweep_scratch[kStaticSweepScrat
 
 static std::mutex g_scratch_mu;
 static void* g_scratch_addr[128] = {};
+static CUcontext g_scratch_ctx[128] = {};
 
-// Device address of g_sweep_scratch on the current device (looked up once).
+typedef CUresult (*CtxGetCurrentFn)(CUcontext*);
+
+// The calling thread's current CUDA context (driver entry point, so the
+// library needs no link against libcuda); nullptr when it cannot be read.
+static CUcontext current_context() {
+  static CtxGetCurrentFn fn = [] {
+    void* ptr = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuCtxGetCurrent", &ptr, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      return reinterpret_cast<CtxGetCurrentFn>(ptr);
+    return static_cast<CtxGetCurrentFn>(nullptr);
+  }();
+  CUcontext ctx = nullptr;
+  if (fn == nullptr || fn(&ctx) != CUDA_SUCCESS) return nullptr;
+  return ctx;
+}
+
+// Device address of g_sweep_scratch on the current device, looked up once per
+// (device, context) pair.
 static int static_scratch_address(void** out) {
   int dev = -1;
   GQ_CHECK_CUDA(cudaGetDevice(&dev));
   GQ_REQUIRE(dev >= 0 && dev < 128, "gq_gptq_sweep_static: device index %d out of range", dev);
+  // nullptr until the runtime has bound a context to this thread; the lookup
+  // below binds the device's primary context
+  CUcontext ctx = current_context();
   std::lock_guard<std::mutex> lock(g_scratch_mu);
-  if (g_scratch_addr[dev] == nullptr) {
+  if (g_scratch_addr[dev] == nullptr || ctx == nullptr || g_scratch_ctx[dev] != ctx) {
     void* addr = nullptr;
     cudaError_t e = cudaGetSymbolAddress(&addr, g_sweep_scratch);
     if (e != cudaSuccess || addr == nullptr)
       return fail(GQ_ECUDA, "gq_gptq_sweep_static: cudaGetSymbolAddress failed on device %d: %s",
                   dev, cudaGetErrorString(e));
     g_scratch_addr[dev] = addr;
+    g_scratch_ctx[dev] = current_context();
   }
   *out = g_scratch_addr[dev];
   return GQ_OK;
@@ -69,7 +99,7 @@ extern "C" int gq_gptq_sweep_static(const float* w, int64_t m, int64_t n, int64_
                                     const float* group0_zero, int noprop_cols, float* dequant,
                                     uint8_t* codes, float* scales, float* zeros, int32_t* g_idx,
                                     void* stream) {
-  GQ_REQUIRE(m >= 0 && n >= 0, "gq_gptq_sweep_static: negative shape");
+  GQ_TRY(gq::sweep_shape_ok("gq_gptq_sweep_static", m, n));  // before any size arithmetic
   const int64_t need = gq::sweep_ws_bytes(m, n);
   GQ_REQUIRE(need <= gq::kStaticSweepScratchBytes,
              "gq_gptq_sweep_static: a %lld x %lld sweep needs %lld bytes of scratch but the "

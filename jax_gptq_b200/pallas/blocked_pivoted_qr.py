@@ -323,10 +323,30 @@ def benchmark(n: int = 4096, panel: int = 64, reps: int = 2, seed: int = 1) -> d
         if sem == "intended":
             q_err = _residual_dev(mat, res)
             entry["residual"] = q_err
-            d = res.work.diagonal().abs()
-            entry["numerical_rank"] = int((d > d[0] * 1e-5).sum().item())
+            entry.update(numerical_rank(res.work))
         out[label] = entry
     return out
+
+
+RANK_RCOND = 1e-7  # relative to max |R_jj|: just under float32 epsilon (1.19e-7)
+
+
+def numerical_rank(work: torch.Tensor, rcond: float = RANK_RCOND) -> dict:
+    """Numerical rank from the diagonal of R: the number of ``|R_jj|`` above
+    ``rcond * max_j |R_jj|`` (the largest, not the first: in ``smallest`` mode
+    the first pivot is the smallest column), plus the position of the largest
+    drop between consecutive ``|R_jj|`` of the sorted diagonal."""
+    d = work.diagonal().abs().double()
+    top = float(d.max().item()) if d.numel() else 0.0
+    rank = int((d > rcond * top).sum().item()) if top > 0 else 0
+    ds = torch.sort(d, descending=True).values
+    gap_at, gap = 0, 1.0
+    if ds.numel() > 1:
+        ratios = ds[:-1] / torch.clamp(ds[1:], min=1e-300)
+        j = int(torch.argmax(ratios).item())
+        gap_at, gap = j + 1, float(ratios[j].item())
+    return {"numerical_rank": rank, "rank_rcond": rcond, "largest_gap_at": gap_at,
+            "largest_gap_ratio": gap}
 
 
 def _residual_dev(a: torch.Tensor, res: QRResult) -> float:

@@ -1,8 +1,9 @@
 """Generate the golden vectors in ``tests/golden/*.npz`` from the reference itself.
 
-Run in a container that has the reference checked out (read-only is fine):
+Run in a container that has the reference checked out (read-only is fine),
+naming its ``src`` directory on the command line or in ``JAX_GPTQ_REFERENCE_SRC``:
 
-    python tests/golden/make_golden.py --reference-src /root/reference/src
+    python tests/golden/make_golden.py --reference-src <checkout>/src
 
 JAX is not installable offline, so the reference's own, unmodified modules
 (``quant.py``, ``stats.py``, ``gptq_ref.py``, ``qronos_ref.py``,
@@ -190,9 +191,12 @@ def make_eigh_cases(jnp, ref, gptq_ref):
 
 def main() -> None:
     ap = argparse.ArgumentParser()
-    ap.add_argument("--reference-src", default="/root/reference/src")
+    ap.add_argument("--reference-src", default=os.environ.get("JAX_GPTQ_REFERENCE_SRC"),
+                    help="the reference checkout's src directory (or set JAX_GPTQ_REFERENCE_SRC)")
     ap.add_argument("--out", default=HERE)
     args = ap.parse_args()
+    if not args.reference_src:
+        ap.error("--reference-src (or JAX_GPTQ_REFERENCE_SRC) is required")
     jnp, ref, gptq_ref, bpq = _import_reference(args.reference_src)
     np.savez_compressed(os.path.join(args.out, "rtn_golden.npz"), **make_rtn_cases(jnp, ref))
     np.savez_compressed(os.path.join(args.out, "gptq_golden.npz"),

@@ -70,3 +70,25 @@ def test_single_rank_driver_matches_layer_set_path():
     for name, _m, _n, _g in SHAPES:
         assert got[name].dequant.equal(ref[name].dequant), name
         assert got[name].codes.equal(ref[name].codes), name
+
+
+def test_empty_row_shard_still_writes_group_indices():
+    """A rank whose row shard is empty (fewer rows than 32 * world) still
+    returns the group index of every column: g_idx depends only on the
+    permutation, and the sharded driver hands one rank's g_idx to every
+    member linear.  The output buffer starts as garbage on purpose."""
+    w = LS.synth_weights(SHAPES, 0.02, 3)["q"]
+    x = _inputs()["a"]
+    h = torch.empty((512, 512), dtype=torch.float32, device="cuda")
+    stats.syrk_into(h, x, accumulate=False)
+    cfg = QuantConfig(w_bits=4, group_size=128, ordering_mode="diag_h", semantics="intended")
+    f = factor_hessian(h, cfg)
+    whole = gptq_sweep(w, f.u, f.perm, cfg)
+    r0, r1 = D.shard_range(w.shape[0], 8, 9, D.SWEEP_ROW_ALIGN)
+    assert r0 == r1  # 256 rows, 9 ranks of 32: the last rank has none
+    torch.cuda.empty_cache()
+    junk = torch.full((1 << 20,), -7, dtype=torch.int32, device="cuda")  # dirty the allocator's blocks
+    del junk
+    empty = gptq_sweep(w[r0:r1], f.u, f.perm, cfg)
+    assert empty.dequant.shape == (0, 512)
+    assert empty.g_idx.equal(whole.g_idx)
