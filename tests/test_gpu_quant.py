@@ -174,7 +174,7 @@ def test_gptq_intended_reconstruction_matches_oracle():
     e_gpu = og.reconstruction_error(w, res.dequant.cpu().numpy(), h)
     e_ref = og.reconstruction_error(w, ref["dequant"], h)
     e_rtn = og.reconstruction_error(w, oq.quantize_dequantize(w, 4, 128), h)
-    assert abs(e_gpu - e_ref) <= 1e-3 * max(e_ref, 1e-12) + 2e-3 * e_ref, (e_gpu, e_ref)
+    assert abs(e_gpu - e_ref) <= 1e-3 * e_ref, (e_gpu, e_ref)
     assert e_gpu < e_rtn
     codes = res.codes.cpu().numpy().astype(np.float32)
     agree = np.mean(codes == ref["q"])
@@ -194,7 +194,7 @@ def test_qronos_intended_matches_oracle():
     def err(w_hat):
         return np.linalg.norm(x.astype(np.float64) @ w.T - xt.astype(np.float64) @ w_hat.T)
     e_gpu, e_ref = err(out), err(ref["dequant"])
-    assert abs(e_gpu - e_ref) <= 5e-3 * e_ref, (e_gpu, e_ref)
+    assert abs(e_gpu - e_ref) <= 1e-3 * e_ref, (e_gpu, e_ref)
     assert e_gpu < err(oq.quantize_dequantize(w, 3, 128))
 
 
