@@ -129,6 +129,26 @@ int gq_gemm_tn_bf16(const uint16_t* xa, int64_t lda, const uint16_t* xb, int64_t
  * the stream; reset = 1 clears the word afterwards. */
 int gq_device_status(int* status_out, int reset, void* stream);
 
+/* gq_device_status as a status code: BLOCKING (synchronizes the stream),
+ * clears the word, and returns GQ_ETIMEOUT when a kernel's bounded wait
+ * expired since the last check (that kernel returned early and its outputs
+ * are incomplete), GQ_OK otherwise.  The reference has no device-side waits;
+ * this is the device half of its failure handling (gptq_ref.py:79-92 catches
+ * numeric failures on the host). */
+int gq_check_device(void* stream);
+
+/* Bound, in nanoseconds, on every device-side wait of the tensor-core
+ * kernels launched afterwards on the current device (default 2 s; accepted
+ * range 1 ms .. 60 s).  For tests that make a wait expire on purpose. */
+int gq_set_wait_limit_ns(uint64_t ns);
+
+/* Test entry: launches one thread that waits on an mbarrier nothing arrives
+ * on, through the same bounded-wait code as the statistics kernels (unit 0)
+ * or the fp32 tensor-core GEMM (unit 1).  The wait expires after the limit
+ * above, *observed (device int) becomes 1, and the unit's status word reads
+ * GQ_DEVERR_TIMEOUT; nothing traps or faults.  No reference counterpart. */
+int gq_test_expire_wait(int unit, int* observed, void* stream);
+
 /* stats.py:4-18 for float32 activations (CUDA-core fp32 GEMM). */
 int gq_syrk_f32(const float* x, int64_t tokens, int64_t d, int64_t ldx,
                 float* h, int64_t ldh, int accumulate, void* stream);
@@ -342,8 +362,16 @@ int gq_unpack_dequant(const uint32_t* packed, int64_t m, int64_t n, int64_t ldp,
  * gq_allreduce_sum_f32  buf[0:count] summed over the ranks, in place,
  *                       stream-ordered on `stream` (device of the handle).
  *                       A rank that never joins leaves the others waiting
- *                       inside NCCL; hosts that need a bound use NCCL's own
- *                       timeout settings. */
+ *                       inside NCCL until a host-side watchdog (a heartbeat
+ *                       or a timeout on another thread) calls
+ *                       gq_handle_abort, which ends the wait with an error.
+ * gq_comm_check         polls NCCL's asynchronous error state (a failed or
+ *                       lost peer); GQ_ENCCL when set, after aborting the
+ *                       communicator if abort_on_error and the handle owns it.
+ *                       Later collectives on an aborted handle return
+ *                       GQ_ENCCL without launching.
+ * gq_handle_abort       aborts an owned communicator (safe from another host
+ *                       thread while a collective is stuck). */
 typedef struct gq_handle gq_handle;
 int gq_nccl_unique_id(void* id_out, int64_t id_bytes);
 int gq_handle_create(int device, void* nccl_comm, gq_handle** out);
@@ -352,6 +380,8 @@ int gq_handle_create_nccl(int device, const void* unique_id, int nranks, int ran
 int gq_handle_destroy(gq_handle* h);
 int gq_handle_ranks(const gq_handle* h, int* nranks, int* rank);
 int gq_allreduce_sum_f32(gq_handle* h, float* buf, int64_t count, void* stream);
+int gq_comm_check(gq_handle* h, int abort_on_error);
+int gq_handle_abort(gq_handle* h);
 
 #ifdef __cplusplus
 }

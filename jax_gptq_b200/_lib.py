@@ -40,6 +40,8 @@ SIGNATURES = {
     "gq_handle_destroy": (c_int, [_P]),
     "gq_handle_ranks": (c_int, [_P, ctypes.POINTER(c_int), ctypes.POINTER(c_int)]),
     "gq_allreduce_sum_f32": (c_int, [_P, _P, c_int64, _P]),
+    "gq_comm_check": (c_int, [_P, c_int]),
+    "gq_handle_abort": (c_int, [_P]),
     "gq_rtn": (c_int, [_P, c_int64, c_int64, c_int64, _P, c_int, c_int, c_int, _P, _P, _P, _P, _P]),
     "gq_sgemm": (c_int, [c_int, c_int, c_int64, c_int64, c_int64, c_float, _P, c_int64, _P, c_int64,
                          c_float, _P, c_int64, c_int, _P]),
@@ -67,6 +69,9 @@ SIGNATURES = {
     "gq_gptq_sweep": (c_int, [_P, c_int64, c_int64, c_int64, _P, _P, c_int64, _P, c_int, c_int, c_int,
                               c_int, _P, _P, c_int, _P, _P, _P, _P, _P, _P, c_int64, _P]),
     "gq_device_status": (c_int, [ctypes.POINTER(c_int), c_int, _P]),
+    "gq_check_device": (c_int, [_P]),
+    "gq_set_wait_limit_ns": (c_int, [ctypes.c_uint64]),
+    "gq_test_expire_wait": (c_int, [c_int, _P, _P]),
     "gq_gptq_sweep_static": (c_int, [_P, c_int64, c_int64, c_int64, _P, _P, c_int64, _P, c_int,
                                      c_int, c_int, c_int, _P, _P, c_int, _P, _P, _P, _P, _P, _P]),
     "gq_qrcp_workspace_size": (c_int64, [c_int64, c_int64, c_int]),
@@ -86,6 +91,11 @@ class GQError(RuntimeError):
     def __init__(self, status: int, message: str):
         super().__init__(f"libgq status {status}: {message}")
         self.status = status
+
+
+class DeviceTimeout(GQError):
+    """GQ_ETIMEOUT: a kernel's bounded device-side wait expired; the kernel
+    returned early (no trap), so its outputs are incomplete."""
 
 
 _lib = None
@@ -122,5 +132,17 @@ def call(name: str, *args):
         msg = lib().gq_last_error().decode(errors="replace")
         if status == GQ_EINVAL:
             raise ValueError(msg)
+        if status == GQ_ETIMEOUT:
+            raise DeviceTimeout(status, msg)
         raise GQError(status, msg)
     return status
+
+
+def check_device(stream=None) -> None:
+    """Raise :class:`DeviceTimeout` if a bounded device-side wait expired
+    since the last check (``gq_check_device``; synchronizes ``stream``, by
+    default torch's current stream)."""
+    if stream is None:
+        import torch
+        stream = torch.cuda.current_stream().cuda_stream
+    call("gq_check_device", stream)

@@ -20,6 +20,7 @@ struct gq_handle {
   int owns_comm;
   int nranks;
   int rank;
+  int aborted;      // the communicator was aborted (gq_comm_check / gq_handle_abort)
 };
 
 namespace gq {
@@ -34,6 +35,8 @@ struct Api {
   ncclResult_t (*all_reduce)(const void*, void*, size_t, ncclDataType_t, ncclRedOp_t, ncclComm_t,
                              cudaStream_t) = nullptr;
   const char* (*error_string)(ncclResult_t) = nullptr;
+  ncclResult_t (*get_async_error)(ncclComm_t, ncclResult_t*) = nullptr;
+  ncclResult_t (*comm_abort)(ncclComm_t) = nullptr;
   bool ok = false;
 };
 
@@ -52,8 +55,12 @@ static const Api& api() {
     a.comm_user_rank = reinterpret_cast<decltype(a.comm_user_rank)>(dlsym(h, "ncclCommUserRank"));
     a.all_reduce = reinterpret_cast<decltype(a.all_reduce)>(dlsym(h, "ncclAllReduce"));
     a.error_string = reinterpret_cast<decltype(a.error_string)>(dlsym(h, "ncclGetErrorString"));
+    a.get_async_error =
+        reinterpret_cast<decltype(a.get_async_error)>(dlsym(h, "ncclCommGetAsyncError"));
+    a.comm_abort = reinterpret_cast<decltype(a.comm_abort)>(dlsym(h, "ncclCommAbort"));
     a.ok = a.get_unique_id && a.comm_init_rank && a.comm_destroy && a.comm_count &&
-           a.comm_user_rank && a.all_reduce && a.error_string;
+           a.comm_user_rank && a.all_reduce && a.error_string && a.get_async_error &&
+           a.comm_abort;
   });
   return a;
 }
@@ -104,7 +111,7 @@ int gq_handle_create(int device, void* nccl_comm, gq_handle** out) {
     if (r == ncclSuccess) r = a.comm_user_rank(static_cast<ncclComm_t>(nccl_comm), &rank);
     if (r != ncclSuccess) return gq::comm::nccl_fail("gq_handle_create", r);
   }
-  *out = new gq_handle{device, static_cast<ncclComm_t>(nccl_comm), 0, nranks, rank};
+  *out = new gq_handle{device, static_cast<ncclComm_t>(nccl_comm), 0, nranks, rank, 0};
   return GQ_OK;
 }
 
@@ -122,7 +129,7 @@ int gq_handle_create_nccl(int device, const void* unique_id, int nranks, int ran
   ncclComm_t comm = nullptr;
   ncclResult_t r = a.comm_init_rank(&comm, nranks, id, rank);
   if (r != ncclSuccess) return gq::comm::nccl_fail("ncclCommInitRank", r);
-  *out = new gq_handle{device, comm, 1, nranks, rank};
+  *out = new gq_handle{device, comm, 1, nranks, rank, 0};
   return GQ_OK;
 }
 
@@ -145,8 +152,43 @@ int gq_handle_ranks(const gq_handle* h, int* nranks, int* rank) {
   return GQ_OK;
 }
 
+int gq_comm_check(gq_handle* h, int abort_on_error) {
+  GQ_REQUIRE(h != nullptr, "gq_comm_check: NULL handle");
+  if (h->aborted) return gq::fail(GQ_ENCCL, "gq_comm_check: the communicator was aborted");
+  if (h->comm == nullptr) return GQ_OK;
+  const auto& a = gq::comm::api();
+  ncclResult_t async = ncclSuccess;
+  ncclResult_t r = a.get_async_error(h->comm, &async);
+  if (r != ncclSuccess) return gq::comm::nccl_fail("ncclCommGetAsyncError", r);
+  if (async == ncclSuccess || async == ncclInProgress) return GQ_OK;
+  if (abort_on_error && h->owns_comm) {
+    gq::comm::DeviceScope scope(h->device);
+    a.comm_abort(h->comm);  // ends this rank's outstanding collectives
+    h->comm = nullptr;
+    h->aborted = 1;
+  }
+  return gq::fail(GQ_ENCCL, "NCCL asynchronous error on rank %d of %d: %s%s", h->rank, h->nranks,
+                  a.error_string(async), h->aborted ? " (communicator aborted)" : "");
+}
+
+int gq_handle_abort(gq_handle* h) {
+  GQ_REQUIRE(h != nullptr, "gq_handle_abort: NULL handle");
+  GQ_REQUIRE(h->owns_comm || h->comm == nullptr,
+             "gq_handle_abort: the communicator belongs to the caller; abort it there");
+  if (h->comm) {
+    gq::comm::DeviceScope scope(h->device);
+    ncclResult_t r = gq::comm::api().comm_abort(h->comm);
+    h->comm = nullptr;
+    h->aborted = 1;
+    if (r != ncclSuccess) return gq::comm::nccl_fail("ncclCommAbort", r);
+  }
+  h->aborted = 1;
+  return GQ_OK;
+}
+
 int gq_allreduce_sum_f32(gq_handle* h, float* buf, int64_t count, void* stream) {
   GQ_REQUIRE(h != nullptr, "gq_allreduce_sum_f32: NULL handle");
+  if (h->aborted) return gq::fail(GQ_ENCCL, "gq_allreduce_sum_f32: the communicator was aborted");
   GQ_REQUIRE(h->comm != nullptr, "gq_allreduce_sum_f32: the handle has no communicator");
   GQ_REQUIRE(count >= 0 && (count == 0 || buf != nullptr), "gq_allreduce_sum_f32: bad buffer");
   if (count == 0) return GQ_OK;

@@ -68,8 +68,11 @@ __device__ __forceinline__ uint64_t globaltimer_ns() {
   return t;
 }
 
-// Upper bound for any device-side wait (a wait that outlives it records
-// GQ_DEVERR_TIMEOUT in the kernel's status word and gives up).
+// Default upper bound for any device-side wait (a wait that outlives it
+// records GQ_DEVERR_TIMEOUT in the kernel's status word and gives up).  Each
+// translation unit with bounded waits keeps the bound in a __device__
+// variable that gq_set_wait_limit_ns changes (tests shorten it to make a
+// wait expire quickly).
 constexpr uint64_t kWaitLimitNs = 2000000000ull;  // 2 s
 
 // Device status word values written by kernels.

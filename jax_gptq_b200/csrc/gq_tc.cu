@@ -38,6 +38,8 @@
 namespace gq {
 
 __device__ int g_device_status = 0;
+// this file's bound on every mbarrier wait (gq_set_wait_limit_ns)
+static __device__ uint64_t g_wait_limit_ns = kWaitLimitNs;
 
 namespace tc {
 
@@ -101,7 +103,7 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volati
   while (true) {
     if (mbar_try_wait(bar, parity)) return true;
     if (*abort_flag) return false;
-    if (globaltimer_ns() - t0 > kWaitLimitNs) {
+    if (globaltimer_ns() - t0 > g_wait_limit_ns) {
       *abort_flag = 1;
       atomicExch(&g_device_status, GQ_DEVERR_TIMEOUT);
       return false;
@@ -906,8 +908,32 @@ int launch(const void* xa, int64_t lda, const void* xb, int64_t ldb, int64_t K, 
 
 int symmetrize_upper(float* h, int64_t d, int64_t ldh, cudaStream_t st);
 
+namespace tc {
+// Failure-path check of this file's bounded wait: one thread waits on an
+// mbarrier that nothing arrives on, so mbar_wait must give up after
+// g_wait_limit_ns, record GQ_DEVERR_TIMEOUT and return false; *observed gets
+// 1 when it did.  No trap, no fault: the kernel then simply returns.
+__global__ void expire_wait_kernel(int* observed) {
+  __shared__ __align__(8) uint64_t bar;
+  __shared__ int abort_flag;
+  if (threadIdx.x == 0) {
+    abort_flag = 0;
+    mbar_init(&bar, 1);
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) *observed = mbar_wait(&bar, 0, &abort_flag) ? 0 : 1;
+}
+
+int set_wait_limit(uint64_t ns) {
+  GQ_CHECK_CUDA(cudaMemcpyToSymbol(g_wait_limit_ns, &ns, sizeof(ns)));
+  return GQ_OK;
+}
+}  // namespace tc
+
 namespace tc32 {
 int read_status(int reset, int* out);
+int set_wait_limit(uint64_t ns);
+int launch_expire_test(int* observed, cudaStream_t st);
 }
 
 }  // namespace gq
@@ -931,6 +957,31 @@ int gq_gemm_tn_bf16(const uint16_t* xa, int64_t lda, const uint16_t* xb, int64_t
   GQ_REQUIRE(g != nullptr && ldg >= db, "gq_gemm_tn_bf16: bad output");
   return gq::tc::launch(xa, lda, xb, ldb, tokens, da, db, g, ldg, accumulate, 0,
                         gq::as_stream(stream), 0);
+}
+
+int gq_set_wait_limit_ns(uint64_t ns) {
+  GQ_REQUIRE(ns >= 1000000ull && ns <= 60000000000ull,
+             "gq_set_wait_limit_ns: %llu ns is outside [1 ms, 60 s]", (unsigned long long)ns);
+  GQ_TRY(gq::tc::set_wait_limit(ns));
+  return gq::tc32::set_wait_limit(ns);
+}
+
+int gq_test_expire_wait(int unit, int* observed, void* stream) {
+  GQ_REQUIRE(observed != nullptr, "gq_test_expire_wait: NULL observed");
+  GQ_REQUIRE(unit == 0 || unit == 1, "gq_test_expire_wait: unit must be 0 or 1");
+  if (unit == 1) return gq::tc32::launch_expire_test(observed, gq::as_stream(stream));
+  gq::tc::expire_wait_kernel<<<1, 32, 0, gq::as_stream(stream)>>>(observed);
+  return gq::check_launch("bf16 expire_wait");
+}
+
+int gq_check_device(void* stream) {
+  int v = 0;
+  GQ_TRY(gq_device_status(&v, 1, stream));
+  if (v == gq::GQ_DEVERR_TIMEOUT)
+    return gq::fail(GQ_ETIMEOUT, "a bounded device-side wait expired: a kernel gave up and "
+                                 "returned early, so its outputs are incomplete");
+  if (v != gq::GQ_DEVERR_NONE) return gq::fail(GQ_ECUDA, "device status word %d", v);
+  return GQ_OK;
 }
 
 int gq_device_status(int* status_out, int reset, void* stream) {

@@ -31,6 +31,8 @@ namespace tc32 {
 // This file's device status word (device variables are per translation unit
 // without relocatable device code); gq_device_status() reads it.
 static __device__ int g_device_status = 0;
+// this file's bound on every mbarrier wait (gq_set_wait_limit_ns)
+static __device__ uint64_t g_wait_limit_ns = kWaitLimitNs;
 
 int read_status(int reset, int* out) {
   int v = 0;
@@ -104,7 +106,7 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volati
   while (true) {
     if (mbar_try_wait(bar, parity)) return true;
     if (*abort_flag) return false;
-    if (globaltimer_ns() - t0 > kWaitLimitNs) {
+    if (globaltimer_ns() - t0 > g_wait_limit_ns) {
       *abort_flag = 1;
       atomicExch(&g_device_status, GQ_DEVERR_TIMEOUT);
       return false;
@@ -612,6 +614,31 @@ int launch(int tb, int64_t M, int64_t N, int64_t K, float alpha, const float* A,
   const int grid = std::min(p.num_tiles, cta_budget());
   tf32x3_kernel<<<grid, THREADS, SMEM_BYTES, st>>>(ma, mbm, mc, p);
   return check_launch("tcgen05 tf32x3 gemm");
+}
+
+// Failure-path check of this file's bounded wait: one thread waits on an
+// mbarrier that nothing arrives on, so mbar_wait must give up after
+// g_wait_limit_ns, record GQ_DEVERR_TIMEOUT and return false; *observed gets
+// 1 when it did.  No trap, no fault: the kernel then simply returns.
+__global__ void expire_wait_kernel(int* observed) {
+  __shared__ __align__(8) uint64_t bar;
+  __shared__ int abort_flag;
+  if (threadIdx.x == 0) {
+    abort_flag = 0;
+    mbar_init(&bar, 1);
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) *observed = mbar_wait(&bar, 0, &abort_flag) ? 0 : 1;
+}
+
+int set_wait_limit(uint64_t ns) {
+  GQ_CHECK_CUDA(cudaMemcpyToSymbol(g_wait_limit_ns, &ns, sizeof(ns)));
+  return GQ_OK;
+}
+
+int launch_expire_test(int* observed, cudaStream_t st) {
+  expire_wait_kernel<<<1, 32, 0, st>>>(observed);
+  return check_launch("tf32x3 expire_wait");
 }
 
 }  // namespace tc32

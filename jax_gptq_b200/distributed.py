@@ -109,13 +109,78 @@ def layer_set_cost(shapes, tokens: int) -> float:
     return t
 
 
+class RankFailure(RuntimeError):
+    """A peer rank failed, left, or never contributed to a collective.
+
+    Raised on the surviving ranks, on the host, between launches: by
+    :class:`Heartbeat` when a rank's beat for a step does not arrive in time,
+    and by the collective helpers when the process group's timeout (or a
+    broken connection) ends a collective with an error."""
+
+
+def _collective(what: str, fn):
+    try:
+        return fn()
+    except RankFailure:
+        raise
+    except RuntimeError as exc:  # DistBackendError and gloo/NCCL timeouts derive from it
+        raise RankFailure(f"{what} failed: a peer rank did not contribute ({exc})") from exc
+
+
+class _Work:
+    """Wraps an async collective's work handle so ``wait`` raises RankFailure."""
+
+    def __init__(self, what: str, work):
+        self._what, self._work = what, work
+
+    def wait(self):
+        return _collective(self._what, self._work.wait)
+
+
 def allreduce_sum_(t: torch.Tensor, group=None, async_op: bool = False):
     """In-place sum over the ranks of ``group``; returns the work handle when
-    ``async_op`` (None for a single rank)."""
+    ``async_op`` (None for a single rank).  A rank that never joins ends the
+    call (or the handle's ``wait``) with :class:`RankFailure` once the
+    process group's timeout expires."""
     dist = _dist()
     if not (dist.is_available() and dist.is_initialized()) or dist.get_world_size(group) == 1:
         return None
-    return dist.all_reduce(t, op=dist.ReduceOp.SUM, group=group, async_op=async_op)
+    work = _collective("all_reduce", lambda: dist.all_reduce(t, op=dist.ReduceOp.SUM, group=group,
+                                                             async_op=async_op))
+    return _Work("all_reduce", work) if async_op else work
+
+
+class Heartbeat:
+    """Host-side liveness check between steps, through a ``torch.distributed``
+    key-value store (``TCPStore`` / ``FileStore``).
+
+    Each rank calls :meth:`beat` with the step it is about to start and then
+    :meth:`wait_all`, which returns once every rank has beaten for that step
+    and raises :class:`RankFailure` naming the missing ranks after
+    ``timeout_s``.  Ranks thus learn of a lost peer before launching the
+    step's kernels or collectives, instead of inside a collective."""
+
+    def __init__(self, store, rank: int, world: int, prefix: str = "gq/alive"):
+        self.store, self.rank, self.world, self.prefix = store, rank, world, prefix
+
+    def _key(self, step: int, rank: int) -> str:
+        return f"{self.prefix}/{step}/{rank}"
+
+    def beat(self, step: int) -> None:
+        self.store.set(self._key(step, self.rank), b"1")
+
+    def wait_all(self, step: int, timeout_s: float = 5.0, poll_s: float = 0.02) -> None:
+        import time
+        keys = [self._key(step, r) for r in range(self.world)]
+        deadline = time.monotonic() + timeout_s
+        while True:
+            missing = [r for r, k in enumerate(keys) if not self.store.check([k])]
+            if not missing:
+                return
+            if time.monotonic() >= deadline:
+                raise RankFailure(f"step {step}: no heartbeat from rank(s) {missing} within "
+                                  f"{timeout_s:g} s")
+            time.sleep(poll_s)
 
 
 def gather_rows(local: torch.Tensor, n_rows: int, group=None,
@@ -135,7 +200,7 @@ def gather_rows(local: torch.Tensor, n_rows: int, group=None,
     pad = torch.zeros((rows_max,) + tail, dtype=local.dtype, device=local.device)
     pad[: r1 - r0] = local
     blocks = [torch.empty_like(pad) for _ in range(world)]
-    _dist().all_gather(blocks, pad, group=group)
+    _collective("all_gather", lambda: _dist().all_gather(blocks, pad, group=group))
     return torch.cat([blocks[r][: b - a] for r, (a, b) in enumerate(spans)], dim=0)
 
 
@@ -254,6 +319,17 @@ class CommHandle:
             raise ValueError("allreduce_sum_ needs a contiguous float32 CUDA tensor")
         self._lib.call("gq_allreduce_sum_f32", self._h, A.ptr(t), t.numel(), A.stream())
 
+    def check(self, abort: bool = True) -> None:
+        """Raise ``GQError`` (GQ_ENCCL) if NCCL reports an asynchronous error
+        (a failed or lost peer); the communicator is aborted first when
+        ``abort``, so no later collective waits on the lost rank."""
+        self._lib.call("gq_comm_check", self._h, int(abort))
+
+    def abort(self) -> None:
+        """Abort the communicator: a collective stuck on a rank that never
+        joins ends with an error.  Callable from a watchdog thread."""
+        self._lib.call("gq_handle_abort", self._h)
+
     def close(self) -> None:
         if self._h is not None and self._h.value:
             self._lib.call("gq_handle_destroy", self._h)
@@ -267,7 +343,7 @@ class CommHandle:
 
 
 __all__ = [
-    "SWEEP_ROW_ALIGN", "rank_world", "shard_range", "lpt_assign", "layer_set_cost",
+    "SWEEP_ROW_ALIGN", "RankFailure", "Heartbeat", "rank_world", "shard_range", "lpt_assign", "layer_set_cost",
     "allreduce_sum_", "gather_rows", "hessians_token_sharded", "quantize_layer_gptq_sharded",
     "layer_sets_for_rank", "tokens_for_rank", "CommHandle",
 ]

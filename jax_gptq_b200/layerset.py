@@ -273,6 +273,7 @@ def _run_groups_concurrently(sizes: dict, form, work, redo, prepare=None, late=N
         for t in (res.dequant, res.codes, res.scales, res.zeros, res.g_idx, res.perm):
             t.record_stream(main)
     bad = torch.cat([st for st, _ in pending.values()]).cpu().tolist()
+    _lib.check_device()  # a kernel whose bounded wait expired left incomplete outputs
     out = {}
     for (grp, (_, res)), b in zip(pending.items(), bad):
         out[grp] = redo(grp, hs[grp]) if b else res

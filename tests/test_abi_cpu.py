@@ -124,3 +124,25 @@ def test_factor_from_activations_validates_before_launching():
     assert call(d=40000, ldx=40000, ldu=40000,
                 ws_bytes=lib.gq_factor_from_x_workspace_size(1024, 40000)) == _lib.GQ_EINVAL
     assert b"too large" in lib.gq_last_error()
+
+
+def test_wait_limit_and_failure_entries_reject_bad_arguments():
+    with pytest.raises(ValueError, match="outside"):
+        _lib.call("gq_set_wait_limit_ns", 10)
+    with pytest.raises(ValueError, match="outside"):
+        _lib.call("gq_set_wait_limit_ns", 10 ** 12)
+    with pytest.raises(ValueError, match="unit"):
+        _lib.call("gq_test_expire_wait", 2, ctypes.c_void_p(16), None)
+    with pytest.raises(ValueError, match="NULL"):
+        _lib.call("gq_comm_check", None, 1)
+    with pytest.raises(ValueError, match="NULL"):
+        _lib.call("gq_handle_abort", None)
+
+
+def test_sweep_rejects_shapes_whose_workspace_would_overflow():
+    with pytest.raises(ValueError, match="too large"):
+        _lib.call("gq_gptq_sweep_static", None, 1 << 60, 4096, 4096, None, None, 4096, None, 4,
+                  128, 0, 128, None, None, 0, None, None, None, None, None, None)
+    with pytest.raises(ValueError, match="row buffer"):
+        _lib.call("gq_gptq_sweep_static", None, 4, 1 << 20, 1 << 20, None, None, 1 << 20, None, 4,
+                  128, 0, 128, None, None, 0, None, None, None, None, None, None)

@@ -126,3 +126,62 @@ def test_gloo_two_ranks(tmp_path):
     assert sorted(outs[0]["layers"] + outs[1]["layers"]) == list(range(7))
     assert not set(outs[0]["layers"]) & set(outs[1]["layers"])
     assert outs[0]["tokens"] == (0, 501) and outs[1]["tokens"] == (501, 1001)
+
+
+def _worker_lost_peer(rank, world, port, store_port, out_dir):
+    """Rank 1 misses the step-1 heartbeat and never joins the all-reduce."""
+    import time
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world,
+                            timeout=datetime.timedelta(seconds=3))
+    store = dist.TCPStore("127.0.0.1", store_port, world, rank == 0,
+                          timeout=datetime.timedelta(seconds=60))
+    hb = D.Heartbeat(store, rank, world)
+    res = {}
+    hb.beat(0)
+    hb.wait_all(0, timeout_s=30)
+    if rank == 0:
+        hb.beat(1)
+        t0 = time.monotonic()
+        try:
+            hb.wait_all(1, timeout_s=1.0)
+            res["heartbeat"] = "no error"
+        except D.RankFailure as exc:
+            res["heartbeat"] = str(exc)
+        res["heartbeat_s"] = time.monotonic() - t0
+        t0 = time.monotonic()
+        try:
+            D.allreduce_sum_(torch.ones(8))
+            res["allreduce"] = "no error"
+        except D.RankFailure as exc:
+            res["allreduce"] = str(exc)
+        res["allreduce_s"] = time.monotonic() - t0
+        np.save(os.path.join(out_dir, "lost.npy"), res, allow_pickle=True)
+        store.set("done", b"1")
+        store.wait(["ack"])  # rank 0 hosts the store: keep it up until rank 1 has read "done"
+    else:
+        store.wait(["done"])  # stays alive (a lost peer, not a closed connection) until rank 0 is done
+        store.set("ack", b"1")
+    os._exit(0)  # no teardown collective with a peer that did not take part
+
+
+def test_gloo_rank_that_never_contributes_is_detected(tmp_path):
+    """Failure detection on the host: a missing heartbeat names the lost rank
+    before the next launch, and a collective the lost rank never joins ends
+    with RankFailure after the process group's timeout, not a hang."""
+    world = 2
+    ctx = mp.get_context("spawn")
+    port, store_port = _free_port(), _free_port()
+    procs = [ctx.Process(target=_worker_lost_peer, args=(r, world, port, store_port, str(tmp_path)))
+             for r in range(world)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(120)
+        assert p.exitcode == 0, p.exitcode
+    res = np.load(tmp_path / "lost.npy", allow_pickle=True).item()
+    assert "rank(s) [1]" in res["heartbeat"], res
+    assert 0.9 <= res["heartbeat_s"] < 10, res
+    assert "did not contribute" in res["allreduce"], res
+    assert res["allreduce_s"] < 60, res

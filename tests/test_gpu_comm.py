@@ -69,3 +69,22 @@ def test_two_gpu_hessian_allreduce(tmp_path):
     for o in outs:
         assert o["rel"] < 1e-6, o["rel"]
     assert np.array_equal(outs[0]["h"], outs[1]["h"])
+
+
+def test_single_rank_check_then_abort():
+    """A healthy communicator reports no asynchronous error; after an abort
+    (what a host watchdog does when a peer is lost) every collective on the
+    handle fails at once with GQ_ENCCL instead of waiting."""
+    from jax_gptq_b200 import _lib
+    uid = D.CommHandle.unique_id()
+    h = D.CommHandle(torch.cuda.current_device(), uid, 1, 0)
+    try:
+        h.check()
+        h.abort()
+        t = torch.randn(64, device="cuda")
+        with pytest.raises(_lib.GQError, match="aborted"):
+            h.allreduce_sum_(t)
+        with pytest.raises(_lib.GQError, match="aborted"):
+            h.check()
+    finally:
+        h.close()
