@@ -657,7 +657,7 @@ int gq_gptq_sweep(const float* w, int64_t m, int64_t n, int64_t ldw, const float
              "gq_gptq_sweep: group_size %d must divide 128 (>= 4) or be a multiple of 128",
              group_size);
   GQ_REQUIRE(u != nullptr && ldu >= n, "gq_gptq_sweep: bad u");
-  GQ_REQUIRE(w != nullptr && ldw >= n, "gq_gptq_sweep: bad w");
+  GQ_REQUIRE((w != nullptr || m == 0) && ldw >= n, "gq_gptq_sweep: bad w");
   GQ_REQUIRE((group0_scale == nullptr) == (group0_zero == nullptr),
              "gq_gptq_sweep: group0_scale and group0_zero must both be given or both NULL");
   GQ_REQUIRE((scales == nullptr) == (zeros == nullptr),

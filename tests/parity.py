@@ -10,7 +10,10 @@ codes of that row follow from the flipped error feedback and are counted,
 not checked.
 
 ``TIE_TOL`` is the largest distance from the half step (in units of one
-quantization step) that is accepted as a tie.
+quantization step) that is accepted as a tie: 1e-5, about ten float32 ulps
+of a 4-bit code value (ulp(8) = 9.5e-7).  Measured on B200, the first
+differing codes of the benchmark-size sweeps sat 1e-6 to 4e-6 from the half
+step.
 """
 
 from __future__ import annotations
@@ -20,7 +23,7 @@ import os
 
 import numpy as np
 
-TIE_TOL = 2e-3
+TIE_TOL = 1e-5
 
 
 def code_diffs(got_perm: np.ndarray, ref_perm: np.ndarray, ref_pre_perm: np.ndarray) -> dict:

@@ -26,6 +26,8 @@ from oracle import qronos as oqn
 from oracle import quant as oq
 from oracle import stats as ost
 
+from parity import TIE_TOL, code_diffs, report
+
 
 def _golden(golden_dir, name):
     return np.load(os.path.join(golden_dir, name))
@@ -205,7 +207,7 @@ def test_sweep_codes_match_float32_oracle_up_to_rounding_ties(m, n, bits, g):
     permutation: the two differ only in the order of float32 additions (lazy
     updates batched two-level on the GPU, BLAS in the oracle).  Rows are
     independent, so in every row the first code that differs must be a
-    rounding tie: the oracle's unrounded value within 2e-3 of a half step.
+    rounding tie: the oracle's unrounded value within TIE_TOL of a half step.
     Later codes of such a row follow from the flipped error and are counted,
     not checked.  g = 384 takes the 128-column fallback of the far update."""
     rng = np.random.default_rng(m + n + g)
@@ -221,14 +223,12 @@ def test_sweep_codes_match_float32_oracle_up_to_rounding_ties(m, n, bits, g):
     codes_p = res.codes.cpu().numpy().astype(np.float32)[:, perm]   # permuted order
     qmin = oq.qrange(bits, False)[0]
     ref_p = ref["q"][:, perm]
-    diff = codes_p + qmin != ref_p
-    bad_rows = np.flatnonzero(diff.any(axis=1))
-    first = diff[bad_rows].argmax(axis=1)
-    pre = ref["pre"][bad_rows, first].astype(np.float64)
-    dist = np.abs(pre - np.floor(pre) - 0.5)
-    assert np.all(dist <= 2e-3), (dist.max(), len(bad_rows))
+    cd = code_diffs(codes_p + qmin, ref_p, ref["pre"])
+    report(f"sweep_ties_{m}x{n}_b{bits}_g{g}", rows=m, tie_rows=cd["tie_rows"],
+           codes_differing=cd["codes_differing"], max_tie_dist=cd["max_tie_dist"])
+    assert cd["max_tie_dist"] <= TIE_TOL, (cd["max_tie_dist"], cd["tie_rows"])
     # and the flips are rare
-    assert len(bad_rows) <= 0.05 * m, (len(bad_rows), int(diff.sum()))
+    assert cd["tie_rows"] <= 0.05 * m, (cd["tie_rows"], cd["codes_differing"])
     assert np.array_equal(res.g_idx.cpu().numpy(), ref["g_idx"])
 
 
@@ -254,7 +254,7 @@ def test_sweep_single_warp_and_four_warp_block_steps_agree():
 def test_qronos_codes_match_float32_oracle_up_to_rounding_ties():
     """Qronos on the GPU against the float32 oracle given the same factor
     (U, permutation, damped H): the first code that differs in a row must be
-    a rounding tie of the oracle's unrounded value (within 2e-3 of a half
+    a rounding tie of the oracle's unrounded value (within TIE_TOL of a half
     step); later codes of that row follow from the flip."""
     m, n, bits, g = 256, 1024, 3, 128
     rng = np.random.default_rng(21)
@@ -274,13 +274,11 @@ def test_qronos_codes_match_float32_oracle_up_to_rounding_ties():
     qmin = oq.qrange(bits, False)[0]
     got_p = res.codes.cpu().numpy().astype(np.float32)[:, perm] + qmin
     ref_p = ref["q"][:, perm]
-    diff = got_p != ref_p
-    bad_rows = np.flatnonzero(diff.any(axis=1))
-    first = diff[bad_rows].argmax(axis=1)
-    pre = ref["pre"][bad_rows, first].astype(np.float64)
-    dist = np.abs(pre - np.floor(pre) - 0.5)
-    assert np.all(dist <= 2e-3), (dist.max(), len(bad_rows))
-    assert len(bad_rows) <= 0.1 * m, (len(bad_rows), int(diff.sum()))
+    cd = code_diffs(got_p, ref_p, ref["pre"])
+    report("qronos_ties_256x1024_b3", rows=m, tie_rows=cd["tie_rows"],
+           codes_differing=cd["codes_differing"], max_tie_dist=cd["max_tie_dist"])
+    assert cd["max_tie_dist"] <= TIE_TOL, (cd["max_tie_dist"], cd["tie_rows"])
+    assert cd["tie_rows"] <= 0.1 * m, (cd["tie_rows"], cd["codes_differing"])
 
 
 def test_factor_attempt_replays_from_a_cuda_graph():
