@@ -221,6 +221,221 @@ def intended_port_sample(shapes, sample_tokens=2048, sample_rows=64, chol_d=1024
                    f"linear (x m/{sample_rows})")
 
 
+# ----------------------------------------------------------------------------- single linear
+
+SINGLE_LINEAR = ("GPTQ on one 1024x1024 linear: W ~ N(0, 0.02^2) fp32, X 2048x1024 fp32 ~ N(0, 1) "
+                 "with 8 channels x20, H = X^T X / n, damp 0.01, 4-bit asym g128, block 128, "
+                 "no act-order, seed 0")
+
+
+def _single_linear_inputs(seed=0, m=1024, n=1024, tokens=2048, n_outliers=8):
+    """The single-linear configuration's inputs (numpy PCG64, the same bytes
+    the oracle's generator makes)."""
+    rng = np.random.Generator(np.random.PCG64(seed))
+    w = (rng.standard_normal((m, n)) * 0.02).astype(np.float32)
+    x = rng.standard_normal((tokens, n)).astype(np.float32)
+    cols = rng.choice(n, size=n_outliers, replace=False)
+    x[:, cols] *= np.float32(20.0)
+    return w, x
+
+
+def run_single_linear(peaks, steps=20, warmup=3, cpu=True):
+    """One linear end to end: H (fp32 activations), the damped factor and the
+    sweep.  ``value`` = device-resident ms per linear; ``e2e`` = the same
+    through the reference-facing calls h_g_from_activations ->
+    process_hessian -> gptq_forward_step on host numpy arrays."""
+    import torch
+    from jax_gptq_b200 import QuantConfig, gptq_forward_step, h_g_from_activations
+    from jax_gptq_b200 import process_hessian
+    from jax_gptq_b200 import gptq_ref as G
+    from jax_gptq_b200 import stats
+    w, x = _single_linear_inputs(0)
+    m, n = w.shape
+    tokens = x.shape[0]
+    cfg = QuantConfig(w_bits=4, group_size=128, sym=False, damp_percent=0.01,
+                      ordering_mode="none", semantics="intended")
+    wd, xd = torch.from_numpy(w).cuda(), torch.from_numpy(x).cuda()
+    h = torch.empty((n, n), dtype=torch.float32, device="cuda")
+
+    def step():
+        stats.syrk_into(h, xd, accumulate=False)
+        h.mul_(1.0 / tokens)
+        f = G.factor_hessian(h, cfg)
+        return G.gptq_sweep(wd, f.u, f.perm, cfg)
+
+    ms = _time(step, steps, warmup)
+    f = G.factor_hessian(h, cfg)
+    sweep_ms = _time(lambda: G.gptq_sweep(wd, f.u, f.perm, cfg), steps, warmup)
+    syrk_ms = _time(lambda: stats.syrk_into(h, xd, accumulate=False), steps, warmup)
+    factor_ms = _time(lambda: G.factor_hessian(h, cfg), steps, warmup)
+
+    # e2e: the reference's own call sequence on host arrays (each call copies in and out)
+    def host_step():
+        hh, _ = h_g_from_activations(x)
+        hh = hh / np.float32(tokens)
+        hinv, perm = process_hessian(hh, cfg)
+        return gptq_forward_step(w, hinv, perm, cfg), hh, hinv, perm
+
+    for _ in range(warmup):
+        host_step()
+    torch.cuda.synchronize()
+    t0 = time.perf_counter()
+    for _ in range(steps):
+        out, hh, hinv, perm = host_step()
+    e2e_s = (time.perf_counter() - t0) / steps
+    h2d = x.nbytes + hh.nbytes + w.nbytes + hinv.nbytes + perm.nbytes
+    d2h = hh.nbytes + hinv.nbytes + perm.nbytes + out.nbytes
+
+    sweep_bytes = 4 * m * n + 4 * n * n + 4 * m * n + m * n // 2 + 8 * m * (n // 128)
+    hbm = peaks["hbm_gbs"]
+    res = {
+        "workload": SINGLE_LINEAR, "value": ms, "unit": "ms/linear",
+        "phases_ms": {"h": syrk_ms, "factor": factor_ms, "sweep": sweep_ms},
+        "e2e": {"value": e2e_s * 1e3, "unit": "ms/linear", "h2d_bytes_per_step": int(h2d),
+                "d2h_bytes_per_step": int(d2h),
+                "path": "h_g_from_activations -> process_hessian -> gptq_forward_step on numpy"},
+        "roofline": {"bound": "hbm", "kernel": "gq_gptq_sweep (1024 x 1024)",
+                     "achieved": sweep_bytes / (sweep_ms / 1e3) / 1e9, "peak": hbm,
+                     "unit": "GB/s", "frac": sweep_bytes / (sweep_ms / 1e3) / 1e9 / hbm,
+                     "algorithmic": f"{sweep_bytes} bytes per sweep (W, U, dequant, packed codes, "
+                                    "scales/zeros)",
+                     "note": "latency-bound: a chain of 1024 dependent columns; the trailing "
+                             "updates are 0.94 GFLOP of 3xTF32 GEMMs"},
+    }
+    if cpu:
+        from oracle import gptq as og
+        with _all_host_threads():
+            t_cpu = []
+            for _ in range(2):
+                t0 = time.perf_counter()
+                hc = (x.T @ x) / np.float32(tokens)
+                u, perm_c, _ = og.process_hessian_intended(hc, "none", 0.01, dtype=np.float32)
+                og.gptq_sweep(w, u, perm_c, 4, 128, False, 128, np.float32)
+                t_cpu.append(time.perf_counter() - t0)
+        res["cpu_baseline"] = {"value": min(t_cpu) * 1e3, "unit": "ms/linear",
+                               "cores": _cpu_cores(), "kind": "port",
+                               "sample": "the whole configuration, not extrapolated: the oracle's "
+                                         "float32 H, damped Cholesky factor and GPTQ sweep"}
+    return res
+
+
+def qronos_port_sample(shapes, sample_tokens=2048, sample_rows=64, dc=1024, seed=0):
+    """The oracle's Qronos (the work the GPU does) on a bounded sample: h and g
+    on ``sample_tokens`` tokens (x tokens / sample), the damped factor at
+    d = ``dc`` (x (d/dc)^3), and the update of ``sample_rows`` rows at d = dc
+    given that factor (x (m/rows)(d/dc)^2: its products are m d^2)."""
+    from oracle import gptq as og
+    from oracle import qronos as oqn
+    rng = np.random.default_rng(seed + 2)
+    total = 0.0
+    dims, rows = {}, {}
+    for _, m, n, grp in shapes:
+        dims[grp] = n
+        rows[grp] = rows.get(grp, 0) + m
+    for grp, d in dims.items():
+        x = rng.standard_normal((sample_tokens, d)).astype(np.float32)
+        xt = (x + 0.05 * rng.standard_normal(x.shape)).astype(np.float32)
+        t0 = time.perf_counter()
+        h = xt.T @ xt
+        g = x.T @ xt
+        t_hg = time.perf_counter() - t0
+        hs, gs = h[:dc, :dc].astype(np.float32), g[:dc, :dc].astype(np.float32)
+        t0 = time.perf_counter()
+        u, perm, _ = og.process_hessian_intended(hs, "diag_h", 0.01, dtype=np.float32)
+        hd = og.damped_permuted(hs, perm, 0.01, np.float32)
+        t_f = time.perf_counter() - t0
+        w = (rng.standard_normal((sample_rows, dc)) * 0.02).astype(np.float32)
+        t0 = time.perf_counter()
+        oqn.qronos_intended(w, w, hs, gs, 3, 128, False, dtype=np.float32, factor=(u, perm, hd))
+        t_u = time.perf_counter() - t0
+        total += (t_hg * (TOKENS / sample_tokens) + t_f * (d / dc) ** 3 +
+                  t_u * (rows[grp] / sample_rows) * (d / dc) ** 2)
+    return total, (f"oracle Qronos: h and g on {sample_tokens} tokens/input "
+                   f"(x{TOKENS // sample_tokens}), factor at d={dc} (x(d/{dc})^3), update of "
+                   f"{sample_rows} rows at d={dc} (x(m/{sample_rows})(d/{dc})^2)")
+
+
+def qr_cpu_baseline(n=4096, sample_n=1024):
+    """The oracle's exact pivoted QR (the reference's eager path at panel 1,
+    the factorization the intended GPU path computes) on a ``sample_n``
+    matrix of the benchmark's construction, scaled by (n / sample_n)^3; plus
+    LAPACK sgeqp3 through scipy on the full matrix (a library reference)."""
+    import scipy.linalg as sl
+    from oracle import inputs as oin
+    from oracle import qr as oqr
+    with _all_host_threads():
+        a_s = oin.qr_matrix(1, sample_n, sample_n)
+        t0 = time.perf_counter()
+        oqr.exact_pivoted_qr(a_s, "largest")
+        t_s = time.perf_counter() - t0
+        a = oin.qr_matrix(1, n, n)
+        t0 = time.perf_counter()
+        sl.qr(a, mode="r", pivoting=True)
+        t_l = time.perf_counter() - t0
+    return {"value": t_s * (n / sample_n) ** 3 * 1e3, "unit": "ms", "cores": _cpu_cores(),
+            "kind": "port",
+            "sample": f"extrapolated from the oracle's exact QRCP of the {sample_n}^2 matrix of "
+                      f"the same construction, x(n/{sample_n})^3",
+            "lapack_sgeqp3_ms": t_l * 1e3,
+            "lapack_note": f"scipy LAPACK sgeqp3 on the full {n}^2 matrix (library, measured)"}
+
+
+def parity_sample(weights, inputs, cfg, shapes, rows=32):
+    """Sampled parity of the timed configuration, outside the timed region:
+    the first ``rows`` rows of o_proj (d = 4096) and down_proj (d = 11008)
+    against the oracle's float32 sweep with the same factor (codes equal
+    except rows whose first differing code is a rounding tie, counted), and a
+    256 x 256 tile of the d = 11008 H against a float64 sum of the same bf16
+    columns."""
+    import torch
+    from jax_gptq_b200 import layerset as LS
+    from jax_gptq_b200 import stats
+    from jax_gptq_b200.gptq_ref import factor_hessian
+    from oracle import gptq as og
+    from oracle import quant as oq
+    tie_tol = 1e-5
+    results, _ = LS.quantize_layer_gptq(weights, inputs, cfg, shapes)
+    qmin = oq.qrange(cfg.w_bits, cfg.sym)[0]
+    out = {"rows_per_linear": rows, "tie_tol": tie_tol}
+    ok = True
+    flips = 0
+    for name, grp in (("o", "attn_out"), ("down", "mlp_out")):
+        x = inputs[grp]
+        d = x.shape[1]
+        h = torch.empty((d, d), dtype=torch.float32, device="cuda")
+        stats.syrk_into(h, x, accumulate=False)
+        f = factor_hessian(h, cfg)
+        u, perm = f.u.cpu().numpy(), f.perm.cpu().numpy()
+        w = weights[name][:rows].cpu().numpy()
+        with _all_host_threads():
+            ref = og.gptq_sweep(w, u, perm, cfg.w_bits, cfg.group_size, cfg.sym, 128, np.float32,
+                                return_pre=True)
+        got = results[name].codes[:rows].cpu().numpy().astype(np.float32)[:, perm] + qmin
+        diff = got != ref["q"][:, perm]
+        bad = np.flatnonzero(diff.any(axis=1))
+        dist = 0.0
+        if bad.size:
+            first = diff[bad].argmax(axis=1)
+            pre = ref["pre"][bad, first].astype(np.float64)
+            dist = float(np.max(np.abs(pre - np.floor(pre) - 0.5)))
+        flips += int(bad.size)
+        ok &= dist <= tie_tol
+        out[name] = {"tie_flip_rows": int(bad.size), "codes_differing": int(diff.sum()),
+                     "max_first_diff_dist": dist}
+        if grp == "mlp_out":
+            xr = x[:, :256].float().cpu().numpy().astype(np.float64)
+            href = xr.T @ xr
+            hg = h[:256, :256].cpu().numpy().astype(np.float64)
+            dn = np.sqrt(np.diag(href))
+            worst = float(np.max(np.abs(hg - href) / np.outer(dn, dn)))
+            out["h_tile_worst_normalized"] = worst
+            ok &= worst <= 1e-5
+        del h, f
+    out["tie_flips"] = flips
+    out["pass"] = bool(ok)
+    return out
+
+
 # ----------------------------------------------------------------------------- distributed
 
 def _dist_init():
@@ -259,27 +474,45 @@ def _max_over_ranks(v: float, world: int) -> float:
 
 # ----------------------------------------------------------------------------- arms
 
+def _all_host_threads():
+    """A context that lets numpy's BLAS use every host core this process may
+    run on (torchrun sets OMP_NUM_THREADS=1 for its ranks)."""
+    from threadpoolctl import threadpool_limits
+    return threadpool_limits(limits=_cpu_cores())
+
+
 def run_reference(args, world, rank):
     if rank != 0:
         return
     from jax_gptq_b200.layerset import LLAMA2_7B
-    times, samples = [], None
-    for i in range(args.warmup + args.steps):
-        t, parts, samples = reference_port_sample(LLAMA2_7B, seed=i)
-        if i >= args.warmup:
-            times.append(t)
+    times, walls, samples = [], [], None
+    with _all_host_threads():
+        from threadpoolctl import threadpool_info
+        blas_threads = max([i.get("num_threads", 0) for i in threadpool_info()] or [0])
+        for i in range(args.warmup + args.steps):
+            w0 = time.perf_counter()
+            t, parts, samples = reference_port_sample(LLAMA2_7B, seed=i)
+            if i >= args.warmup:
+                times.append(t)
+                walls.append(time.perf_counter() - w0)
     v = statistics.mean(times)
     cores = _cpu_cores()
     line = {
         "impl": "reference", "metric": METRIC, "value": v, "unit": "s/layer", "n_gpus": world,
-        "steps": args.steps, "warmup": args.warmup, "ms_per_step": v * 1000.0,
+        "steps": args.steps, "warmup": args.warmup,
+        # the wall time of each timed step: the bounded sample actually run
+        "ms_per_step": statistics.mean(walls) * 1000.0,
         "higher_is_better": False, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
         "data": "synthetic", "config": {"workload": WORKLOAD, "tokens": TOKENS},
+        "value_kind": "extrapolated: each step times a bounded sample of one layer set and "
+                      "scales each part to the full layer set (see cpu_baseline.sample)",
         "cpu_baseline": {"value": v, "unit": "s/layer", "cores": cores, "kind": "port",
-                         "sample": samples, "cpu": _cpu_model()},
+                         "blas_threads": blas_threads,
+                         "sample": "extrapolated from " + samples, "cpu": _cpu_model()},
         "e2e": {"value": v, "unit": "s/layer", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
         "note": "numpy port of the reference's own CPU op sequence (JAX is not installable "
-                "offline); BLAS threads = all host cores",
+                "offline), BLAS on every host core; the value is whole-host seconds per layer "
+                "set, the same at every N (the N GPU ranks share one host)",
     }
     print(json.dumps(line), flush=True)
 
@@ -439,6 +672,7 @@ def run_ours(args, world, rank, local):
         syrk_ms.append(a.elapsed_time(b) / reps)
         syrk_flop.append(LS.syrk_flops(args.tokens, d))
         del h
+    del x
     h_tflops = sum(syrk_flop) / (sum(syrk_ms) / 1e3) / 1e12
     # roofline of the dominant launch: the largest-d H accumulation
     top = max(range(len(syrk_ms)), key=lambda i: syrk_ms[i])
@@ -456,6 +690,8 @@ def run_ours(args, world, rank, local):
                           f"on CTA pairs), d = {top_d}",
                 "achieved": top_tflops, "peak": peak, "unit": "TFLOP/s", "frac": top_tflops / peak,
                 "peak_kind": f"{peak_kind} bf16 sustained (kernel timed inside a long step)",
+                "peak_burst": peaks.get("bf16_tflops"),
+                "frac_burst": top_tflops / peaks.get("bf16_tflops", peak),
                 "algorithmic": f"tokens*d*(d+1) = {syrk_flop[top]:.4g} flops per launch",
                 "traffic": traffic,
                 "traffic_note": "dram read+write bytes per launch (ncu, scaled by tokens)"}
@@ -501,9 +737,24 @@ def run_ours(args, world, rank, local):
         LS.quantize_layer_qronos(weights, inputs, xq, qcfg, shapes, concurrent=False)
         _, qph = LS.quantize_layer_qronos(weights, inputs, xq, qcfg, shapes, timed=True)
         qronos = {"s_per_layer": q_ms / 1000.0 / world, "steps": qsteps,
+                  "workload": "Qronos 3-bit g128 act-order on the same layer set; h = Xt^T Xt, "
+                              "g = X^T Xt, Xt = X + N(0, (0.05 sigma_c)^2), seed 2 offsets",
                   "phases_ms": {"h_and_g": qph.stats_ms, "factor": qph.factor_ms,
                                 "qronos_sweeps": qph.sweep_ms}}
-        del xq
+        gx, gq_ = inputs["mlp_out"], xq["mlp_out"]
+        gd = gx.shape[1]
+        gbuf = torch.empty((gd, gd), dtype=torch.float32, device="cuda")
+        g_ms = _time(lambda: stats.gemm_tn_into(gbuf, gx, gq_, accumulate=False), 3, 1)
+        g_tf = LS.gemm_flops(args.tokens, gd) / (g_ms / 1e3) / 1e12
+        qronos["roofline"] = {
+            "bound": "tensor", "kernel": f"gq_tc gemm_tn_pair_kernel (G = X^T Xt, full 256 x 256 "
+                                         f"tiles on CTA pairs), d = {gd}",
+            "achieved": g_tf, "peak": peak, "unit": "TFLOP/s", "frac": g_tf / peak,
+            "frac_burst": g_tf / peaks.get("bf16_tflops", peak),
+            "peak_kind": f"{peak_kind} bf16 sustained",
+            "algorithmic": f"2*tokens*d^2 = {LS.gemm_flops(args.tokens, gd):.4g} flops per launch",
+            "ms": g_ms}
+        del gbuf, gx, gq_, xq
 
     # --- blocked pivoted QR (4096 x 4096 fp32, panel 64)
     qr = None
@@ -518,14 +769,31 @@ def run_ours(args, world, rank, local):
             for v in qr.values():
                 if isinstance(v, dict) and "ms" in v:
                     v["blas2_gbs"] = blas2 / (v["ms"] / 1e3) / 1e9
+            il = qr["intended_largest"]
+            qr["roofline"] = {
+                "bound": "hbm", "kernel": "gq_qrcp intended/largest: the per-pivot exposed-row "
+                                          "pass over the trailing block (BLAS-2)",
+                "achieved": il["blas2_gbs"], "peak": peaks["hbm_gbs"], "unit": "GB/s",
+                "frac": il["blas2_gbs"] / peaks["hbm_gbs"],
+                "algorithmic": "4 * sum_{i=1..n} i^2 = 91.7 GB per factorization (one trailing-"
+                               "block read per pivot step), over the whole factorization's time",
+                "note": "the 64 MB matrix stays in the 126 MB L2, so these reads come from L2; "
+                        "the pivot chain (4096 dependent steps) bounds the factorization"}
+            if rank == 0 and not args.no_cpu_baseline:
+                qr["cpu_baseline"] = qr_cpu_baseline(qr["n"])
         except Exception as exc:  # report, do not hide
             qr = {"error": repr(exc)[:200]}
 
     cpu = None
     if rank == 0 and not args.no_cpu_baseline:
-        v, sample = intended_port_sample(shapes)
+        with _all_host_threads():
+            v, sample = intended_port_sample(shapes)
+            if qronos is not None:
+                qv, qsample = qronos_port_sample(shapes)
+                qronos["cpu_baseline"] = {"value": qv, "unit": "s/layer", "cores": _cpu_cores(),
+                                          "kind": "port", "sample": "extrapolated from " + qsample}
         cpu = {"value": v, "unit": "s/layer", "cores": _cpu_cores(), "kind": "port",
-               "sample": sample, "cpu": _cpu_model()}
+               "sample": "extrapolated from " + sample, "cpu": _cpu_model()}
 
     if rank == 0:
         line = {
@@ -546,53 +814,153 @@ def run_ours(args, world, rank, local):
             "roofline": roofline, "e2e": e2e, "gpu_launches": int(launches), "clocks": clocks,
             "qronos": qronos, "qr": qr, "cpu_baseline": cpu,
         }
+        if not args.no_parity:
+            line["parity"] = parity_sample(weights, inputs, cfg, shapes)
+    del weights, inputs
+    torch.cuda.empty_cache()
+    if rank == 0 and not args.no_single and args.model == "llama2-7b":
+        line["single_linear"] = run_single_linear(peaks, cpu=not args.no_cpu_baseline)
+    # strong scaling of one layer set over all ranks (token-sharded H + row-sharded sweep)
+    if not args.no_sharded and args.model == "llama2-7b":
+        sharded = {}
+        for model in ("llama2-7b", "llama3-70b"):
+            if model == "llama3-70b" and args.no_70b:
+                continue
+            _barrier(world)
+            sharded[model] = sharded_layer_set(model, None, 2, 1, world, rank, local)
+        if rank == 0:
+            line["sharded"] = sharded
+    if rank == 0:
         print(json.dumps(line), flush=True)
 
 
-def run_sharded(args, world, rank, local):
-    """One layer set spread over all ranks (strong scaling): each rank holds a
-    1/N token shard of every input, H is summed by NCCL all-reduce, every rank
-    factors it, and each sweeps its 1/N of the rows (outputs gathered)."""
+def sharded_layer_set(model, tokens, steps, warmup, world, rank, local, check=True):
+    """One layer set spread over all ranks (strong scaling): every rank holds
+    a 1/N token shard of each input and all weights; the partial H are summed
+    by NCCL all-reduce, every rank factors the summed H, and each sweeps its
+    1/N of the rows (outputs gathered).  Returns the measured figures (rank 0)
+    or None."""
     import torch
-    from jax_gptq_b200 import _lib
+    import torch.distributed as dist
     from jax_gptq_b200 import distributed as D
     from jax_gptq_b200 import layerset as LS
+    from jax_gptq_b200 import stats
     from jax_gptq_b200.config import QuantConfig
+    from jax_gptq_b200.gptq_ref import factor_hessian, gptq_sweep
 
-    _lib.lib()
-    shapes, w_std, act_kind, args.tokens, workload = _workload(args)
+    class _A:
+        pass
+    a = _A()
+    a.model, a.tokens = model, tokens
+    shapes, w_std, act_kind, tokens, workload = _workload(a)
     dims = LS.group_dims(shapes)
     cfg = QuantConfig(w_bits=4, group_size=128, sym=False, damp_percent=0.01,
                       ordering_mode="diag_h", semantics="intended")
     weights = LS.synth_weights(shapes, w_std, 0)
-    t0, t1 = D.shard_range(args.tokens, rank, world)
+    t0, t1 = D.shard_range(tokens, rank, world)
     inputs = {grp: LS.synth_activations(t1 - t0, d, 10 + i + 100 * rank, kind=act_kind)[0]
               for i, (grp, d) in enumerate(dims.items())}
     torch.cuda.synchronize()
-    for _ in range(args.warmup):
+    for _ in range(warmup):
         D.quantize_layer_gptq_sharded(weights, inputs, cfg, shapes)
-    sampler = ClockSampler(local)
     _barrier(world)
-    sampler.start()
     e0 = torch.cuda.Event(enable_timing=True)
     e1 = torch.cuda.Event(enable_timing=True)
     e0.record()
-    for _ in range(args.steps):
+    for _ in range(steps):
         D.quantize_layer_gptq_sharded(weights, inputs, cfg, shapes)
     e1.record()
     _barrier(world)
+    ms = _max_over_ranks(e0.elapsed_time(e1) / max(steps, 1), world)
+
+    # per-phase figures from one sequential, instrumented pass (one stream)
+    phases = {}
+    factors = {}
+    for grp, x in inputs.items():
+        d = x.shape[1]
+        ev = [torch.cuda.Event(enable_timing=True) for _ in range(5)]
+        h = torch.empty((d, d), dtype=torch.float32, device="cuda")
+        _barrier(world)
+        ev[0].record()
+        stats.syrk_into(h, x, accumulate=False)
+        ev[1].record()
+        D.allreduce_sum_(h)
+        ev[2].record()
+        f = factor_hessian(h, cfg)
+        ev[3].record()
+        members = [(nm, m) for nm, m, _, g in shapes if g == grp]
+        w = D._stacked(weights, members)
+        r0, r1 = D.shard_range(w.shape[0], rank, world, D.SWEEP_ROW_ALIGN)
+        res = gptq_sweep(w[r0:r1], f.u, f.perm, cfg)
+        ev[4].record()
+        torch.cuda.synchronize()
+        t = [ev[i].elapsed_time(ev[i + 1]) for i in range(4)]
+        t = [_max_over_ranks(v, world) for v in t]
+        ar_bytes = 4 * d * d
+        # NCCL's bus-bandwidth convention for all-reduce: 2 (N - 1) / N of the buffer per rank
+        bus = ar_bytes * 2 * (world - 1) / world / (t[1] / 1e3) / 1e9 if world > 1 else None
+        phases[grp] = {"d": d, "rows_per_rank": r1 - r0, "h_partial_ms": t[0],
+                       "allreduce_ms": t[1], "allreduce_bytes": ar_bytes,
+                       "allreduce_busbw_gbs": bus, "factor_ms": t[2], "sweep_ms": t[3]}
+        factors[grp] = (h, f, res, (r0, r1), w)
+
+    parity = None
+    if check:
+        # (1) all-reduced H against the ranks' partial tiles summed in rank order
+        grp0 = min(dims, key=lambda g: dims[g])
+        h, f, res, (r0, r1), w = factors[grp0]
+        x = inputs[grp0]
+        tile = torch.empty((256, 256), dtype=torch.float32, device="cuda")
+        stats.syrk_into(tile, x[:, :256].contiguous(), accumulate=False)
+        parts = [torch.empty_like(tile) for _ in range(world)]
+        if world > 1:
+            dist.all_gather(parts, tile)
+        else:
+            parts = [tile]
+        ref = sum(p.double() for p in parts)
+        got = h[:256, :256].double()
+        h_rel = float((got - ref).abs().max() / ref.abs().max())
+        # (2) this rank's row shard against the unsharded sweep (same U): bit-exact
+        whole = gptq_sweep(w, f.u, f.perm, cfg)
+        rows_equal = bool(torch.equal(whole.codes[r0:r1], res.codes) and
+                          torch.equal(whole.dequant[r0:r1], res.dequant))
+        flags = torch.tensor([0.0 if rows_equal else 1.0, h_rel], dtype=torch.float64,
+                             device="cuda")
+        if world > 1:
+            dist.all_reduce(flags, op=dist.ReduceOp.MAX)
+        parity = {"group": grp0, "h_tile_max_rel_vs_rank_sum": float(flags[1].item()),
+                  "row_shards_bitexact_vs_unsharded": bool(flags[0].item() == 0.0),
+                  "pass": bool(flags[0].item() == 0.0 and flags[1].item() <= 1e-6)}
+    del factors, inputs, weights
+    torch.cuda.empty_cache()
+    if rank != 0:
+        return None
+    top = max(phases, key=lambda g: phases[g]["d"])
+    return {"workload": workload, "tokens": tokens, "n_gpus": world, "s_per_layer": ms / 1e3,
+            "steps": steps, "warmup": warmup, "per_group": phases,
+            "replicated_factor_ms": sum(p["factor_ms"] for p in phases.values()),
+            "limiter": f"the replicated factor of the d = {phases[top]['d']} group "
+                       f"({phases[top]['factor_ms']:.1f} ms, not sharded) and its "
+                       f"{phases[top]['allreduce_bytes'] / 1e9:.2f} GB all-reduce",
+            "parity": parity}
+
+
+def run_sharded(args, world, rank, local):
+    """``--strategy sharded``: one layer set over all ranks, as the headline line."""
+    sampler = ClockSampler(local)
+    sampler.start()
+    r = sharded_layer_set(args.model, args.tokens, args.steps, args.warmup, world, rank, local)
     clocks = sampler.stop()
-    ms = _max_over_ranks(e0.elapsed_time(e1) / args.steps, world)
     if rank == 0:
         print(json.dumps({
-            "metric": METRIC, "value": ms / 1000.0, "unit": "s/layer", "n_gpus": world,
-            "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
+            "metric": METRIC, "value": r["s_per_layer"], "unit": "s/layer", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": r["s_per_layer"] * 1e3,
             "higher_is_better": False, "scaling": "strong", "vs_baseline": None, "dtype": "f32",
             "data": "synthetic (seeded, on device)",
-            "config": {"workload": workload, "tokens": args.tokens,
+            "config": {"workload": r["workload"], "tokens": r["tokens"],
                        "parallelism": f"token-sharded H (NCCL all-reduce) + row-sharded sweep x{world}",
                        "l2_flush": "inputs larger than L2"},
-            "clocks": clocks}), flush=True)
+            "sharded": r, "clocks": clocks}), flush=True)
 
 
 def main():
@@ -610,6 +978,12 @@ def main():
     ap.add_argument("--no-qronos", action="store_true")
     ap.add_argument("--no-qr", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-parity", action="store_true", help="skip the sampled parity check")
+    ap.add_argument("--no-single", action="store_true", help="skip the single-linear workload")
+    ap.add_argument("--no-sharded", action="store_true",
+                    help="skip the strong-scaling (token/row-sharded) layer-set runs")
+    ap.add_argument("--no-70b", action="store_true",
+                    help="skip the 70B block in the strong-scaling runs")
     ap.add_argument("--syrk-traffic", type=float, default=None,
                     help="DRAM bytes per H-accumulation launch from an ncu capture")
     ap.add_argument("--only", choices=["all", "syrk", "qr", "gemm", "factor", "sweep"],

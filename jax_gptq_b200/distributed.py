@@ -237,8 +237,14 @@ def _members(shapes, grp):
     return [(name, m) for name, m, _, g in shapes if g == grp]
 
 
+def _stacked(weights: dict, members) -> torch.Tensor:
+    return weights[members[0][0]] if len(members) == 1 else \
+        torch.cat([weights[name] for name, _ in members], dim=0)
+
+
 def quantize_layer_gptq_sharded(weights: dict, inputs_local: dict, cfg: QuantConfig, shapes,
-                                group=None, gather: bool = True) -> dict[str, SweepResult]:
+                                group=None, gather: bool = True,
+                                concurrent: bool = True) -> dict[str, SweepResult]:
     """GPTQ for one layer set spread over the ranks of ``group``.
 
     ``inputs_local[grp]``: this rank's token shard of the group's activations.
@@ -246,21 +252,66 @@ def quantize_layer_gptq_sharded(weights: dict, inputs_local: dict, cfg: QuantCon
     its ``shard_range`` rows of the group's row-stacked linears).  With
     ``gather`` every rank returns whole results keyed by linear name;
     otherwise results are keyed by input group and hold this rank's rows of
-    the group's row-stacked matrix."""
+    the group's row-stacked matrix.
+
+    With ``concurrent`` the groups run as chains, largest first (the
+    layer-set schedule of ``layerset.quantize_layer_gptq``): a group's
+    partial H is formed on the current stream and its all-reduce issued
+    asynchronously; the group's factor and row-shard sweep then run on a side
+    stream that waits for that all-reduce, while the current stream goes on
+    to the next group's partial H.  The factor's first damping attempt reads
+    no status on the host; a group that needed more damping is redone at the
+    end.  The results equal the sequential order bit for bit."""
     rank, world = rank_world(group)
-    hs = hessians_token_sharded(inputs_local, group)
     out: dict[str, SweepResult] = {}
-    for grp, h in hs.items():
-        f = factor_hessian(h, cfg)
+    if concurrent:
+        from . import layerset as LS
+        from .gptq_ref import factor_hessian_attempt0
+        works: dict = {}
+
+        def form(grp, chunk):
+            x = inputs_local[grp]
+            d = x.shape[1]
+            h = torch.empty((d, d), dtype=torch.float32, device=x.device)
+            stats.syrk_into(h, x, accumulate=False, token_chunk=chunk)
+            works[grp] = allreduce_sum_(h, group, async_op=True)
+            return h
+
+        def prepare(grp, h):
+            if works.get(grp) is not None:
+                works[grp].wait()  # the side stream (current here) waits for the all-reduce
+            return factor_hessian_attempt0(h, cfg)
+
+        def rows(grp):
+            w = _stacked(weights, _members(shapes, grp))
+            r0, r1 = shard_range(w.shape[0], rank, world, SWEEP_ROW_ALIGN)
+            return w[r0:r1]
+
+        def work(grp, state):
+            f, status = state
+            return status, gptq_sweep(rows(grp), f.u, f.perm, cfg)
+
+        def redo(grp, h):
+            f = factor_hessian(h, cfg)
+            return gptq_sweep(rows(grp), f.u, f.perm, cfg)
+
+        sizes = LS._chain_sizes(inputs_local, shapes)
+        local = LS._run_groups_concurrently(sizes, form, work, redo, prepare)
+        items = [(grp, local[grp]) for grp in inputs_local]
+    else:
+        hs = hessians_token_sharded(inputs_local, group)
+        items = []
+        for grp, h in hs.items():
+            f = factor_hessian(h, cfg)
+            w = _stacked(weights, _members(shapes, grp))
+            r0, r1 = shard_range(w.shape[0], rank, world, SWEEP_ROW_ALIGN)
+            items.append((grp, gptq_sweep(w[r0:r1], f.u, f.perm, cfg)))
+    for grp, res in items:
         members = _members(shapes, grp)
-        w = weights[members[0][0]] if len(members) == 1 else \
-            torch.cat([weights[name] for name, _ in members], dim=0)
-        m = w.shape[0]
-        r0, r1 = shard_range(m, rank, world, SWEEP_ROW_ALIGN)
-        res = gptq_sweep(w[r0:r1], f.u, f.perm, cfg)
         if not gather:
             out[grp] = res
             continue
+        m = sum(mi for _, mi in members)
         deq = gather_rows(res.dequant, m, group)
         codes = gather_rows(res.codes, m, group)
         scales = gather_rows(res.scales, m, group)

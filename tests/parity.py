@@ -12,7 +12,7 @@ not checked.
 ``TIE_TOL`` is the largest distance from the half step (in units of one
 quantization step) that is accepted as a tie: 1e-5, about ten float32 ulps
 of a 4-bit code value (ulp(8) = 9.5e-7).  Measured on B200, the first
-differing codes of the benchmark-size sweeps sat 1e-6 to 4e-6 from the half
+differing codes of the sweep and Qronos tests sat 0 to 6.2e-6 from the half
 step.
 """
 
