@@ -399,7 +399,7 @@ def parity_sample(weights, inputs, cfg, shapes, rows=32):
     out = {"rows_per_linear": rows, "tie_tol": tie_tol}
     ok = True
     flips = 0
-    for name, grp in (("o", "attn_out"), ("down", "mlp_out")):
+    for name, grp in (("o_proj", "attn_out"), ("down_proj", "mlp_out")):
         x = inputs[grp]
         d = x.shape[1]
         h = torch.empty((d, d), dtype=torch.float32, device="cuda")
