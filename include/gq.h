@@ -346,6 +346,24 @@ int gq_unpack_dequant(const uint32_t* packed, int64_t m, int64_t n, int64_t ldp,
                       const int32_t* g_idx, float* dequant, uint8_t* codes, void* stream);
 
 /* ------------------------------------------------------------------------
+ * eval.py:9-22 _masked_nll_from_logits: the next-token negative
+ * log-likelihood summed over scored positions, for perplexity evaluation.
+ *
+ * logits  [batch, tokens, vocab] contiguous, dtype 0 = float32, 1 = bf16.
+ * labels  [batch, tokens] int64; position t of entry b is scored against
+ *         labels[b, t + 1] unless that label is -100 (then skipped); labels
+ *         outside [0, vocab) are clamped to the range.
+ * nll_sum (device double) = sum of logsumexp(logits[b, t]) - logits[b, t,
+ *         label]; count (device int64) = number of scored positions.
+ * Deterministic (fixed-order reduction).  Workspace from
+ * gq_masked_nll_workspace_size(batch, tokens), 256-byte aligned.
+ */
+int64_t gq_masked_nll_workspace_size(int64_t batch, int64_t tokens);
+int gq_masked_nll(const void* logits, int dtype, int64_t batch, int64_t tokens, int64_t vocab,
+                  const int64_t* labels, double* nll_sum, int64_t* count, void* workspace,
+                  int64_t workspace_bytes, void* stream);
+
+/* ------------------------------------------------------------------------
  * Multi-GPU: a per-device handle with an optional NCCL communicator and the
  * in-place fp32 sum all-reduce used for token-sharded Hessians (H = sum over
  * ranks of X_r^T X_r).  The reference is single-device and has no

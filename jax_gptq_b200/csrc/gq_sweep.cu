@@ -9,8 +9,12 @@
 //
 // The lazy updates are two-level: blocks of 128 columns inside super-blocks
 // of 512.  Per block [b0, b1) of super-block [s0, s1):
-//   1. the band U[b0:b1, b0:s1] is transposed into ubt (column j of the band
-//      is a contiguous 128-float row);
+//   0. (once per super-block) U[s0:s1, s0:n] is transposed into ubt, so
+//      column j of U's super-block rows is one contiguous run of <= 512
+//      floats; the band of every block and both GEMMs' U operands are views
+//      of it;
+//   1. the block's own 128 x 128 band U[b0:b1, b0:b1] is staged in shared
+//      memory (cp.async) by the block-step kernel;
 //   2. the block step, one lane per weight row: the lane quantizes its row's
 //      columns one by one (32-column sub-blocks in registers, the rest of the
 //      block in a shared-memory row buffer) and writes codes, dequantized
@@ -92,7 +96,8 @@ struct SweepArgs {
   uint8_t* cp;          // [m, ldp]
   float* err;           // [m, ld_err]: this block's scaled errors
   int64_t ld_err;
-  const float* ubt;     // [s1 - b0, 128]: ubt[j][i] = U[b0 + i][b0 + j]
+  const float* ubt;     // band: ubt[j * ldub + i] = U[b0 + i][b0 + j]
+  int64_t ldub;
   int64_t m, n, ldp;
   int64_t b0;           // first column of this block
   int bw;               // block width (<= 128)
@@ -148,9 +153,22 @@ __device__ __forceinline__ void sweep_group_params(const SweepArgs& a, int64_t r
 constexpr int SR_THREADS = 128;
 constexpr int SR_CP = 2 * SW_SUB + 4;  // pitch of the critical U tile (up to 64 columns)
 
+// The block's band U[b0:b1, b0:b1], staged in dynamic shared memory:
+// us[j * SW_BLOCK + i] = U[b0 + i][b0 + j] for i <= j (the zero triangle is
+// not copied and never read).
+constexpr size_t SR_BAND_BYTES = (size_t)SW_BLOCK * SW_BLOCK * 4;  // 64 KB
+
+__device__ __forceinline__ void cp_async16(void* smem_dst, const void* gmem_src) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(
+                   (uint32_t)__cvta_generic_to_shared(smem_dst)),
+               "l"(gmem_src)
+               : "memory");
+}
+
 template <int G>
 __global__ void __launch_bounds__(SR_THREADS) sweep_rows_kernel(SweepArgs a) {
   constexpr int GD = (G > 0) ? G : 1;  // divisor-safe group size for the G = 0 instance
+  extern __shared__ __align__(16) float us[];             // the band, see SR_BAND_BYTES
   __shared__ float ws[SW_BLOCK * SW_WP];                  // ws[j][lane]: column j of the rows
   __shared__ __align__(16) float tile[2][SW_SUB * SW_TP];  // U inside sub-block s, [k][t]
   __shared__ __align__(16) float ucrit[SW_SUB * SR_CP];    // U rows of sub-block s, critical columns
@@ -159,7 +177,6 @@ __global__ void __launch_bounds__(SR_THREADS) sweep_rows_kernel(SweepArgs a) {
   __shared__ uint32_t cs[2][(SW_SUB / 4) * 32];           // packed codes of sub-block s
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int bw = a.bw;
-  const float* __restrict__ ubt = a.ubt;  // ubt[j][i] = U[b0 + i][b0 + j]
   const int64_t row = (int64_t)blockIdx.x * 32 + lane;
   const bool valid = row < a.m;
   float* wrow = valid ? a.wp + row * a.ldp + a.b0 : nullptr;
@@ -179,7 +196,7 @@ __global__ void __launch_bounds__(SR_THREADS) sweep_rows_kernel(SweepArgs a) {
     for (int e = t0; e < SW_SUB * (SW_SUB / 4); e += nt) {
       const int t = e / (SW_SUB / 4), q = e % (SW_SUB / 4);
       float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
-      if (c0 + t < bw) v = __ldg(reinterpret_cast<const float4*>(ubt + (int64_t)(c0 + t) * SW_BLOCK + c0) + q);
+      if (c0 + t < bw) v = *(reinterpret_cast<const float4*>(us + (c0 + t) * SW_BLOCK + c0) + q);
       float* dst = &tile[s & 1][(4 * q) * SW_TP + t];
       dst[0] = v.x;
       dst[SW_TP] = v.y;
@@ -192,7 +209,7 @@ __global__ void __launch_bounds__(SR_THREADS) sweep_rows_kernel(SweepArgs a) {
     const int c0 = SW_SUB * s, c1 = c0 + SW_SUB, wdt = crit_width(s);
     for (int e = t0; e < wdt * (SW_SUB / 4); e += nt) {
       const int t = e / (SW_SUB / 4), q = e % (SW_SUB / 4);
-      const float4 v = __ldg(reinterpret_cast<const float4*>(ubt + (int64_t)(c1 + t) * SW_BLOCK + c0) + q);
+      const float4 v = *(reinterpret_cast<const float4*>(us + (c1 + t) * SW_BLOCK + c0) + q);
       float* dst = &ucrit[(4 * q) * SR_CP + t];
       dst[0] = v.x;
       dst[SR_CP] = v.y;
@@ -200,19 +217,35 @@ __global__ void __launch_bounds__(SR_THREADS) sweep_rows_kernel(SweepArgs a) {
       dst[3 * SR_CP] = v.w;
     }
   };
-  // column j -= sum_k ev[k] U[b0 + c0 + k][b0 + j], k increasing (U from global, broadcast)
-  auto update_from_global = [&](const float (&ev)[SW_SUB], int c0, int j) {
-    const float4* u4 = reinterpret_cast<const float4*>(ubt + (int64_t)j * SW_BLOCK + c0);
-    float v = ws[j * SW_WP + lane];
+  // column j -= sum_k ev[k] U[b0 + c0 + k][b0 + j], k increasing (U broadcast from the band)
+  // columns j0, j0 + dj, ... (nj <= 4 of them) -= sum_k ev[k] U[b0 + c0 + k][b0 + j],
+  // k increasing, U broadcast from the band: independent chains side by side
+  // (each column still adds its 32 terms in increasing k), so the FMA latency
+  // of one chain hides behind the others
+  auto update_cols_from_band = [&](const float (&ev)[SW_SUB], int c0, int j0, int dj, int nj) {
+    constexpr int NJ = 4;
+    float v[NJ];
+    const float4* u4[NJ];
+#pragma unroll
+    for (int c = 0; c < NJ; ++c) {
+      const int j = (c < nj) ? j0 + c * dj : j0;
+      u4[c] = reinterpret_cast<const float4*>(us + j * SW_BLOCK + c0);
+      v[c] = ws[j * SW_WP + lane];
+    }
 #pragma unroll
     for (int kc = 0; kc < SW_SUB / 4; ++kc) {
-      const float4 u = __ldg(u4 + kc);
-      v = fmaf(-ev[4 * kc + 0], u.x, v);
-      v = fmaf(-ev[4 * kc + 1], u.y, v);
-      v = fmaf(-ev[4 * kc + 2], u.z, v);
-      v = fmaf(-ev[4 * kc + 3], u.w, v);
+#pragma unroll
+      for (int c = 0; c < NJ; ++c) {
+        const float4 u = u4[c][kc];
+        v[c] = fmaf(-ev[4 * kc + 0], u.x, v[c]);
+        v[c] = fmaf(-ev[4 * kc + 1], u.y, v[c]);
+        v[c] = fmaf(-ev[4 * kc + 2], u.z, v[c]);
+        v[c] = fmaf(-ev[4 * kc + 3], u.w, v[c]);
+      }
     }
-    ws[j * SW_WP + lane] = v;
+#pragma unroll
+    for (int c = 0; c < NJ; ++c)
+      if (c < nj) ws[(j0 + c * dj) * SW_WP + lane] = v[c];
   };
   // sub-block s's results to global memory (dequantized values, errors, codes)
   auto store_sub = [&](int s, int t0, int nt) {
@@ -244,9 +277,13 @@ __global__ void __launch_bounds__(SR_THREADS) sweep_rows_kernel(SweepArgs a) {
     }
   };
 
-  // ---- prologue (all warps): the row block, reciprocal pivots, the first tiles
-  for (int i = threadIdx.x; i < SW_BLOCK; i += SR_THREADS)
-    rinv[i] = (i < bw) ? 1.f / ubt[(int64_t)i * SW_BLOCK + i] : 0.f;
+  // ---- prologue (all warps): the band (asynchronously), the row block,
+  // reciprocal pivots, the first tiles
+  for (int c = threadIdx.x; c < bw * (SW_BLOCK / 4); c += SR_THREADS) {
+    const int j = c / (SW_BLOCK / 4), q = c % (SW_BLOCK / 4);
+    if (4 * q <= j) cp_async16(us + j * SW_BLOCK + 4 * q, a.ubt + (int64_t)j * a.ldub + 4 * q);
+  }
+  asm volatile("cp.async.commit_group;" ::: "memory");
   if (valid) {
     // warp w loads columns [32 w, 32 w + 32): eight float4 loads in flight per lane
     float4 v[SW_SUB / 4];
@@ -267,6 +304,10 @@ __global__ void __launch_bounds__(SR_THREADS) sweep_rows_kernel(SweepArgs a) {
 #pragma unroll
     for (int k = 0; k < SW_SUB; ++k) ws[(SW_SUB * warp + k) * SW_WP + lane] = 0.f;
   }
+  asm volatile("cp.async.wait_group 0;" ::: "memory");
+  __syncthreads();
+  for (int i = threadIdx.x; i < SW_BLOCK; i += SR_THREADS)
+    rinv[i] = (i < bw) ? 1.f / us[i * SW_BLOCK + i] : 0.f;
   stage_tile(0, threadIdx.x, SR_THREADS);
   float scale = 1.f, zero = 0.f;  // warp 0: the current group's parameters
   if (G == 0 && valid) {
@@ -354,8 +395,9 @@ __global__ void __launch_bounds__(SR_THREADS) sweep_rows_kernel(SweepArgs a) {
         float ev[SW_SUB];
 #pragma unroll
         for (int k = 0; k < SW_SUB; ++k) ev[k] = es[(s - 1) & 1][k * SW_WP + lane];
-        for (int j = SW_SUB * s + w_prev + lw; j < bw; j += SR_THREADS / 32 - 1)
-          update_from_global(ev, SW_SUB * (s - 1), j);
+        constexpr int LW = SR_THREADS / 32 - 1;  // look-ahead warps
+        for (int j = SW_SUB * s + w_prev + lw; j < bw; j += 4 * LW)
+          update_cols_from_band(ev, SW_SUB * (s - 1), j, LW, min(4, (bw - j + LW - 1) / LW));
         store_sub(s - 1, lw, SR_THREADS / 32 - 1);
       }
       if (s + 1 < nsub) stage_tile(s + 1, lt, SR_THREADS - 32);
@@ -368,12 +410,22 @@ __global__ void __launch_bounds__(SR_THREADS) sweep_rows_kernel(SweepArgs a) {
       float ev[SW_SUB];
 #pragma unroll
       for (int k = 0; k < SW_SUB; ++k) ev[k] = es[s & 1][k * SW_WP + lane];
-      for (int t = warp; t < wc; t += SR_THREADS / 32) {
-        const int j = c0 + SW_SUB + t;
-        float v = ws[j * SW_WP + lane];
+      constexpr int NW = SR_THREADS / 32;
+      // columns t, t + NW, t + 2 NW, t + 3 NW together: four independent chains
+      for (int t = warp; t < wc; t += 4 * NW) {
+        float v[4];
 #pragma unroll
-        for (int k = 0; k < SW_SUB; ++k) v = fmaf(-ev[k], ucrit[k * SR_CP + t], v);
-        ws[j * SW_WP + lane] = v;
+        for (int c = 0; c < 4; ++c)
+          v[c] = (t + c * NW < wc) ? ws[(c0 + SW_SUB + t + c * NW) * SW_WP + lane] : 0.f;
+#pragma unroll
+        for (int k = 0; k < SW_SUB; ++k) {
+#pragma unroll
+          for (int c = 0; c < 4; ++c)
+            v[c] = fmaf(-ev[k], ucrit[k * SR_CP + min(t + c * NW, wc - 1)], v[c]);
+        }
+#pragma unroll
+        for (int c = 0; c < 4; ++c)
+          if (t + c * NW < wc) ws[(c0 + SW_SUB + t + c * NW) * SW_WP + lane] = v[c];
       }
     }
     __syncthreads();
@@ -403,7 +455,7 @@ __global__ void __launch_bounds__(32) sweep_rows1_kernel(SweepArgs a) {
   const int bw = a.bw;
   const float* __restrict__ ubt = a.ubt;
   for (int i = lane; i < SW_BLOCK; i += 32)
-    rinv[i] = (i < bw) ? 1.f / ubt[(int64_t)i * SW_BLOCK + i] : 0.f;
+    rinv[i] = (i < bw) ? 1.f / ubt[(int64_t)i * a.ldub + i] : 0.f;
   const int64_t row = (int64_t)blockIdx.x * 32 + lane;
   const bool valid = row < a.m;
   float* wrow = valid ? a.wp + row * a.ldp + a.b0 : nullptr;
@@ -440,7 +492,7 @@ __global__ void __launch_bounds__(32) sweep_rows1_kernel(SweepArgs a) {
     const int trail = bw - c0 - SW_SUB;
     for (int ch = lane; ch < trail * (SW_SUB / 4); ch += 32) {
       const int r = ch / (SW_SUB / 4), part = ch % (SW_SUB / 4);
-      const float* src = ubt + (int64_t)(c0 + SW_SUB + r) * SW_BLOCK + c0 + 4 * part;
+      const float* src = ubt + (int64_t)(c0 + SW_SUB + r) * a.ldub + c0 + 4 * part;
       asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(
                        (uint32_t)__cvta_generic_to_shared(stg + r * SW_SUB + 4 * part)),
                    "l"(src)
@@ -449,7 +501,7 @@ __global__ void __launch_bounds__(32) sweep_rows1_kernel(SweepArgs a) {
     asm volatile("cp.async.commit_group;" ::: "memory");
     // tile[k][t] = U[b0 + c0 + k][b0 + c0 + t]  (lane t copies its row of the band)
     if (c0 + lane < bw) {
-      const float4* src = reinterpret_cast<const float4*>(ubt + (int64_t)(c0 + lane) * SW_BLOCK + c0);
+      const float4* src = reinterpret_cast<const float4*>(ubt + (int64_t)(c0 + lane) * a.ldub + c0);
 #pragma unroll
       for (int q = 0; q < SW_SUB / 4; ++q) {
         const float4 v = __ldg(src + q);
@@ -639,6 +691,34 @@ int sweep_shape_ok(const char* who, int64_t m, int64_t n) {
 int transpose2d(const float* src, int64_t rows, int64_t cols, int64_t lds, float* dst, int64_t ldd,
                 cudaStream_t st);
 
+// The four-warp block step takes its band in dynamic shared memory above the
+// default 48 KB; allow it once per (device, instance).
+template <int G>
+static int allow_band_smem() {
+  static int done_dev = -1;
+  int dev = 0;
+  GQ_CHECK_CUDA(cudaGetDevice(&dev));
+  if (done_dev != dev) {
+    GQ_CHECK_CUDA(cudaFuncSetAttribute(sweep_rows_kernel<G>,
+                                       cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       (int)SR_BAND_BYTES));
+    done_dev = dev;
+  }
+  return GQ_OK;
+}
+
+int sweep_rows_smem_setup(int group_size) {
+  switch (group_size) {
+    case 4: return allow_band_smem<4>();
+    case 8: return allow_band_smem<8>();
+    case 16: return allow_band_smem<16>();
+    case 32: return allow_band_smem<32>();
+    case 64: return allow_band_smem<64>();
+    case 128: return allow_band_smem<128>();
+    default: return allow_band_smem<0>();
+  }
+}
+
 }  // namespace gq
 
 extern "C" {
@@ -698,7 +778,7 @@ int gq_gptq_sweep(const float* w, int64_t m, int64_t n, int64_t ldw, const float
   }
 
   SweepArgs a;
-  a.wp = wp; a.cp = cp; a.ubt = ubt;
+  a.wp = wp; a.cp = cp; a.ubt = ubt; a.ldub = super_w;
   a.ld_err = super_w;
   a.m = m; a.n = n; a.ldp = ldp;
   a.n_groups = (int)(n / group_size);
@@ -713,6 +793,7 @@ int gq_gptq_sweep(const float* w, int64_t m, int64_t n, int64_t ldw, const float
   GQ_CHECK_CUDA(cudaGetDevice(&dev));
   GQ_CHECK_CUDA(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
   const bool four_warps = grid <= (unsigned)(4 * sms);
+  if (four_warps) GQ_TRY(sweep_rows_smem_setup(group_size));
   for (int64_t b0 = 0; b0 < n; b0 += SW_BLOCK) {
     const int bw = (int)std::min<int64_t>(SW_BLOCK, n - b0);
     if (group_size > SW_BLOCK && b0 % group_size == 0) {
@@ -737,19 +818,23 @@ int gq_gptq_sweep(const float* w, int64_t m, int64_t n, int64_t ldw, const float
     a.b0 = b0;
     a.bw = bw;
     a.err = err + (b0 - s0);
-    // U[b0:b1, b0:s1] transposed: the sweep reads the block's rows of U as
-    // contiguous runs, and the near GEMM gets both operands K-major
-    // (tensor-core path)
-    GQ_TRY(transpose2d(u + b0 * ldu + b0, bw, s1 - b0, ldu, ubt, SW_BLOCK, st));
+    if (b0 == s0) {
+      // U[s0:s1, s0:n] transposed: the block steps read U's super-block rows
+      // as contiguous runs, and both GEMMs get their U operand K-major
+      // (tensor-core path)
+      GQ_TRY(transpose2d(u + s0 * ldu + s0, s1 - s0, n - s0, ldu, ubt, super_w, st));
+    }
+    a.ubt = ubt + (b0 - s0) * super_w + (b0 - s0);
     if (four_warps) {
+      const size_t band = SR_BAND_BYTES;
       switch (group_size) {
-        case 4: sweep_rows_kernel<4><<<grid, SR_THREADS, 0, st>>>(a); break;
-        case 8: sweep_rows_kernel<8><<<grid, SR_THREADS, 0, st>>>(a); break;
-        case 16: sweep_rows_kernel<16><<<grid, SR_THREADS, 0, st>>>(a); break;
-        case 32: sweep_rows_kernel<32><<<grid, SR_THREADS, 0, st>>>(a); break;
-        case 64: sweep_rows_kernel<64><<<grid, SR_THREADS, 0, st>>>(a); break;
-        case 128: sweep_rows_kernel<128><<<grid, SR_THREADS, 0, st>>>(a); break;
-        default: sweep_rows_kernel<0><<<grid, SR_THREADS, 0, st>>>(a); break;
+        case 4: sweep_rows_kernel<4><<<grid, SR_THREADS, band, st>>>(a); break;
+        case 8: sweep_rows_kernel<8><<<grid, SR_THREADS, band, st>>>(a); break;
+        case 16: sweep_rows_kernel<16><<<grid, SR_THREADS, band, st>>>(a); break;
+        case 32: sweep_rows_kernel<32><<<grid, SR_THREADS, band, st>>>(a); break;
+        case 64: sweep_rows_kernel<64><<<grid, SR_THREADS, band, st>>>(a); break;
+        case 128: sweep_rows_kernel<128><<<grid, SR_THREADS, band, st>>>(a); break;
+        default: sweep_rows_kernel<0><<<grid, SR_THREADS, band, st>>>(a); break;
       }
     } else {
       switch (group_size) {
@@ -766,14 +851,13 @@ int gq_gptq_sweep(const float* w, int64_t m, int64_t n, int64_t ldw, const float
     const int64_t b1 = b0 + bw;
     if (b1 < s1) {
       // near: wp[:, b1:s1] -= err_block @ U[b0:b1, b1:s1]
-      GQ_TRY(sgemm(0, 1, m, s1 - b1, bw, -1.f, a.err, super_w, ubt + (int64_t)bw * SW_BLOCK,
-                   SW_BLOCK, 1.f, wp + b1, ldp, 0, st));
+      GQ_TRY(sgemm(0, 1, m, s1 - b1, bw, -1.f, a.err, super_w, a.ubt + (int64_t)bw * super_w,
+                   super_w, 1.f, wp + b1, ldp, 0, st));
     }
     if (b1 == s1 && s1 < n) {
       // far: wp[:, s1:] -= err @ U[s0:s1, s1:]
-      GQ_TRY(transpose2d(u + s0 * ldu + s1, s1 - s0, n - s1, ldu, ubt, super_w, st));
-      GQ_TRY(sgemm(0, 1, m, n - s1, s1 - s0, -1.f, err, super_w, ubt, super_w, 1.f, wp + s1, ldp,
-                   0, st));
+      GQ_TRY(sgemm(0, 1, m, n - s1, s1 - s0, -1.f, err, super_w, ubt + (s1 - s0) * super_w,
+                   super_w, 1.f, wp + s1, ldp, 0, st));
     }
   }
   if (dequant || codes) {

@@ -234,6 +234,40 @@ def quantize_stack(blocks: list[DecoderBlock], calib: list[torch.Tensor], cfg: Q
     return reports
 
 
+class TinyLM(torch.nn.Module):
+    """Token embedding -> decoder blocks -> RMSNorm -> LM head: a small
+    language model around a block stack, for perplexity checks of a
+    quantized stack (eval.py's role in the reference).  ``hidden(ids)`` is
+    the blocks' input (the calibration batches of :func:`quantize_stack`);
+    ``forward(ids)`` returns [B, T, vocab] logits."""
+
+    def __init__(self, blocks, vocab: int, cfg: BlockConfig, seed: int = 0,
+                 head_std: float | None = None, dtype=torch.bfloat16):
+        super().__init__()
+        gen = torch.Generator(device="cpu").manual_seed(seed)
+        self.embed = torch.nn.Embedding(vocab, cfg.hidden)
+        self.blocks = torch.nn.ModuleList(blocks)
+        self.norm = RMSNorm(cfg.hidden, cfg.eps)
+        self.lm_head = torch.nn.Linear(cfg.hidden, vocab, bias=False)
+        std = head_std if head_std is not None else 4.0 / cfg.hidden ** 0.5
+        with torch.no_grad():
+            self.embed.weight.copy_(torch.randn(self.embed.weight.shape, generator=gen))
+            self.lm_head.weight.copy_(torch.randn(self.lm_head.weight.shape, generator=gen) * std)
+        self.embed.to(device="cuda", dtype=dtype)
+        self.norm.to(device="cuda", dtype=dtype)
+        self.lm_head.to(device="cuda", dtype=dtype)
+        self.eval()
+
+    def hidden(self, ids: torch.Tensor) -> torch.Tensor:
+        return self.embed(ids)
+
+    def forward(self, ids: torch.Tensor) -> torch.Tensor:
+        x = self.embed(ids)
+        for blk in self.blocks:
+            x = blk(x)
+        return self.lm_head(self.norm(x))
+
+
 def stack_forward(blocks, batches):
     with torch.no_grad():
         out = []

@@ -67,3 +67,48 @@ def test_qronos_stack_walk():
     assert _rel(pipeline.stack_forward(blocks, calib), ref) < 0.5
     with pytest.raises(ValueError):
         pipeline.quantize_stack(blocks, calib, cfg, method="awq")
+
+
+def test_walk_first_block_matches_the_oracle(tmp_path):
+    """The layer walk's q/k/v (first block, group attn_in) against the oracle:
+    the H the walk accumulates from the captured bf16 activations, factored
+    the same way, gives codes equal to the float32 oracle sweep up to
+    rounding ties (the walk's packed codes, unpacked), and the walk's
+    reconstruction error is within 1e-3 relative of the float64 oracle's."""
+    import numpy as np
+    from jax_gptq_b200 import stats
+    from jax_gptq_b200.gptq_ref import factor_hessian
+    from oracle import gptq as og
+    from oracle import quant as oq
+    from parity import TIE_TOL, code_diffs, report
+
+    calib = _calib(5)
+    blocks = pipeline.synth_stack(1, CFG, seed=4)
+    w_orig = torch.cat([getattr(blocks[0], n).weight.float() for n in ("q_proj", "k_proj", "v_proj")])
+    with torch.no_grad():
+        xs = [blocks[0].input_layernorm(b).reshape(-1, CFG.hidden) for b in calib]
+    cfg = QuantConfig(w_bits=4, group_size=128, ordering_mode="diag_h", semantics="intended")
+    pipeline.quantize_stack(blocks, calib, cfg, checkpoint_dir=str(tmp_path))
+    packed = packing.load_layer(str(tmp_path / "layer0.pt"), "cuda")
+    codes = torch.cat([packing.unpack_codes(packed[n]) for n in ("q_proj", "k_proj", "v_proj")])
+    deq = torch.cat([packing.dequantize(packed[n]) for n in ("q_proj", "k_proj", "v_proj")])
+
+    acc = stats.HessianAccumulator(CFG.hidden)
+    for x in xs:
+        acc.add(x)
+    f = factor_hessian(acc.h, cfg)
+    u, perm = f.u.cpu().numpy(), f.perm.cpu().numpy()
+    w = w_orig.cpu().numpy()
+    ref32 = og.gptq_sweep(w, u, perm, 4, 128, False, dtype=np.float32, return_pre=True)
+    got_p = codes.cpu().numpy().astype(np.float32)[:, perm] + oq.qrange(4, False)[0]
+    cd = code_diffs(got_p, ref32["q"][:, perm], ref32["pre"])
+    assert cd["max_tie_dist"] <= TIE_TOL, cd["max_tie_dist"]
+
+    x64 = np.concatenate([x.float().cpu().numpy().astype(np.float64) for x in xs])
+    h64 = x64.T @ x64
+    u64, perm64, _ = og.process_hessian_intended(h64, "diag_h", 0.01)
+    ref64 = og.gptq_sweep(w, u64, perm64, 4, 128, False, dtype=np.float64)
+    e_walk = og.reconstruction_error(w, deq.cpu().numpy(), h64)
+    e_ref = og.reconstruction_error(w, ref64["dequant"], h64)
+    report("walk_first_block_attn_in", tie_rows=cd["tie_rows"], e_walk=e_walk, e_oracle64=e_ref)
+    assert abs(e_walk - e_ref) <= 1e-3 * e_ref, (e_walk, e_ref)
