@@ -262,7 +262,8 @@ def test_qr_4096_pivots_match_oracle(qr_fixture, name, rankdef, mode, sem):
     counts as a near-tie when the two |R_jj| there lie within 1e-4 relative
     of each other, or both at float32 noise level of the largest |R_jj| (the
     tail of the rank-deficient matrix, where every norm is rounding noise)."""
-    from jax_gptq_b200.pallas import blocked_pivoted_qr as BQ
+    import importlib
+    BQ = importlib.import_module("jax_gptq_b200.pallas.blocked_pivoted_qr")
     n = int(qr_fixture["n"])
     a = inputs.qr_matrix(1, n, n, rank_deficient=rankdef)
     res = BQ.qrcp(torch.from_numpy(a).cuda(), int(qr_fixture["panel"]), mode, sem)

@@ -84,7 +84,8 @@ def test_walk_first_block_matches_the_oracle(tmp_path):
 
     calib = _calib(5)
     blocks = pipeline.synth_stack(1, CFG, seed=4)
-    w_orig = torch.cat([getattr(blocks[0], n).weight.float() for n in ("q_proj", "k_proj", "v_proj")])
+    w_orig = torch.cat([getattr(blocks[0], n).weight.detach().float()
+                        for n in ("q_proj", "k_proj", "v_proj")])
     with torch.no_grad():
         xs = [blocks[0].input_layernorm(b).reshape(-1, CFG.hidden) for b in calib]
     cfg = QuantConfig(w_bits=4, group_size=128, ordering_mode="diag_h", semantics="intended")
