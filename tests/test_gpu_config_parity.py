@@ -299,8 +299,14 @@ def test_qr_4096_pivots_match_oracle(qr_fixture, name, rankdef, mode, sem):
         assert resid <= 1e-5, resid
     report("qr4096_" + name, **fields)
     assert near_tie, fields
-    assert d_rel <= 1e-3, fields
+    if mode == "largest":
+        assert d_rel <= 1e-3, fields
+    else:
+        # smallest-first pivoting is not rank revealing: the later diagonal
+        # entries carry amplified rounding, so only pivots and residual count
+        assert first >= n - 256, fields
     if rankdef and mode == "largest":
         # rank-revealing order: the pivots agree with the oracle over all
         # 3840 independent columns; the 256 dependent ones come last
         assert first >= n - 256, fields
+        assert fields["numerical_rank"] == n - 256, fields
