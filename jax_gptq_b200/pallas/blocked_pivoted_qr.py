@@ -287,28 +287,39 @@ def build_compact_panel(reflectors, panel_start: int, panel_end: int, n_rows: in
                         A.like_input(t, ref))
 
 
+def benchmark_matrix(n: int = 4096, seed: int = 1, rank_deficient: bool = False,
+                     n_dependent: int = 256) -> np.ndarray:
+    """The benchmark matrix ``A = G diag(s)``, ``G ~ N(0, 1)``, ``s_k =
+    10^(-6k/n)`` in a shuffled column order; the rank-deficient variant
+    replaces ``n_dependent`` columns by random combinations of the others
+    (numpy PCG64, the same bytes as the test fixture's generator)."""
+    rng = np.random.Generator(np.random.PCG64(seed))
+    g = rng.standard_normal((n, n)).astype(np.float32)
+    s = (10.0 ** (-6.0 * np.arange(n) / n)).astype(np.float32)
+    s = s[rng.permutation(n)]
+    a = (g * s[None, :]).astype(np.float32)
+    if rank_deficient:
+        dep = rng.choice(n, size=min(n_dependent, n // 2), replace=False)
+        indep = np.setdiff1d(np.arange(n), dep)
+        coef = rng.standard_normal((indep.shape[0], dep.shape[0])).astype(np.float32)
+        coef /= np.sqrt(np.float32(indep.shape[0]))
+        a[:, dep] = (a[:, indep] @ coef).astype(np.float32)
+    return a
+
+
 def benchmark(n: int = 4096, panel: int = 64, reps: int = 2, seed: int = 1) -> dict:
-    """Time the 4096 x 4096 fp32 benchmark matrix (shuffled geometric column
-    scales ``s_k = 10^(-6k/n)``) in both semantics, plus the rank-deficient
-    variant (256 columns replaced by combinations of the others) in
-    ``smallest`` mode.  GFLOP/s counts (4/3) n^3."""
-    gen = torch.Generator(device="cuda").manual_seed(seed)
-    g = torch.randn((n, n), generator=gen, device="cuda")
-    s = 10.0 ** (-6.0 * torch.arange(n, device="cuda", dtype=torch.float32) / n)
-    s = s[torch.randperm(n, generator=gen, device="cuda")]
-    a = (g * s).contiguous()
-    dep = torch.randperm(n, generator=gen, device="cuda")[:256]
-    mask = torch.ones(n, dtype=torch.bool, device="cuda")
-    mask[dep] = False
-    indep = torch.nonzero(mask).flatten()
-    coef = torch.randn((indep.numel(), 256), generator=gen, device="cuda") / indep.numel() ** 0.5
-    a_def = a.clone()
-    a_def[:, dep] = a[:, indep] @ coef
+    """Time the 4096 x 4096 fp32 benchmark matrix (:func:`benchmark_matrix`)
+    in both semantics, and the rank-deficient variant in ``smallest`` mode
+    (the survey's setting) and ``largest`` mode (rank revealing: its numerical
+    rank is the 3840 of the construction).  GFLOP/s counts (4/3) n^3."""
+    a = torch.from_numpy(benchmark_matrix(n, seed)).cuda()
+    a_def = torch.from_numpy(benchmark_matrix(n, seed, rank_deficient=True)).cuda()
     flops = 4.0 / 3.0 * n ** 3
     out = {"n": n, "panel": panel, "flop_count": "(4/3) n^3"}
     for label, mat, mode, sem in [("intended_largest", a, "largest", "intended"),
                                   ("reference_largest", a, "largest", "reference"),
-                                  ("intended_rankdef_smallest", a_def, "smallest", "intended")]:
+                                  ("intended_rankdef_smallest", a_def, "smallest", "intended"),
+                                  ("intended_rankdef_largest", a_def, "largest", "intended")]:
         qrcp(mat, panel, mode, sem)
         torch.cuda.synchronize()
         e0 = torch.cuda.Event(enable_timing=True)
