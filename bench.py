@@ -518,29 +518,26 @@ def run_reference(args, world, rank):
 
 
 def run_kernel_only(args):
-    """``--only syrk``: just the H-accumulation kernel on [tokens, dim] (profiling runs)."""
+    """``--only syrk``: just the H-accumulation kernel on [tokens, dim];
+    ``--only gemmtn``: just the Qronos cross term G = X^T Xt (profiling runs)."""
     import torch
     from jax_gptq_b200 import _lib
     from jax_gptq_b200 import layerset as LS
     from jax_gptq_b200 import stats
     _lib.lib()
     args.tokens = args.tokens or TOKENS
-    x, _ = LS.synth_activations(args.tokens, args.dim, 7)
+    x, std = LS.synth_activations(args.tokens, args.dim, 7)
     h = torch.empty((args.dim, args.dim), dtype=torch.float32, device="cuda")
-    for _ in range(args.warmup):
-        stats.syrk_into(h, x, accumulate=False)
-    a = torch.cuda.Event(enable_timing=True)
-    b = torch.cuda.Event(enable_timing=True)
-    torch.cuda.synchronize()
-    a.record()
-    for _ in range(args.steps):
-        stats.syrk_into(h, x, accumulate=False)
-    b.record()
-    torch.cuda.synchronize()
-    ms = a.elapsed_time(b) / max(args.steps, 1)
-    tf = LS.syrk_flops(args.tokens, args.dim) / (ms / 1e3) / 1e12
-    print(json.dumps({"kernel": "syrk", "tokens": args.tokens, "d": args.dim, "ms": ms,
-                      "tflops": tf}), flush=True)
+    if args.only == "gemmtn":
+        xt = LS.perturb_activations(x, std, 0.05, 9)
+        fn = lambda: stats.gemm_tn_into(h, x, xt, accumulate=False)
+        flops = LS.gemm_flops(args.tokens, args.dim)
+    else:
+        fn = lambda: stats.syrk_into(h, x, accumulate=False)
+        flops = LS.syrk_flops(args.tokens, args.dim)
+    ms = _time(fn, args.steps, args.warmup)
+    print(json.dumps({"kernel": args.only, "tokens": args.tokens, "d": args.dim, "ms": ms,
+                      "tflops": flops / (ms / 1e3) / 1e12}), flush=True)
 
 
 def _time(fn, steps: int, warmup: int) -> float:
@@ -986,7 +983,7 @@ def main():
                     help="skip the 70B block in the strong-scaling runs")
     ap.add_argument("--syrk-traffic", type=float, default=None,
                     help="DRAM bytes per H-accumulation launch from an ncu capture")
-    ap.add_argument("--only", choices=["all", "syrk", "qr", "gemm", "factor", "sweep"],
+    ap.add_argument("--only", choices=["all", "syrk", "gemmtn", "qr", "gemm", "factor", "sweep"],
                     default="all",
                     help="syrk: time only the H kernel on [--tokens, --dim]; qr: only the "
                          "pivoted QR on a --dim x --dim matrix; gemm / factor / sweep: one "
@@ -996,6 +993,10 @@ def main():
     ap.add_argument("--k", type=int, default=128)
     ap.add_argument("--dim", type=int, default=4096)
     ap.add_argument("--panel", type=int, default=64)
+    ap.add_argument("--qr-variants", default=None,
+                    help="comma-separated subset of the QR variants for --only qr "
+                         "(intended_largest, reference_largest, intended_rankdef_smallest, "
+                         "intended_rankdef_largest)")
     ap.add_argument("--strategy", choices=["layer", "sharded"], default="layer",
                     help="layer: each rank quantizes its own layer set (weak scaling, no "
                          "collective); sharded: one layer set over all ranks (strong scaling)")
@@ -1003,7 +1004,7 @@ def main():
     if args.only != "all":
         import torch
         torch.cuda.set_device(0)
-        if args.only == "syrk":
+        if args.only in ("syrk", "gemmtn"):
             run_kernel_only(args)
         elif args.only in ("gemm", "factor", "sweep"):
             run_component(args)
@@ -1011,6 +1012,7 @@ def main():
             import importlib
             BQ = importlib.import_module("jax_gptq_b200.pallas.blocked_pivoted_qr")
             print(json.dumps({"kernel": "qr", **BQ.benchmark(n=args.dim, panel=args.panel,
+                                                            variants=args.qr_variants,
                                                             reps=max(1, args.steps))}), flush=True)
         return
     if args.impl == "reference":

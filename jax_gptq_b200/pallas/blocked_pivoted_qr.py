@@ -307,7 +307,8 @@ def benchmark_matrix(n: int = 4096, seed: int = 1, rank_deficient: bool = False,
     return a
 
 
-def benchmark(n: int = 4096, panel: int = 64, reps: int = 2, seed: int = 1) -> dict:
+def benchmark(n: int = 4096, panel: int = 64, reps: int = 2, seed: int = 1,
+              variants: str | None = None) -> dict:
     """Time the 4096 x 4096 fp32 benchmark matrix (:func:`benchmark_matrix`)
     in both semantics, and the rank-deficient variant in ``smallest`` mode
     (the survey's setting) and ``largest`` mode (rank revealing: its numerical
@@ -320,6 +321,8 @@ def benchmark(n: int = 4096, panel: int = 64, reps: int = 2, seed: int = 1) -> d
                                   ("reference_largest", a, "largest", "reference"),
                                   ("intended_rankdef_smallest", a_def, "smallest", "intended"),
                                   ("intended_rankdef_largest", a_def, "largest", "intended")]:
+        if variants and label not in variants.split(","):
+            continue
         qrcp(mat, panel, mode, sem)
         torch.cuda.synchronize()
         e0 = torch.cuda.Event(enable_timing=True)
