@@ -296,7 +296,9 @@ int gq_qronos(const float* w, const float* w_orig, int64_t m, int64_t n, const f
  * pallas/blocked_pivoted_qr.py:1627-1722 blocked_pivoted_qr: column-pivoted
  * Householder QR of a [m, n] float32 (lda), in place: on return a holds R in
  * its upper triangle and explicit zeros below (like the reference's `work`),
- * perm [n] int32 the column order.  pivot_mode 0 = "largest", 1 = "smallest".
+ * perm [n] int32 the column order.  pivot_mode 0 = "largest", 1 = "smallest",
+ * 2 = no pivoting (plain Householder QR; perm is the identity; used with
+ * semantics 1 for the unpivoted reduced QR of gptq_ref.py:112-122).
  * semantics 0 reproduces the reference's compiled panel path exactly (index
  * quirks and stale mid-panel pivots included); 1 is a correct blocked QRCP
  * (A[:, perm] = Q R, run in 64-wide panels).  panel_size <= 256 or >= min(m, n);
@@ -344,6 +346,23 @@ int gq_pack_codes(const uint8_t* codes, int64_t m, int64_t n, int64_t ldc, int b
 int gq_unpack_dequant(const uint32_t* packed, int64_t m, int64_t n, int64_t ldp, int bits, int sym,
                       const float* scales, const float* zeros, int64_t n_groups,
                       const int32_t* g_idx, float* dequant, uint8_t* codes, void* stream);
+
+/* ------------------------------------------------------------------------
+ * gptq_ref.py:95-99 (jnp.linalg.eigh of the Hessian in process_hessian's
+ * eigh branch): symmetric eigendecomposition by parallel cyclic Jacobi.
+ *
+ * a [n, n] float32 symmetric (lda; read only).  w [n] eigenvalues in
+ * ascending order (ties by index), v [n, n] (ldv) the matching eigenvectors
+ * as columns, a = v diag(w) v^T.  Sweeps stop when a sweep rotates no pair
+ * (|a_pq| <= 4 eps sqrt(|a_pp a_qq|) for all p < q) or after max_sweeps
+ * (1..100); *sweeps_done (host, nullable) reports the count.  n <= 51200.
+ * BLOCKING: synchronizes the stream once per sweep.  Workspace from
+ * gq_syevj_workspace_size(n) (two n x n float32 buffers), 256-byte aligned.
+ */
+int64_t gq_syevj_workspace_size(int64_t n);
+int gq_syevj(const float* a, int64_t n, int64_t lda, float* w, float* v, int64_t ldv,
+             int max_sweeps, int* sweeps_done, void* workspace, int64_t workspace_bytes,
+             void* stream);
 
 /* ------------------------------------------------------------------------
  * eval.py:9-22 _masked_nll_from_logits: the next-token negative

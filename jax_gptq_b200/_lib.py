@@ -81,6 +81,9 @@ SIGNATURES = {
                                    _P, _P, _P, ctypes.POINTER(c_int), _P, c_int64, _P]),
     "gq_qr_apply_panel": (c_int, [_P, c_int64, c_int64, c_int64, _P, c_int64, _P, c_int64, c_int, _P,
                                   _P]),
+    "gq_syevj_workspace_size": (c_int64, [c_int64]),
+    "gq_syevj": (c_int, [_P, c_int64, c_int64, _P, _P, c_int64, c_int, ctypes.POINTER(c_int), _P,
+                         c_int64, _P]),
     "gq_masked_nll_workspace_size": (c_int64, [c_int64, c_int64]),
     "gq_masked_nll": (c_int, [_P, c_int, c_int64, c_int64, c_int64, _P, _P, _P, _P, c_int64, _P]),
     "gq_qronos_workspace_size": (c_int64, [c_int64, c_int64]),

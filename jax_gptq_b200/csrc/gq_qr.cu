@@ -157,6 +157,7 @@ struct StepArgs {
   float* left;     // m - k
   Ctrl* ctrl;
   int smallest;
+  int nopivot;     // unpivoted Householder QR: the pivot of step j is column j
   int semantics;   // 0 reference, 1 intended
 };
 
@@ -261,8 +262,8 @@ qr_step_cluster_kernel(StepArgs a) {
     }
   }
   // 2. pivot: first argmax / argmin over columns >= j (every CTA alike)
-  int p;
-  {
+  int p = (int)j;
+  if (!a.nopivot) {
     const bool larger = !a.smallest;
     float bv = larger ? -INFINITY : INFINITY;
     int bi = 0x7fffffff;
@@ -660,7 +661,8 @@ int factor_panel(Work& W, int64_t m, int64_t n, int64_t k, int P, int smallest, 
     a.at = W.at; a.m = m; a.n = n; a.k = k; a.pe = pe; a.j = j; a.P = P;
     a.yt = W.yt; a.t = W.t; a.tau = W.tau; a.norms = W.norms; a.perm = perm; a.left = W.left;
     a.normref = W.normref;
-    a.ctrl = W.ctrl; a.smallest = smallest; a.semantics = semantics;
+    a.ctrl = W.ctrl; a.smallest = smallest == 1; a.nopivot = smallest == 2;
+    a.semantics = semantics;
     // both kernels start with griddepcontrol.wait, so each may be launched
     // while its predecessor is still running (programmatic dependent launch)
     cudaLaunchAttribute pdl;
@@ -714,7 +716,8 @@ int gq_qrcp(float* a, int64_t m, int64_t n, int64_t lda, int panel_size, int piv
   GQ_REQUIRE(m > 0 && n > 0 && lda >= n, "gq_qrcp: bad shape (m=%lld n=%lld lda=%lld)",
              (long long)m, (long long)n, (long long)lda);
   GQ_REQUIRE(panel_size > 0, "panel_size must be positive, got %d", panel_size);
-  GQ_REQUIRE(pivot_mode == 0 || pivot_mode == 1, "gq_qrcp: pivot_mode must be 0 (largest) or 1 (smallest)");
+  GQ_REQUIRE(pivot_mode >= 0 && pivot_mode <= 2,
+             "gq_qrcp: pivot_mode must be 0 (largest), 1 (smallest) or 2 (none)");
   GQ_REQUIRE(semantics == 0 || semantics == 1, "gq_qrcp: semantics must be 0 or 1");
   GQ_REQUIRE(m * 8 <= 200 * 1024, "gq_qrcp: m=%lld exceeds the step kernel's shared memory", (long long)m);
   GQ_REQUIRE(n < (1ll << 31) && m < (1ll << 31), "gq_qrcp: dimension too large");

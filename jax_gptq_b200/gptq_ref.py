@@ -160,12 +160,32 @@ def factor_from_activations_attempt0(x: torch.Tensor, cfg: QuantConfig,
     return HessianFactor(u, perm, 0, None), status
 
 
+EIGH_MAX_SWEEPS = 30
+
+
+def eigh(h) -> tuple[torch.Tensor, torch.Tensor]:
+    """``jnp.linalg.eigh`` (gptq_ref.py:98) on the device with the library's
+    Jacobi eigensolver (``gq_syevj``): eigenvalues ascending, eigenvectors as
+    columns, ``h = v diag(w) v^T``."""
+    hd = A.to_device(h)
+    n = hd.shape[0]
+    w = A.empty((n,))
+    v = A.empty((n, n))
+    ws = A.workspace(_lib.lib().gq_syevj_workspace_size(n))
+    import ctypes
+    sweeps = ctypes.c_int(0)
+    _lib.call("gq_syevj", A.ptr(hd), n, hd.stride(0), A.ptr(w), A.ptr(v), n, EIGH_MAX_SWEEPS,
+              ctypes.byref(sweeps), A.ptr(ws), ws.numel(), A.stream())
+    return w, v
+
+
 def _process_hessian_eigh(h, cfg: QuantConfig, panel_size: int):
     """gptq_ref.py:95-133 on the device.
 
-    The eigendecomposition and the unpivoted reduced QR are cuSOLVER calls
-    (``torch.linalg.eigh`` / ``torch.linalg.qr``); the act-order ranking and
-    the blocked pivoted QR of the pivot_* modes are this library's kernels.
+    Every step runs on this library's kernels: the eigendecomposition by
+    parallel Jacobi (:func:`eigh`, ``gq_syevj``), the unpivoted reduced QR by
+    the Householder QR without pivoting (``gq_qrcp`` mode 2), the act-order
+    ranking and the blocked pivoted QR of the pivot_* modes.
     ``sqrt_h = sqrt(lam) V^T`` and ``sqrt_hinv = lam^-1/2 V^T`` over the kept
     eigenpairs (descending, rank from the truncation rule).  For none / diag_h
     / pivot_sqrt_h the factor is R of ``sqrt_hinv.T[:, perm]``: in reference
@@ -179,7 +199,7 @@ def _process_hessian_eigh(h, cfg: QuantConfig, panel_size: int):
     BQ = importlib.import_module("jax_gptq_b200.pallas.blocked_pivoted_qr")
     hd = A.to_device(h)
     n = hd.shape[0]
-    evals, evecs = torch.linalg.eigh(hd)
+    evals, evecs = eigh(hd)
     evals, evecs = evals.flip(0), evecs.flip(1)
     rank = _select_truncation_rank(evals, cfg)
     lam, v = evals[:rank], evecs[:, :rank]
@@ -199,8 +219,8 @@ def _process_hessian_eigh(h, cfg: QuantConfig, panel_size: int):
         m = sqrt_hinv.T[:, idx.clamp(max=rank - 1)]
     else:
         m = sqrt_hinv[:, idx]
-    r = torch.linalg.qr(m.contiguous(), mode="r").R
-    return r.contiguous(), perm
+    r = BQ.householder_qr_r(m.contiguous())
+    return r, perm
 
 
 def process_hessian(h, cfg: QuantConfig, panel_size: int = 32):

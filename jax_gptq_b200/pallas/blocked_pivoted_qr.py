@@ -34,6 +34,7 @@ ZERO_TOL = 1e-12
 ZERO_TOL_SQ = ZERO_TOL * ZERO_TOL
 
 _MODES = {"largest": 0, "smallest": 1}
+_NO_PIVOTING = 2  # gq_qrcp pivot_mode for plain Householder QR (not a reference mode)
 _SEMANTICS = {"reference": 0, "intended": 1}
 
 
@@ -72,13 +73,15 @@ def _mode(pivot_mode: str) -> int:
     return _MODES[pivot_mode]
 
 
-def qrcp(a, panel_size: int, pivot_mode: str = "largest", semantics: str = "reference") -> QRResult:
-    """Full factorization on the device; returns work, perm, reflectors."""
+def qrcp(a, panel_size: int, pivot_mode: str = "largest", semantics: str = "reference",
+         _unpivoted: bool = False) -> QRResult:
+    """Full factorization on the device; returns work, perm, reflectors.
+    ``_unpivoted`` runs plain Householder QR instead (``pivot_mode`` ignored)."""
     if len(tuple(a.shape)) != 2:
         raise ValueError(f"a must be 2D, got {tuple(a.shape)}")
     if panel_size <= 0:
         raise ValueError(f"panel_size must be positive, got {panel_size}")
-    mode = _mode(pivot_mode)
+    mode = _NO_PIVOTING if _unpivoted else _mode(pivot_mode)
     if semantics not in _SEMANTICS:
         raise ValueError(f"unsupported semantics={semantics}")
     work = A.to_device(a).clone()
@@ -95,6 +98,13 @@ def qrcp(a, panel_size: int, pivot_mode: str = "largest", semantics: str = "refe
               A.ptr(perm), A.ptr(v), r, A.ptr(tau), ctypes.c_void_p(ends.data_ptr()),
               ctypes.byref(npan), A.ptr(ws), ws.numel(), A.stream())
     return QRResult(work, perm, v, tau, ends[: npan.value].tolist())
+
+
+def householder_qr_r(a, panel_size: int = 64) -> torch.Tensor:
+    """R of the reduced QR of ``a`` [m, n] (``mode="r"``: min(m, n) x n, upper
+    triangular) by the library's own Householder QR without pivoting."""
+    res = qrcp(a, panel_size, semantics="intended", _unpivoted=True)
+    return torch.triu(res.work[: min(res.work.shape)]).contiguous()
 
 
 def blocked_pivoted_qr(a, panel_size: int, pivot_mode: str = "largest",

@@ -146,3 +146,15 @@ def test_sweep_rejects_shapes_whose_workspace_would_overflow():
     with pytest.raises(ValueError, match="row buffer"):
         _lib.call("gq_gptq_sweep_static", None, 4, 1 << 20, 1 << 20, None, None, 1 << 20, None, 4,
                   128, 0, 128, None, None, 0, None, None, None, None, None, None)
+
+
+def test_eigensolver_and_qr_modes_reject_bad_arguments():
+    with pytest.raises(ValueError, match="max_sweeps"):
+        _lib.call("gq_syevj", ctypes.c_void_p(16), 8, 8, ctypes.c_void_p(16), ctypes.c_void_p(16),
+                  8, 0, None, ctypes.c_void_p(256), 1 << 20, None)
+    with pytest.raises(ValueError, match="staged row"):
+        _lib.call("gq_syevj", ctypes.c_void_p(16), 60000, 60000, ctypes.c_void_p(16),
+                  ctypes.c_void_p(16), 60000, 10, None, ctypes.c_void_p(256), 1 << 40, None)
+    with pytest.raises(ValueError, match="pivot_mode"):
+        _lib.call("gq_qrcp", ctypes.c_void_p(16), 8, 8, 8, 8, 3, 1, ctypes.c_void_p(16), None, 8,
+                  None, None, None, ctypes.c_void_p(256), 1 << 20, None)
