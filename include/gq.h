@@ -113,10 +113,10 @@ int gq_gemm_f32_tc(int trans_b, int64_t M, int64_t N, int64_t K, float alpha,
  *                  xb = x_quant)
  * accumulate = 0 overwrites, 1 adds to the existing contents (streamed
  * calibration batches).  ldh/ldg are in elements.
- * Products are summed in chunks of 512 tokens (each chunk in tensor memory),
+ * Products are summed in chunks of 1024 tokens (each chunk in tensor memory),
  * and the chunk results are added in token order to a float32 running sum
  * that starts from the existing contents when accumulating; so splitting the
- * tokens into calls at multiples of 512 gives the same bits as one call.
+ * tokens into calls at multiples of 1024 gives the same bits as one call.
  */
 int gq_syrk_bf16(const uint16_t* x, int64_t tokens, int64_t d, int64_t ldx,
                  float* h, int64_t ldh, int accumulate, void* stream);

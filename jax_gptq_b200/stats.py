@@ -36,7 +36,7 @@ def _is_bf16(x) -> bool:
 
 # bf16 products are summed in tensor-memory chunks of this many tokens; calls
 # split at multiples of it give the same bits as one call (see gq.h)
-TOKEN_CHUNK_QUANTUM = 512
+TOKEN_CHUNK_QUANTUM = 1024
 
 
 def _token_slices(tokens: int, token_chunk):

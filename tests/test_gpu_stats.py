@@ -102,9 +102,9 @@ def test_zero_tokens_gives_zero_h():
     assert float(h.abs().max()) == 0.0
 
 
-@pytest.mark.parametrize("tokens,d,chunk", [(4096, 520, 512), (6144, 1024, 2048), (5000, 384, 1024)])
+@pytest.mark.parametrize("tokens,d,chunk", [(4096, 520, 1024), (6144, 1024, 2048), (5000, 384, 1024)])
 def test_token_chunked_launches_equal_one_launch(tokens, d, chunk):
-    """Splitting the tokens at multiples of 512 continues the same float32
+    """Splitting the tokens at multiples of 1024 continues the same float32
     running sum: H and G are bit-identical to a single launch (the tail chunk
     may be ragged)."""
     from jax_gptq_b200 import stats
@@ -122,7 +122,7 @@ def test_token_chunked_launches_equal_one_launch(tokens, d, chunk):
     assert _status() == 0
     assert torch.equal(h1, h2)
     assert torch.equal(g1, g2)
-    # a streamed accumulator over 512-multiple batches is the same sum again
+    # a streamed accumulator over 1024-multiple batches is the same sum again
     acc = HessianAccumulator(d, with_cross=True)
     for t0 in range(0, tokens, chunk):
         acc.add(xq[t0:t0 + chunk], xf[t0:t0 + chunk])
@@ -130,12 +130,13 @@ def test_token_chunked_launches_equal_one_launch(tokens, d, chunk):
     assert torch.equal(acc.g, g1)
 
 
-def test_token_chunk_must_be_a_multiple_of_512():
+def test_token_chunk_must_be_a_multiple_of_1024():
     from jax_gptq_b200 import stats
-    x = torch.zeros((2048, 64), dtype=torch.bfloat16, device="cuda")
+    x = torch.zeros((4096, 64), dtype=torch.bfloat16, device="cuda")
     h = torch.empty((64, 64), device="cuda")
-    with pytest.raises(ValueError):
-        stats.syrk_into(h, x, accumulate=False, token_chunk=1000)
+    for bad in (1000, 512):
+        with pytest.raises(ValueError):
+            stats.syrk_into(h, x, accumulate=False, token_chunk=bad)
 
 
 @pytest.mark.parametrize("tokens,d,sym", [(4096, 1000, True), (2048, 520, True), (3000, 392, False)])
