@@ -651,6 +651,30 @@ def run_ours(args, world, rank, local):
     LS.quantize_layer_gptq(weights, inputs, cfg, shapes, concurrent=False)  # warm its buffers
     _, phases = LS.quantize_layer_gptq(weights, inputs, cfg, shapes, timed=True)
 
+    # --- the sweeps against both of their bounds: the lazy-update flops on
+    # the 3xTF32 tensor-core GEMM (ceiling: the same kernel on a large square
+    # product, timed here) and the algorithmic HBM bytes
+    sweep_flop = float(sum(m * n * (n - 128) for _, m, n, _ in shapes))
+    sweep_bytes = float(sum(8.5 * m * n + 8 * m * (n // 128) + 4 * n * n for _, m, n, _ in shapes))
+    from jax_gptq_b200 import _arrays as A
+    ga = torch.randn(4096, 4096, device="cuda")
+    gb = torch.randn(4096, 4096, device="cuda")
+    gc = torch.empty(4096, 4096, device="cuda")
+    g_ms = _time(lambda: _lib.call("gq_gemm_f32_tc", 1, 4096, 4096, 4096, 1.0, A.ptr(ga), 4096,
+                                   A.ptr(gb), 4096, 0.0, A.ptr(gc), 4096, 0, A.stream()), 5, 2)
+    ceiling = 2.0 * 4096 ** 3 / (g_ms / 1e3) / 1e12
+    del ga, gb, gc
+    sw_s = phases.sweep_ms / 1e3
+    sweep_roof = {
+        "ms_all_linears_sequential": phases.sweep_ms,
+        "tflops": sweep_flop / sw_s / 1e12, "gemm_ceiling_tflops": ceiling,
+        "frac_of_gemm_ceiling": sweep_flop / sw_s / 1e12 / ceiling,
+        "gbs": sweep_bytes / sw_s / 1e9, "frac_hbm": sweep_bytes / sw_s / 1e9 / peaks["hbm_gbs"],
+        "algorithmic": f"sum m*n*(n-128) = {sweep_flop:.4g} flops (3xTF32 lazy updates); "
+                       f"sum 8.5mn + 8m(n/128) + 4n^2 = {sweep_bytes:.4g} bytes",
+        "note": "each column's quantize -> error -> update is a dependent chain (about 200 "
+                "cycles per column per row), so neither bound is reached"}
+
     # --- roofline of the H-accumulation kernel (tcgen05), timed live on its stream
     syrk_ms, syrk_flop = [], []
     for grp, x in inputs.items():
@@ -808,7 +832,8 @@ def run_ours(args, world, rank, local):
                         "tflop_per_layer_distinct_inputs": sum(syrk_flop) / 1e12,
                         "tflop_per_layer_per_linear":
                             sum(LS.syrk_flops(args.tokens, n) for _, _, n, _ in shapes) / 1e12},
-            "roofline": roofline, "e2e": e2e, "gpu_launches": int(launches), "clocks": clocks,
+            "roofline": roofline, "sweep_roofline": sweep_roof, "e2e": e2e,
+            "gpu_launches": int(launches), "clocks": clocks,
             "qronos": qronos, "qr": qr, "cpu_baseline": cpu,
         }
         if not args.no_parity:
