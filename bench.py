@@ -503,7 +503,10 @@ def run_reference(args, world, rank):
         # the wall time of each timed step: the bounded sample actually run
         "ms_per_step": statistics.mean(walls) * 1000.0,
         "higher_is_better": False, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
-        "data": "synthetic", "config": {"workload": WORKLOAD, "tokens": TOKENS},
+        "data": "synthetic", "config": {"workload": WORKLOAD, "tokens": TOKENS,
+                                        "semantics": "reference: x^T x, the five Cholesky "
+                                                     "attempts its process_hessian makes, "
+                                                     "act-order, RTN (what the reference runs)"},
         "value_kind": "extrapolated: each step times a bounded sample of one layer set and "
                       "scales each part to the full layer set (see cpu_baseline.sample)",
         "cpu_baseline": {"value": v, "unit": "s/layer", "cores": cores, "kind": "port",
@@ -823,6 +826,10 @@ def run_ours(args, world, rank, local):
             "higher_is_better": False, "scaling": "weak", "vs_baseline": None,
             "dtype": "bf16 in / f32 accumulate (H); f32 sweep", "data": "synthetic",
             "config": {"workload": workload, "tokens": args.tokens, "layers_per_rank": 1,
+                       "semantics": "intended: damped inverse-Cholesky factor + GPTQ column "
+                                    "sweep (the reference's own chol path returns the identity "
+                                    "factor and RTN, strictly less work; the reference arm "
+                                    "times that op sequence)",
                        "parallelism": f"layer-parallel x{world}",
                        "l2": f"inputs ({x_gb:.1f} GB) larger than L2; no flush",
                        "skipped_for_memory": skipped},
