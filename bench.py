@@ -705,9 +705,9 @@ def run_ours(args, world, rank, local):
     traffic = args.syrk_traffic
     if traffic is None and top_d == 11008:
         # DRAM bytes of one d = 11008 launch from an ncu capture at 32768 tokens
-        # (6.146 GB read: each wave of the 946 pair tiles streams the X columns
-        # of its tile group; 0.245 GB of H written), scaled to this launch's tokens
-        traffic = 6.146e9 * args.tokens / 32768 + 0.245e9
+        # (10.575 GB read: each wave of the 946 pair tiles streams the X columns
+        # of its tile group; 0.265 GB of H written), scaled to this launch's tokens
+        traffic = 10.575e9 * args.tokens / 32768 + 0.265e9
     peak = peaks.get("bf16_tflops_sustained", peaks.get("bf16_tflops"))
     roofline = {"bound": "tensor",
                 "kernel": f"gq_tc gemm_tn_pair_kernel (H = X^T X, symmetric 256 x 256 tiles "
