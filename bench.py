@@ -913,6 +913,11 @@ def sharded_layer_set(model, tokens, steps, warmup, world, rank, local, check=Tr
         ev[0].record()
         stats.syrk_into(h, x, accumulate=False)
         ev[1].record()
+        # every rank's partial H is complete before the all-reduce is timed, so
+        # the figure is the transfer, not the wait for the slowest rank's SYRK
+        _barrier(world)
+        ar0 = torch.cuda.Event(enable_timing=True)
+        ar0.record()
         D.allreduce_sum_(h)
         ev[2].record()
         f = factor_hessian(h, cfg)
@@ -923,7 +928,8 @@ def sharded_layer_set(model, tokens, steps, warmup, world, rank, local, check=Tr
         res = gptq_sweep(w[r0:r1], f.u, f.perm, cfg)
         ev[4].record()
         torch.cuda.synchronize()
-        t = [ev[i].elapsed_time(ev[i + 1]) for i in range(4)]
+        t = [ev[0].elapsed_time(ev[1]), ar0.elapsed_time(ev[2]), ev[2].elapsed_time(ev[3]),
+             ev[3].elapsed_time(ev[4])]
         t = [_max_over_ranks(v, world) for v in t]
         ar_bytes = 4 * d * d
         # NCCL's bus-bandwidth convention for all-reduce: 2 (N - 1) / N of the buffer per rank
