@@ -208,10 +208,46 @@ def test_layer_set_down_proj_sweep_sampled(mlp_out_input):
     assert np.array_equal(res.g_idx.cpu().numpy(), ref["g_idx"])
 
 
+def _recon(w, w_hat, h64):
+    """||(W - W^) X^T|| / ||W X^T|| through H = X^T X (BLAS products)."""
+    w = np.asarray(w, np.float64)
+    d = w - np.asarray(w_hat, np.float64)
+    return float(np.sqrt(np.sum((d @ h64) * d) / np.sum((w @ h64) * w)))
+
+
+def test_layer_set_down_proj_reconstruction_vs_float64(mlp_out_input):
+    """The GPU's GPTQ of the sampled down_proj rows against the float64
+    oracle with its own float64 factor of the same H: the reconstruction
+    errors agree within 1e-3 relative (H itself is checked to 1e-5 above)."""
+    _, _, h = mlp_out_input
+    cfg = QuantConfig(w_bits=4, group_size=128, sym=False, damp_percent=0.01,
+                      ordering_mode="diag_h", semantics="intended")
+    f = G.factor_hessian(h, cfg)
+    w = LS.synth_weights([("down", 4096, D_MLP, "mlp_out")], 0.02, 5)["down"]
+    res = G.gptq_sweep(w, f.u, f.perm, cfg)
+    rows = torch.from_numpy(ROW_BLOCKS).cuda()
+    ws = w[rows].cpu().numpy()
+    h64 = h.cpu().numpy().astype(np.float64)
+    u64, perm64, att = og.process_hessian_intended(h64, "diag_h", 0.01)
+    assert att == 0
+    assert np.array_equal(perm64, f.perm.cpu().numpy())
+    ref64 = og.gptq_sweep(ws, u64, perm64, 4, 128, False, dtype=np.float64)
+    e_gpu = _recon(ws, res.dequant[rows].cpu().numpy(), h64)
+    e_ref = _recon(ws, ref64["dequant"], h64)
+    e_rtn = _recon(ws, oq.quantize_dequantize(ws, 4, 128), h64)
+    report("down_proj_reconstruction_vs_float64", e_gpu=e_gpu, e_oracle64=e_ref, e_rtn=e_rtn,
+           rel=abs(e_gpu - e_ref) / e_ref, rows=len(ROW_BLOCKS))
+    assert abs(e_gpu - e_ref) <= RECON_REL * e_ref, (e_gpu, e_ref)
+    assert e_gpu < e_rtn
+
+
 def test_layer_set_down_proj_qronos_sampled(mlp_out_input):
     """Qronos 3-bit: h = Xt^T Xt, g = X^T Xt, the GPU update against the
-    float32 oracle given the same factor (U, permutation, damped H)."""
-    x, std, _ = mlp_out_input
+    float32 oracle given the same factor (U, permutation, damped H); then the
+    layer's Qronos objective ||X w - Xt w^|| / ||X w|| on the sampled rows
+    against the float64 oracle with its own float64 factor, within 1e-3
+    relative."""
+    x, std, hxx = mlp_out_input
     xt = LS.perturb_activations(x, std, 0.05, 63)
     hq = torch.empty((D_MLP, D_MLP), dtype=torch.float32, device="cuda")
     stats.syrk_into(hq, xt, accumulate=False)
@@ -221,6 +257,7 @@ def test_layer_set_down_proj_qronos_sampled(mlp_out_input):
     cfg = QuantConfig(w_bits=3, group_size=128, sym=False, damp_percent=0.01,
                       ordering_mode="diag_h", semantics="intended")
     f = G.factor_hessian(hq, cfg, want_hd=True)
+    hq64 = hq.cpu().numpy().astype(np.float64)
     del hq
     assert f.attempt == 0
     w = LS.synth_weights([("down", 4096, D_MLP, "mlp_out")], 0.02, 6)["down"]
@@ -236,7 +273,29 @@ def test_layer_set_down_proj_qronos_sampled(mlp_out_input):
                               return_pre=True)
     codes = res.codes[rows].cpu().numpy()
     cd = _ties_ok("down_proj_qronos_sampled", codes, ref, perm, 3)
-    report("down_proj_qronos_rows", rows=len(ROW_BLOCKS), tie_rows=cd["tie_rows"])
+
+    # the Qronos objective through the statistics: with d = w^ (Xt) and w (X),
+    # ||X w - Xt w^||^2 = w Hxx w - 2 w G w^ + w^ Hq w^  (G = X^T Xt)
+    g64 = gn.astype(np.float64)
+    del gn, ref
+    hxx64 = hxx.cpu().numpy().astype(np.float64)
+
+    def objective(w_hat):
+        w64, wh = ws.astype(np.float64), np.asarray(w_hat, np.float64)
+        den = np.sum((w64 @ hxx64) * w64)
+        num = den - 2.0 * np.sum((w64 @ g64) * wh) + np.sum((wh @ hq64) * wh)
+        return float(np.sqrt(max(num, 0.0) / den))
+
+    ref64 = oqn.qronos_intended(ws, ws, hq64, g64, 3, 128, False, ordering_mode="diag_h",
+                                dtype=np.float64)
+    assert np.array_equal(ref64["perm"], perm)
+    e_gpu = objective(res.dequant[rows].cpu().numpy())
+    e_ref = objective(ref64["dequant"])
+    e_rtn = objective(oq.quantize_dequantize(ws, 3, 128))
+    report("down_proj_qronos_rows", rows=len(ROW_BLOCKS), tie_rows=cd["tie_rows"],
+           e_gpu=e_gpu, e_oracle64=e_ref, e_rtn=e_rtn, rel=abs(e_gpu - e_ref) / e_ref)
+    assert abs(e_gpu - e_ref) <= RECON_REL * e_ref, (e_gpu, e_ref)
+    assert e_gpu < e_rtn
 
 
 # ----------------------------------------------------------------------------- pivoted QR 4096
