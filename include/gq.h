@@ -205,6 +205,38 @@ int gq_hessian_factor_attempt(const float* h, int64_t d, int64_t ldh, const int3
                               float* hd_out, void* workspace, int64_t workspace_bytes,
                               int* status, void* stream);
 
+/* The factor's building blocks, for hosts that split the factorization's
+ * products across GPUs (jax_gptq_b200.distributed.factor_hessian_sharded):
+ *
+ * gq_hessian_prepare  b [d, d] (ld d) = J (h[perm][:, perm] + damp I) J in
+ *                     its lower triangle, zeros above (J reverses the order;
+ *                     damp = damp_percent * 10^attempt * mean(diag h), mean 0
+ *                     -> 1, as gptq_ref.py:72-83); hd_out (nullable, ld d) the
+ *                     damped permuted Hessian itself; mean: one device float.
+ * gq_inv_chol         in place: the lower triangle of a [n, n] (lda, strict
+ *                     upper zero) becomes L^-1 where a = L L^T (the recursion
+ *                     and leaves of gq_hessian_factor); a non-positive pivot
+ *                     sets *status (device int, not cleared here) non-zero.
+ * gq_reverse_lower    u = J x J for the lower triangle x: u is the upper factor
+ *                     u = chol(Hd^-1, upper) when x = L^-1 of the prepared b.
+ * gq_sgemm_tri        gq_sgemm (uplo 0) with a triangular operand whose zero
+ *                     triangle starts on 128 boundaries skipped per tile:
+ *                     tri 1 A upper (k >= row), 2 A lower (k <= row), 3 B lower
+ *                     (k <= col), 4 B upper (k >= col); 0 none.  Rows and
+ *                     columns are the call's own, so a row slice of a
+ *                     triangular A needs tri 0.
+ */
+int gq_hessian_prepare(const float* h, int64_t d, int64_t ldh, const int32_t* perm,
+                       double damp_percent, int attempt, float* b, float* hd_out, float* mean,
+                       void* stream);
+int64_t gq_inv_chol_workspace_size(int64_t n);
+int gq_inv_chol(float* a, int64_t n, int64_t lda, void* workspace, int64_t workspace_bytes,
+                int* status, void* stream);
+int gq_reverse_lower(const float* x, int64_t d, int64_t ldx, float* u, int64_t ldu, void* stream);
+int gq_sgemm_tri(int trans_a, int trans_b, int64_t M, int64_t N, int64_t K, float alpha,
+                 const float* a, int64_t lda, const float* b, int64_t ldb, float beta, float* c,
+                 int64_t ldc, int tri, void* stream);
+
 /* No counterpart in the reference: attempt 0 of the factor, formed straight
  * from the bf16 activations x[tokens, d] (ld ldx), with the same u and perm,
  * bit for bit, as gq_syrk_bf16 -> gq_act_order_perm(ordering) ->

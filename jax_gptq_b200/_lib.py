@@ -65,6 +65,12 @@ SIGNATURES = {
                                   ctypes.POINTER(c_int), _P]),
     "gq_hessian_factor_attempt": (c_int, [_P, c_int64, c_int64, _P, c_double, c_int, _P, c_int64,
                                           _P, _P, c_int64, _P, _P]),
+    "gq_hessian_prepare": (c_int, [_P, c_int64, c_int64, _P, c_double, c_int, _P, _P, _P, _P]),
+    "gq_inv_chol_workspace_size": (c_int64, [c_int64]),
+    "gq_inv_chol": (c_int, [_P, c_int64, c_int64, _P, c_int64, _P, _P]),
+    "gq_reverse_lower": (c_int, [_P, c_int64, c_int64, _P, c_int64, _P]),
+    "gq_sgemm_tri": (c_int, [c_int, c_int, c_int64, c_int64, c_int64, c_float, _P, c_int64, _P,
+                             c_int64, c_float, _P, c_int64, c_int, _P]),
     "gq_gptq_sweep_workspace_size": (c_int64, [c_int64, c_int64]),
     "gq_gptq_sweep": (c_int, [_P, c_int64, c_int64, c_int64, _P, _P, c_int64, _P, c_int, c_int, c_int,
                               c_int, _P, _P, c_int, _P, _P, _P, _P, _P, _P, c_int64, _P]),

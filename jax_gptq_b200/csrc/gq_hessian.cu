@@ -851,6 +851,66 @@ int gq_act_order_perm(const float* h, int64_t d, int64_t ldh, int ordering, int3
   return gq::act_order_perm(h, d, ldh, ordering, perm, gq::as_stream(stream));
 }
 
+int64_t gq_inv_chol_workspace_size(int64_t n) {
+  return n <= 0 ? 256 : gq::inv_chol_scratch_floats(n) * (int64_t)sizeof(float) + 256;
+}
+
+int gq_inv_chol(float* a, int64_t n, int64_t lda, void* workspace, int64_t workspace_bytes,
+                int* status, void* stream) {
+  GQ_REQUIRE(a != nullptr && status != nullptr, "gq_inv_chol: NULL a or status");
+  GQ_REQUIRE(n > 0 && lda >= n, "gq_inv_chol: bad shape");
+  GQ_REQUIRE(workspace_bytes >= gq_inv_chol_workspace_size(n), "gq_inv_chol: workspace too small");
+  GQ_REQUIRE((reinterpret_cast<uintptr_t>(workspace) & 255) == 0,
+             "gq_inv_chol: workspace must be 256-byte aligned");
+  GQ_TRY(gq::diag_kernel_setup());
+  return gq::inv_chol(a, n, lda, static_cast<float*>(workspace), status, gq::as_stream(stream));
+}
+
+int gq_hessian_prepare(const float* h, int64_t d, int64_t ldh, const int32_t* perm,
+                       double damp_percent, int attempt, float* b, float* hd_out, float* mean,
+                       void* stream) {
+  GQ_REQUIRE(h != nullptr && b != nullptr && mean != nullptr, "gq_hessian_prepare: NULL argument");
+  GQ_REQUIRE(d > 0 && ldh >= d, "gq_hessian_prepare: bad shape");
+  GQ_REQUIRE(damp_percent >= 0.0 && attempt >= 0 && attempt < 5,
+             "gq_hessian_prepare: bad damp_percent or attempt");
+  GQ_REQUIRE(d * (int64_t)sizeof(float) <= gq::MAX_ROW_BYTES, "gq_hessian_prepare: d = %lld too large",
+             (long long)d);
+  cudaStream_t st = gq::as_stream(stream);
+  GQ_TRY(gq::diag_kernel_setup());
+  gq::diag_mean_kernel<<<1, 1024, 0, st>>>(h, d, ldh, mean);
+  GQ_TRY(gq::check_launch("diag_mean"));
+  const float damp = (float)(std::pow(10.0, attempt) * damp_percent);
+  const unsigned rows_grid = (unsigned)std::min<int64_t>(d, 148 * 16);
+  const size_t row_bytes = (size_t)d * sizeof(float);
+  gq::damp_permute_rows_kernel<true><<<rows_grid, 256, row_bytes, st>>>(h, d, ldh, perm, mean,
+                                                                        damp, b);
+  GQ_TRY(gq::check_launch("damp_permute"));
+  if (hd_out) {
+    gq::damp_permute_rows_kernel<false><<<rows_grid, 256, row_bytes, st>>>(h, d, ldh, perm, mean,
+                                                                           damp, hd_out);
+    GQ_TRY(gq::check_launch("damp_permute"));
+  }
+  return GQ_OK;
+}
+
+int gq_reverse_lower(const float* x, int64_t d, int64_t ldx, float* u, int64_t ldu, void* stream) {
+  GQ_REQUIRE(x != nullptr && u != nullptr && d > 0 && ldx >= d && ldu >= d,
+             "gq_reverse_lower: bad argument");
+  cudaStream_t st = gq::as_stream(stream);
+  gq::reverse_copy_kernel<<<(unsigned)std::min<int64_t>(d, 148 * 16), 256, 0, st>>>(x, d, ldx, u,
+                                                                                   ldu);
+  return gq::check_launch("reverse_copy");
+}
+
+int gq_sgemm_tri(int trans_a, int trans_b, int64_t M, int64_t N, int64_t K, float alpha,
+                 const float* a, int64_t lda, const float* b, int64_t ldb, float beta, float* c,
+                 int64_t ldc, int tri, void* stream) {
+  GQ_REQUIRE(tri >= 0 && tri <= 4, "gq_sgemm_tri: tri must be 0..4");
+  GQ_REQUIRE(M >= 0 && N >= 0 && K >= 0, "gq_sgemm_tri: negative shape");
+  return gq::sgemm_tri(trans_a, trans_b, M, N, K, alpha, a, lda, b, ldb, beta, c, ldc, tri,
+                       gq::as_stream(stream));
+}
+
 int64_t gq_hessian_factor_workspace_size(int64_t d) {
   return gq::hessian_ws_floats(d) * (int64_t)sizeof(float);
 }

@@ -233,6 +233,155 @@ def hessians_token_sharded(inputs_local: dict[str, torch.Tensor], group=None,
     return (hs, gs) if inputs_float_local is not None else hs
 
 
+# Hessians at least this wide split their factor's top-level products
+# across the ranks (factor_hessian_sharded_attempt0); smaller ones are factored
+# whole on every rank.
+FACTOR_SHARD_MIN_D = 2048
+_FACTOR_GROUPS: dict = {}
+
+
+def _factor_group(group):
+    """A second communicator over the same ranks for the factor's
+    all-gathers, so they queue on their own NCCL stream and a group's H
+    all-reduce never waits behind another group's factor (created once per
+    process group, collectively, in the same order on every rank)."""
+    dist = _dist()
+    key = id(group) if group is not None else None
+    if key not in _FACTOR_GROUPS:
+        ranks = list(range(dist.get_world_size(group))) if group is None else \
+            dist.get_process_group_ranks(group)
+        _FACTOR_GROUPS[key] = dist.new_group(ranks)
+    return _FACTOR_GROUPS[key]
+
+
+def _split_n1(n: int, nb: int = 128) -> int:
+    """The leading block of the factor's top split (a multiple of 128, about n/2)."""
+    n1 = ((n // 2 + nb - 1) // nb) * nb
+    return n - nb if n1 >= n else n1
+
+
+def _factor_top_split(h: torch.Tensor, cfg: QuantConfig, world: int, mine: list, gather):
+    """Attempt 0 of the damped inverse-Cholesky factor with the top split's
+    products divided by output rows over ``world`` ranks.
+
+    With B = J (H_perm + damp I) J (lower) split at n1 (``_split_n1``):
+    X11 = L11^-1 and X22 = L22^-1 are computed by every rank (``gq_inv_chol``);
+    L21 = B21 X11^T, T^T = L21 X11, the Schur update B22 -= L21 L21^T and
+    X21 = -X22 T^T are each computed for this rank's row slices (``mine``:
+    the rank indices whose slices this process computes) and combined by
+    ``gather(part, rows_per_rank)`` into all ranks' rows.  Those four
+    products are three quarters of the factor's flops.  Returns the factor
+    (U = J X J) and its device status word (0 = positive definite)."""
+    from . import gptq_ref as GR
+    GR._check_hessian(h, cfg)
+    d = h.shape[0]
+    st = A.stream()
+    call = GR._lib.call
+    perm = GR.act_order_perm(h, cfg.ordering_mode)
+    b = A.empty((d, d))
+    mean = A.empty((1,))
+    status = torch.zeros((1,), dtype=torch.int32, device="cuda")
+    call("gq_hessian_prepare", A.ptr(h), d, h.stride(0), A.ptr(perm), float(cfg.damp_percent), 0,
+         A.ptr(b), None, A.ptr(mean), st)
+    n1 = _split_n1(d)
+    n2 = d - n1
+    lib = GR._lib.lib()
+    ws = A.workspace(lib.gq_inv_chol_workspace_size(max(n1, n2)))
+    call("gq_inv_chol", A.ptr(b), n1, d, A.ptr(ws), ws.numel(), A.ptr(status), st)
+    per = -(-n2 // (world * 128)) * 128  # rows per rank, a multiple of 128
+
+    def span(r):
+        return min(n2, r * per), min(n2, (r + 1) * per)
+
+    def row_ptr(t, row, col=0):
+        return A.ptr(t[row:, col:]) if row < t.shape[0] else A.ptr(t)
+
+    def sgemm_tri(m, n, k, alpha, a, lda, bb, ldb, beta, c, ldc, tri):
+        if m > 0 and n > 0:
+            call("gq_sgemm_tri", 0, 1, m, n, k, float(alpha), a, lda, bb, ldb, float(beta), c,
+                 ldc, tri, st)
+
+    xt = b[:n1, :n1].t().contiguous()            # X11^T (upper)
+    # 1. L21 = B21 X11^T (B operand lower: tri 3)
+    parts = {}
+    for r in mine:
+        r0, r1 = span(r)
+        out = torch.zeros((per, n1), dtype=torch.float32, device="cuda")
+        sgemm_tri(r1 - r0, n1, n1, 1.0, row_ptr(b, n1 + r0), d, A.ptr(b), d, 0.0, A.ptr(out), n1, 3)
+        parts[r] = out
+    l21 = gather(parts, per)[:n2]                 # [n2, n1]
+    # 2. T^T = L21 X11 (B = X11^T upper: tri 4)
+    parts = {}
+    for r in mine:
+        r0, r1 = span(r)
+        out = torch.zeros((per, n1), dtype=torch.float32, device="cuda")
+        sgemm_tri(r1 - r0, n1, n1, 1.0, row_ptr(l21, r0), n1, A.ptr(xt), n1, 0.0, A.ptr(out), n1,
+                  4)
+        parts[r] = out
+    tt = gather(parts, per)[:n2].t().contiguous()  # T [n1, n2]
+    # 3. B22 -= L21 L21^T on this rank's rows: columns left of its diagonal
+    #    block in full, the diagonal block's lower tiles
+    parts = {}
+    for r in mine:
+        r0, r1 = span(r)
+        if r1 > r0 and r0 > 0:
+            call("gq_sgemm", 0, 1, r1 - r0, r0, n1, -1.0, row_ptr(l21, r0), n1, A.ptr(l21), n1,
+                 1.0, row_ptr(b, n1 + r0, n1), d, 0, st)
+        if r1 > r0:
+            call("gq_sgemm", 0, 1, r1 - r0, r1 - r0, n1, -1.0, row_ptr(l21, r0), n1,
+                 row_ptr(l21, r0), n1, 1.0, row_ptr(b, n1 + r0, n1 + r0), d, 1, st)
+        out = torch.zeros((per, n2), dtype=torch.float32, device="cuda")
+        out[:r1 - r0] = b[n1 + r0:n1 + r1, n1:]
+        parts[r] = out
+    b[n1:, n1:] = gather(parts, per)[:n2]
+    # 4. X22 = L22^-1 (every rank)
+    call("gq_inv_chol", row_ptr(b, n1, n1), n2, d, A.ptr(ws), ws.numel(), A.ptr(status), st)
+    # 5. X21 = -X22 T^T: a row slice of the lower X22 has no triangle of its own (tri 0)
+    parts = {}
+    for r in mine:
+        r0, r1 = span(r)
+        out = torch.zeros((per, n1), dtype=torch.float32, device="cuda")
+        sgemm_tri(r1 - r0, n1, n2, -1.0, row_ptr(b, n1 + r0, n1), d, A.ptr(tt), n2, 0.0,
+                  A.ptr(out), n1, 0)
+        parts[r] = out
+    b[n1:, :n1] = gather(parts, per)[:n2]
+    u = A.empty((d, d))
+    call("gq_reverse_lower", A.ptr(b), d, d, A.ptr(u), d, st)
+    return GR.HessianFactor(u, perm, 0, None), status
+
+
+def factor_hessian_sharded_attempt0(h: torch.Tensor, cfg: QuantConfig, group=None):
+    """Attempt 0 of the damped factor (``gptq_ref.factor_hessian_attempt0``)
+    with its top-level products split across the ranks of ``group``: every
+    rank passes the same (all-reduced) H and gets the same factor.  Hessians
+    narrower than ``FACTOR_SHARD_MIN_D`` or a single rank use the unsplit
+    factor.  Returns ``(factor, status)``; a non-zero status (damping too
+    small) is the same on every rank, which then redo the group with the
+    retrying factor."""
+    from .gptq_ref import factor_hessian_attempt0
+    rank, world = rank_world(group)
+    if world == 1 or h.shape[0] < FACTOR_SHARD_MIN_D:
+        return factor_hessian_attempt0(h, cfg)
+    fgroup = _factor_group(group)
+
+    def gather(parts, per):
+        part = parts[rank]
+        full = torch.empty((per * world,) + tuple(part.shape[1:]), dtype=part.dtype,
+                           device=part.device)
+        _collective("all_gather", lambda: _dist().all_gather_into_tensor(full, part, group=fgroup))
+        return full
+
+    return _factor_top_split(h, cfg, world, [rank], gather)
+
+
+def factor_hessian_split_emulated(h: torch.Tensor, cfg: QuantConfig, world: int):
+    """The sharded factor's arithmetic on one GPU: every rank's row slices
+    computed in turn and concatenated instead of all-gathered (for tests)."""
+    def gather(parts, per):
+        return torch.cat([parts[r] for r in range(world)], dim=0)
+    return _factor_top_split(A.to_device(h), cfg, world, list(range(world)), gather)
+
+
 def _members(shapes, grp):
     return [(name, m) for name, m, _, g in shapes if g == grp]
 
@@ -243,8 +392,8 @@ def _stacked(weights: dict, members) -> torch.Tensor:
 
 
 def quantize_layer_gptq_sharded(weights: dict, inputs_local: dict, cfg: QuantConfig, shapes,
-                                group=None, gather: bool = True,
-                                concurrent: bool = True) -> dict[str, SweepResult]:
+                                group=None, gather: bool = True, concurrent: bool = True,
+                                shard_factor: bool = True) -> dict[str, SweepResult]:
     """GPTQ for one layer set spread over the ranks of ``group``.
 
     ``inputs_local[grp]``: this rank's token shard of the group's activations.
@@ -261,9 +410,14 @@ def quantize_layer_gptq_sharded(weights: dict, inputs_local: dict, cfg: QuantCon
     stream that waits for that all-reduce, while the current stream goes on
     to the next group's partial H.  The factor's first damping attempt reads
     no status on the host; a group that needed more damping is redone at the
-    end.  The results equal the sequential order bit for bit."""
+    end.  With ``shard_factor`` the factors of Hessians at least
+    ``FACTOR_SHARD_MIN_D`` wide split their top-level products across the
+    ranks (``factor_hessian_sharded_attempt0``); every rank still ends with the
+    same factor.  The results equal the sequential order bit for bit."""
     rank, world = rank_world(group)
     out: dict[str, SweepResult] = {}
+    if shard_factor and world > 1:
+        _factor_group(group)  # created before any collective is in flight
     if concurrent:
         from . import layerset as LS
         from .gptq_ref import factor_hessian_attempt0
@@ -280,6 +434,8 @@ def quantize_layer_gptq_sharded(weights: dict, inputs_local: dict, cfg: QuantCon
         def prepare(grp, h):
             if works.get(grp) is not None:
                 works[grp].wait()  # the side stream (current here) waits for the all-reduce
+            if shard_factor:
+                return factor_hessian_sharded_attempt0(h, cfg, group)
             return factor_hessian_attempt0(h, cfg)
 
         def rows(grp):
@@ -394,7 +550,8 @@ class CommHandle:
 
 
 __all__ = [
-    "SWEEP_ROW_ALIGN", "RankFailure", "Heartbeat", "rank_world", "shard_range", "lpt_assign", "layer_set_cost",
+    "SWEEP_ROW_ALIGN", "RankFailure", "Heartbeat", "FACTOR_SHARD_MIN_D",
+    "factor_hessian_sharded_attempt0", "factor_hessian_split_emulated", "rank_world", "shard_range", "lpt_assign", "layer_set_cost",
     "allreduce_sum_", "gather_rows", "hessians_token_sharded", "quantize_layer_gptq_sharded",
     "layer_sets_for_rank", "tokens_for_rank", "CommHandle",
 ]

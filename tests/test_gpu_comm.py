@@ -88,3 +88,54 @@ def test_single_rank_check_then_abort():
             h.check()
     finally:
         h.close()
+
+
+def _factor_rank(rank, world, port, out_dir):
+    import datetime
+    import torch.distributed as dist
+    from jax_gptq_b200 import layerset as LS
+    from jax_gptq_b200.config import QuantConfig
+    from jax_gptq_b200.gptq_ref import factor_hessian
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    torch.cuda.set_device(rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world,
+                            timeout=datetime.timedelta(seconds=120),
+                            device_id=torch.device("cuda", rank))
+    try:
+        x = LS.synth_activations(8192, 4096, 31)[0]
+        h = torch.empty((4096, 4096), dtype=torch.float32, device="cuda")
+        stats.syrk_into(h, x, accumulate=False)
+        cfg = QuantConfig(w_bits=4, group_size=128, ordering_mode="diag_h", semantics="intended")
+        f, status = D.factor_hessian_sharded_attempt0(h, cfg)
+        torch.cuda.synchronize()
+        whole = factor_hessian(h, cfg)
+        rel = (torch.linalg.norm(f.u - whole.u) / torch.linalg.norm(whole.u)).item()
+        with open(os.path.join(out_dir, f"f{rank}.pkl"), "wb") as fh:
+            pickle.dump({"status": int(status.item()), "rel": rel,
+                         "u": f.u.cpu().numpy(), "perm_equal": bool(f.perm.equal(whole.perm))}, fh)
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two GPUs")
+def test_two_gpu_split_factor(tmp_path):
+    """The factor with its top-level products split across two GPUs (NCCL
+    all-gathers): the same U on both ranks, bit for bit, within 1e-5 of the
+    unsplit factor."""
+    import socket
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        port = s.getsockname()[1]
+    world = 2
+    ctx = mp.get_context("spawn")
+    procs = [ctx.Process(target=_factor_rank, args=(r, world, port, str(tmp_path)))
+             for r in range(world)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(180)
+        assert p.exitcode == 0, p.exitcode
+    outs = [pickle.load(open(tmp_path / f"f{r}.pkl", "rb")) for r in range(world)]
+    for o in outs:
+        assert o["status"] == 0 and o["perm_equal"] and o["rel"] <= 1e-5, o["rel"]
+    assert np.array_equal(outs[0]["u"], outs[1]["u"])

@@ -92,3 +92,22 @@ def test_empty_row_shard_still_writes_group_indices():
     empty = gptq_sweep(w[r0:r1], f.u, f.perm, cfg)
     assert empty.dequant.shape == (0, 512)
     assert empty.g_idx.equal(whole.g_idx)
+
+
+@pytest.mark.parametrize("world", [1, 2, 3, 8])
+def test_split_factor_matches_the_whole_factor(world):
+    """The factor with its top-level products split by rows over `world`
+    ranks (emulated on one GPU: every slice computed in turn) equals the
+    unsplit factor to float32 rounding: same permutation, U upper
+    triangular, within 1e-5 relative."""
+    x = LS.synth_activations(8192, 2560, 21)[0]
+    h = torch.empty((2560, 2560), dtype=torch.float32, device="cuda")
+    stats.syrk_into(h, x, accumulate=False)
+    cfg = QuantConfig(w_bits=4, group_size=128, ordering_mode="diag_h", semantics="intended")
+    whole = factor_hessian(h, cfg)
+    split, status = D.factor_hessian_split_emulated(h, cfg, world)
+    assert int(status.item()) == 0
+    assert split.perm.equal(whole.perm)
+    assert torch.equal(torch.tril(split.u, -1), torch.zeros_like(split.u))
+    rel = (torch.linalg.norm(split.u - whole.u) / torch.linalg.norm(whole.u)).item()
+    assert rel <= 1e-5, rel
