@@ -736,8 +736,22 @@ def run_ours(args, world, rank, local):
         b.record()
         _barrier(world)
         e2e_ms = _max_over_ranks(a.elapsed_time(b) / args.steps, world)
+        # the link's own rate for pinned host-to-device copies of the largest
+        # input (the step's lower bound is its h2d bytes at this rate)
+        big = max(x_host.values(), key=lambda t: t.numel())
+        dev = torch.empty(big.shape, dtype=big.dtype, device="cuda")
+        dev.copy_(big, non_blocking=True)
+        a.record()
+        for _ in range(3):
+            dev.copy_(big, non_blocking=True)
+        b.record()
+        torch.cuda.synchronize()
+        link_gbs = 3 * big.numel() * big.element_size() / (a.elapsed_time(b) / 1e3) / 1e9
+        del dev
         e2e = {"value": e2e_ms / 1000.0 / world, "unit": "s/layer",
-               "h2d_bytes_per_step": nbytes["h2d"], "d2h_bytes_per_step": nbytes["d2h"]}
+               "h2d_bytes_per_step": nbytes["h2d"], "d2h_bytes_per_step": nbytes["d2h"],
+               "h2d_link_gbs": link_gbs,
+               "h2d_bound_s_per_step": nbytes["h2d"] / (link_gbs * 1e9)}
         del w_host, x_host
 
     # --- Qronos on the same layer set (3-bit), Xt = X + N(0, (0.05 sigma_c)^2)

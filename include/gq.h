@@ -48,6 +48,15 @@ int gq_set_cta_budget(int n);
  * form runs regardless. */
 int gq_set_pair_kernels(int enable);
 
+/* Rows per CTA of the GPTQ sweep's block step, for sweeps launched
+ * afterwards (process-wide): r groups of 32 rows share one CTA and one staged
+ * copy of the block's U band (r = 1, 2 or 4); 0 (default) picks by row count
+ * (one group while such CTAs fit in one wave on the device, four while those
+ * do, else the one-warp form); -1 forces the one-warp form.  Every form gives
+ * the same bits; more groups per CTA leave more SMs to work on other
+ * streams.  GQ_EINVAL for any other value. */
+int gq_set_sweep_row_groups(int r);
+
 /* Library version (major*10000 + minor*100 + patch). */
 int gq_version(void);
 

@@ -29,6 +29,7 @@ SIGNATURES = {
     "gq_last_error": (ctypes.c_char_p, []),
     "gq_launch_count": (ctypes.c_longlong, []),
     "gq_set_cta_budget": (c_int, [c_int]),
+    "gq_set_sweep_row_groups": (c_int, [c_int]),
     "gq_set_pair_kernels": (c_int, [c_int]),
     "gq_packed_words": (c_int64, [c_int64, c_int]),
     "gq_pack_codes": (c_int, [_P, c_int64, c_int64, c_int64, c_int, _P, c_int64, _P]),

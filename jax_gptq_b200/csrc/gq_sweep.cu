@@ -20,7 +20,8 @@
 //      block in a shared-memory row buffer) and writes codes, dequantized
 //      values and scaled errors (w - dq) / U_ii into its 128 columns of err.
 //      sweep_rows_kernel runs it on four warps per 32 rows (one for the
-//      column chain, three applying finished sub-blocks' errors ahead of it);
+//      column chain, three applying finished sub-blocks' errors ahead of it),
+//      with 1, 2 or 4 such row groups per CTA sharing one staged band;
 //      sweep_rows1_kernel, on one warp, serves grids too large for one wave
 //      of those CTAs;
 //   3. near update: wp[:, b1:s1] -= err[:, b0-s0:b1-s0] @ U[b0:b1, b1:s1].
@@ -132,20 +133,22 @@ __device__ __forceinline__ void sweep_group_params(const SweepArgs& a, int64_t r
   }
 }
 
-// One 128-column block of the sweep for 32 rows: lane l of every warp works on
-// row 32 * blockIdx.x + l.  Columns are taken in sub-blocks of 32.  Warp 0
-// runs the serial part: the sub-block's columns one by one in registers, each
-// column's scaled error applied at once to the later columns of the
-// sub-block (U tile broadcast from shared memory).  The sub-block's 32 errors
-// must then reach the block's remaining columns, which live in a shared-memory
-// row buffer (one column of 32 rows per ws row):
-//   critical: all four warps update the next sub-block's columns (the whole
-//             next group when a 64-column group starts there), then warp 0
-//             goes on;
-//   look-ahead: while warp 0 works on that sub-block, warps 1-3 update the
-//             columns beyond it, store the previous sub-block's dequantized
-//             values, errors and codes, and stage the U tiles warp 0 and the
-//             next critical step read.
+// One 128-column block of the sweep for R groups of 32 rows: lane l of every
+// warp of row group g works on row 32 (R blockIdx.x + g) + l.  Columns are
+// taken in sub-blocks of 32.  Per group, the warp of role 0 runs the serial
+// part: the sub-block's columns one by one in registers, each column's scaled
+// error applied at once to the later columns of the sub-block (U tile
+// broadcast from shared memory).  The sub-block's 32 errors must then reach
+// the block's remaining columns, which live in the group's shared-memory row
+// buffer (one column of 32 rows per ws row):
+//   critical: the group's four warps update the next sub-block's columns (the
+//             whole next group when a 64-column group starts there), then
+//             role 0 goes on;
+//   look-ahead: while role 0 works on that sub-block, roles 1-3 update the
+//             columns beyond it and store the previous sub-block's
+//             dequantized values, errors and codes; the look-ahead warps of
+//             all groups together stage the U tiles the chains and the next
+//             critical step read.
 // Every column still receives the updates of all earlier columns in
 // increasing order, one fmaf each, so the result does not depend on the
 // split.  G: group size when it divides 128 (4..128), 0 when groups span
@@ -157,6 +160,16 @@ constexpr int SR_CP = 2 * SW_SUB + 4;  // pitch of the critical U tile (up to 64
 // us[j * SW_BLOCK + i] = U[b0 + i][b0 + j] for i <= j (the zero triangle is
 // not copied and never read).
 constexpr size_t SR_BAND_BYTES = (size_t)SW_BLOCK * SW_BLOCK * 4;  // 64 KB
+// Per row group of 32 rows: the row buffer ws, two sub-blocks of errors es and
+// of packed codes cs (16-byte multiples, so every group's buffers stay aligned).
+constexpr size_t SR_WS_BYTES = (size_t)SW_BLOCK * SW_WP * 4;        // 16,896
+constexpr size_t SR_ES_BYTES = (size_t)2 * SW_SUB * SW_WP * 4;      // 8,448
+constexpr size_t SR_CS_BYTES = (size_t)2 * (SW_SUB / 4) * 32 * 4;  // 2,048
+constexpr size_t SR_GROUP_BYTES = SR_WS_BYTES + SR_ES_BYTES + SR_CS_BYTES;
+static_assert(SR_WS_BYTES % 16 == 0 && SR_ES_BYTES % 16 == 0 && SR_CS_BYTES % 16 == 0,
+              "row-group buffers must keep 16-byte alignment");
+// dynamic shared memory of a block step with R row groups per CTA
+constexpr size_t sr_smem_bytes(int r) { return SR_BAND_BYTES + (size_t)r * SR_GROUP_BYTES; }
 
 __device__ __forceinline__ void cp_async16(void* smem_dst, const void* gmem_src) {
   asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(
@@ -165,19 +178,27 @@ __device__ __forceinline__ void cp_async16(void* smem_dst, const void* gmem_src)
                : "memory");
 }
 
-template <int G>
-__global__ void __launch_bounds__(SR_THREADS) sweep_rows_kernel(SweepArgs a) {
+template <int G, int R>
+__global__ void __launch_bounds__(SR_THREADS * R) sweep_rows_kernel(SweepArgs a) {
   constexpr int GD = (G > 0) ? G : 1;  // divisor-safe group size for the G = 0 instance
-  extern __shared__ __align__(16) float us[];             // the band, see SR_BAND_BYTES
-  __shared__ float ws[SW_BLOCK * SW_WP];                  // ws[j][lane]: column j of the rows
+  // dynamic: the band (SR_BAND_BYTES), then each row group's buffers (SR_GROUP_BYTES)
+  extern __shared__ __align__(16) float us[];
   __shared__ __align__(16) float tile[2][SW_SUB * SW_TP];  // U inside sub-block s, [k][t]
   __shared__ __align__(16) float ucrit[SW_SUB * SR_CP];    // U rows of sub-block s, critical columns
   __shared__ float rinv[SW_BLOCK];
-  __shared__ float es[2][SW_SUB * SW_WP];                 // errors of sub-block s, [k][lane]
-  __shared__ uint32_t cs[2][(SW_SUB / 4) * 32];           // packed codes of sub-block s
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int wid = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  // row group grp = warps 4 grp .. 4 grp + 3; its column-chain warp (role 0)
+  // is warp 4 grp + grp % 4, so the R chains sit on different schedulers
+  const int grp = wid >> 2;
+  const int warp = (wid - grp) & 3;
+  char* gbase = reinterpret_cast<char*>(us) + SR_BAND_BYTES + (size_t)grp * SR_GROUP_BYTES;
+  float* ws = reinterpret_cast<float*>(gbase);            // ws[j][lane]: column j of the rows
+  float (*es)[SW_SUB * SW_WP] =                           // errors of sub-block s, [k][lane]
+      reinterpret_cast<float (*)[SW_SUB * SW_WP]>(gbase + SR_WS_BYTES);
+  uint32_t (*cs)[(SW_SUB / 4) * 32] =                     // packed codes of sub-block s
+      reinterpret_cast<uint32_t (*)[(SW_SUB / 4) * 32]>(gbase + SR_WS_BYTES + SR_ES_BYTES);
   const int bw = a.bw;
-  const int64_t row = (int64_t)blockIdx.x * 32 + lane;
+  const int64_t row = ((int64_t)blockIdx.x * R + grp) * 32 + lane;
   const bool valid = row < a.m;
   float* wrow = valid ? a.wp + row * a.ldp + a.b0 : nullptr;
   const int nsub = (bw + SW_SUB - 1) / SW_SUB;
@@ -279,7 +300,8 @@ __global__ void __launch_bounds__(SR_THREADS) sweep_rows_kernel(SweepArgs a) {
 
   // ---- prologue (all warps): the band (asynchronously), the row block,
   // reciprocal pivots, the first tiles
-  for (int c = threadIdx.x; c < bw * (SW_BLOCK / 4); c += SR_THREADS) {
+  constexpr int NT = SR_THREADS * R;
+  for (int c = threadIdx.x; c < bw * (SW_BLOCK / 4); c += NT) {
     const int j = c / (SW_BLOCK / 4), q = c % (SW_BLOCK / 4);
     if (4 * q <= j) cp_async16(us + j * SW_BLOCK + 4 * q, a.ubt + (int64_t)j * a.ldub + 4 * q);
   }
@@ -306,9 +328,9 @@ __global__ void __launch_bounds__(SR_THREADS) sweep_rows_kernel(SweepArgs a) {
   }
   asm volatile("cp.async.wait_group 0;" ::: "memory");
   __syncthreads();
-  for (int i = threadIdx.x; i < SW_BLOCK; i += SR_THREADS)
+  for (int i = threadIdx.x; i < SW_BLOCK; i += NT)
     rinv[i] = (i < bw) ? 1.f / us[i * SW_BLOCK + i] : 0.f;
-  stage_tile(0, threadIdx.x, SR_THREADS);
+  stage_tile(0, threadIdx.x, NT);
   float scale = 1.f, zero = 0.f;  // warp 0: the current group's parameters
   if (G == 0 && valid) {
     scale = a.big_scale[row];
@@ -388,8 +410,9 @@ __global__ void __launch_bounds__(SR_THREADS) sweep_rows_kernel(SweepArgs a) {
 #pragma unroll
       for (int q = 0; q < SW_SUB / 4; ++q) cs[s & 1][q * 32 + lane] = cw[q];
     } else {
-      // ---- look-ahead (warps 1-3)
-      const int lw = warp - 1, lt = threadIdx.x - 32;
+      // ---- look-ahead (roles 1-3 of every row group; the U tiles are
+      // staged by the look-ahead warps of all groups together)
+      const int lw = warp - 1, lt = (grp * 3 + lw) * 32 + lane;
       if (s > 0) {
         // sub-block s-1's errors reach the columns past its critical update
         float ev[SW_SUB];
@@ -400,8 +423,8 @@ __global__ void __launch_bounds__(SR_THREADS) sweep_rows_kernel(SweepArgs a) {
           update_cols_from_band(ev, SW_SUB * (s - 1), j, LW, min(4, (bw - j + LW - 1) / LW));
         store_sub(s - 1, lw, SR_THREADS / 32 - 1);
       }
-      if (s + 1 < nsub) stage_tile(s + 1, lt, SR_THREADS - 32);
-      stage_crit(s, lt, SR_THREADS - 32);
+      if (s + 1 < nsub) stage_tile(s + 1, lt, (SR_THREADS - 32) * R);
+      stage_crit(s, lt, (SR_THREADS - 32) * R);
     }
     __syncthreads();
     // ---- critical: sub-block s's errors reach the next critical columns (all warps)
@@ -691,32 +714,65 @@ int sweep_shape_ok(const char* who, int64_t m, int64_t n) {
 int transpose2d(const float* src, int64_t rows, int64_t cols, int64_t lds, float* dst, int64_t ldd,
                 cudaStream_t st);
 
-// The four-warp block step takes its band in dynamic shared memory above the
-// default 48 KB; allow it once per (device, instance).
-template <int G>
-static int allow_band_smem() {
+// Row groups per CTA of the four-warp block step (gq_set_sweep_row_groups):
+// 0 picks by row count, 1, 2 or 4 force that many, -1 forces the one-warp
+// kernel.
+static int g_row_groups = 0;
+
+// The four-warp block step takes the band and its row groups' buffers in
+// dynamic shared memory above the default 48 KB; allowed once per (device,
+// instance).
+template <int G, int R>
+static int launch_rows4(const SweepArgs& a, unsigned grid, cudaStream_t st) {
   static int done_dev = -1;
   int dev = 0;
   GQ_CHECK_CUDA(cudaGetDevice(&dev));
   if (done_dev != dev) {
-    GQ_CHECK_CUDA(cudaFuncSetAttribute(sweep_rows_kernel<G>,
+    GQ_CHECK_CUDA(cudaFuncSetAttribute(sweep_rows_kernel<G, R>,
                                        cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                       (int)SR_BAND_BYTES));
+                                       (int)sr_smem_bytes(R)));
     done_dev = dev;
+  }
+  sweep_rows_kernel<G, R><<<grid, SR_THREADS * R, sr_smem_bytes(R), st>>>(a);
+  return GQ_OK;
+}
+
+template <int R>
+static int launch_rows4_g(int group_size, const SweepArgs& a, unsigned grid, cudaStream_t st) {
+  switch (group_size) {
+    case 4: return launch_rows4<4, R>(a, grid, st);
+    case 8: return launch_rows4<8, R>(a, grid, st);
+    case 16: return launch_rows4<16, R>(a, grid, st);
+    case 32: return launch_rows4<32, R>(a, grid, st);
+    case 64: return launch_rows4<64, R>(a, grid, st);
+    case 128: return launch_rows4<128, R>(a, grid, st);
+    default: return launch_rows4<0, R>(a, grid, st);
+  }
+}
+
+static int launch_rows1_g(int group_size, const SweepArgs& a, unsigned grid, cudaStream_t st) {
+  switch (group_size) {
+    case 4: sweep_rows1_kernel<4><<<grid, 32, 0, st>>>(a); break;
+    case 8: sweep_rows1_kernel<8><<<grid, 32, 0, st>>>(a); break;
+    case 16: sweep_rows1_kernel<16><<<grid, 32, 0, st>>>(a); break;
+    case 32: sweep_rows1_kernel<32><<<grid, 32, 0, st>>>(a); break;
+    case 64: sweep_rows1_kernel<64><<<grid, 32, 0, st>>>(a); break;
+    case 128: sweep_rows1_kernel<128><<<grid, 32, 0, st>>>(a); break;
+    default: sweep_rows1_kernel<0><<<grid, 32, 0, st>>>(a); break;
   }
   return GQ_OK;
 }
 
-int sweep_rows_smem_setup(int group_size) {
-  switch (group_size) {
-    case 4: return allow_band_smem<4>();
-    case 8: return allow_band_smem<8>();
-    case 16: return allow_band_smem<16>();
-    case 32: return allow_band_smem<32>();
-    case 64: return allow_band_smem<64>();
-    case 128: return allow_band_smem<128>();
-    default: return allow_band_smem<0>();
-  }
+// Row groups per CTA for m rows on `sms` SMs; 0 selects the one-warp kernel.
+// One group per CTA (110 KB of shared memory, two CTAs per SM) while those
+// fit in one wave; four (194 KB, one per SM) while those do; beyond that the
+// one-warp kernel, whose 34 KB CTAs keep a wave of them resident.
+static int pick_row_groups(int64_t m, int sms) {
+  if (g_row_groups != 0) return g_row_groups < 0 ? 0 : g_row_groups;
+  const int64_t rows32 = ceil_div(m, 32);
+  if (rows32 <= 2 * (int64_t)sms) return 1;
+  if (rows32 <= 4 * (int64_t)sms) return 4;
+  return 0;
 }
 
 }  // namespace gq
@@ -724,6 +780,13 @@ int sweep_rows_smem_setup(int group_size) {
 extern "C" {
 
 int64_t gq_gptq_sweep_workspace_size(int64_t m, int64_t n) { return gq::sweep_ws_bytes(m, n); }
+
+int gq_set_sweep_row_groups(int r) {
+  GQ_REQUIRE(r == -1 || r == 0 || r == 1 || r == 2 || r == 4,
+             "gq_set_sweep_row_groups: %d is not one of -1, 0, 1, 2, 4", r);
+  gq::g_row_groups = r;
+  return GQ_OK;
+}
 
 int gq_gptq_sweep(const float* w, int64_t m, int64_t n, int64_t ldw, const float* start,
                   const float* u, int64_t ldu, const int32_t* perm, int w_bits, int group_size,
@@ -787,13 +850,11 @@ int gq_gptq_sweep(const float* w, int64_t m, int64_t n, int64_t ldw, const float
   a.group0_scale = group0_scale; a.group0_zero = group0_zero;
   a.big_scale = bscale; a.big_zero = bzero;
   a.scales = scales; a.zeros = zeros;
-  const unsigned grid = (unsigned)ceil_div(m, 32);
-  // the four-warp block step while its CTAs (four per SM) fit in one wave
   int dev = 0, sms = 0;
   GQ_CHECK_CUDA(cudaGetDevice(&dev));
   GQ_CHECK_CUDA(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
-  const bool four_warps = grid <= (unsigned)(4 * sms);
-  if (four_warps) GQ_TRY(sweep_rows_smem_setup(group_size));
+  const int row_groups = pick_row_groups(m, sms);
+  const unsigned grid = (unsigned)ceil_div(m, 32 * (int64_t)std::max(1, row_groups));
   for (int64_t b0 = 0; b0 < n; b0 += SW_BLOCK) {
     const int bw = (int)std::min<int64_t>(SW_BLOCK, n - b0);
     if (group_size > SW_BLOCK && b0 % group_size == 0) {
@@ -825,27 +886,11 @@ int gq_gptq_sweep(const float* w, int64_t m, int64_t n, int64_t ldw, const float
       GQ_TRY(transpose2d(u + s0 * ldu + s0, s1 - s0, n - s0, ldu, ubt, super_w, st));
     }
     a.ubt = ubt + (b0 - s0) * super_w + (b0 - s0);
-    if (four_warps) {
-      const size_t band = SR_BAND_BYTES;
-      switch (group_size) {
-        case 4: sweep_rows_kernel<4><<<grid, SR_THREADS, band, st>>>(a); break;
-        case 8: sweep_rows_kernel<8><<<grid, SR_THREADS, band, st>>>(a); break;
-        case 16: sweep_rows_kernel<16><<<grid, SR_THREADS, band, st>>>(a); break;
-        case 32: sweep_rows_kernel<32><<<grid, SR_THREADS, band, st>>>(a); break;
-        case 64: sweep_rows_kernel<64><<<grid, SR_THREADS, band, st>>>(a); break;
-        case 128: sweep_rows_kernel<128><<<grid, SR_THREADS, band, st>>>(a); break;
-        default: sweep_rows_kernel<0><<<grid, SR_THREADS, band, st>>>(a); break;
-      }
-    } else {
-      switch (group_size) {
-        case 4: sweep_rows1_kernel<4><<<grid, 32, 0, st>>>(a); break;
-        case 8: sweep_rows1_kernel<8><<<grid, 32, 0, st>>>(a); break;
-        case 16: sweep_rows1_kernel<16><<<grid, 32, 0, st>>>(a); break;
-        case 32: sweep_rows1_kernel<32><<<grid, 32, 0, st>>>(a); break;
-        case 64: sweep_rows1_kernel<64><<<grid, 32, 0, st>>>(a); break;
-        case 128: sweep_rows1_kernel<128><<<grid, 32, 0, st>>>(a); break;
-        default: sweep_rows1_kernel<0><<<grid, 32, 0, st>>>(a); break;
-      }
+    switch (row_groups) {
+      case 1: GQ_TRY(launch_rows4_g<1>(group_size, a, grid, st)); break;
+      case 2: GQ_TRY(launch_rows4_g<2>(group_size, a, grid, st)); break;
+      case 4: GQ_TRY(launch_rows4_g<4>(group_size, a, grid, st)); break;
+      default: GQ_TRY(launch_rows1_g(group_size, a, grid, st)); break;
     }
     GQ_TRY(check_launch("sweep_rows"));
     const int64_t b1 = b0 + bw;

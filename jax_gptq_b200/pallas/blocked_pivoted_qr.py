@@ -348,6 +348,10 @@ def benchmark(n: int = 4096, panel: int = 64, reps: int = 2, seed: int = 1,
             q_err = _residual_dev(mat, res)
             entry["residual"] = q_err
             entry.update(numerical_rank(res.work))
+            # smallest-norm-first pivoting moves dependent columns to the
+            # front while their residual norms are still large, so R's
+            # diagonal does not reveal the rank in that mode
+            entry["rank_revealing"] = mode == "largest"
         out[label] = entry
     return out
 

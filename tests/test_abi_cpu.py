@@ -99,6 +99,15 @@ def test_pair_kernel_switch_validates_its_argument():
     assert lib.gq_set_pair_kernels(2) != 0
 
 
+def test_sweep_row_group_switch_validates_its_argument():
+    lib = _lib.lib()
+    for r in (-1, 1, 2, 4, 0):
+        assert lib.gq_set_sweep_row_groups(r) == 0
+    for r in (3, 5, -2, 8):
+        assert lib.gq_set_sweep_row_groups(r) == _lib.GQ_EINVAL
+    assert lib.gq_set_sweep_row_groups(0) == 0
+
+
 def test_factor_from_activations_validates_before_launching():
     lib = _lib.lib()
     p = ctypes.c_void_p(256)

@@ -232,10 +232,37 @@ def test_sweep_codes_match_float32_oracle_up_to_rounding_ties(m, n, bits, g):
     assert np.array_equal(res.g_idx.cpu().numpy(), ref["g_idx"])
 
 
+@pytest.mark.parametrize("m,n,g", [(300, 1152, 128), (300, 1000, 8), (200, 1536, 256),
+                                   (97, 640, 32), (640, 512, 64)])
+def test_sweep_block_step_forms_agree(m, n, g):
+    """The block step's forms (one warp per 32 rows; four warps per 32 rows
+    with 1, 2 or 4 row groups sharing one CTA's staged U band) apply the same
+    updates in the same order to every row, so they give the same bits, also
+    for ragged row counts (a partly filled last CTA) and ragged blocks."""
+    from jax_gptq_b200 import _lib
+    rng = np.random.default_rng(m + n + g)
+    x = (rng.standard_normal((2 * n, n)) * rng.lognormal(0, 1, n)).astype(np.float32)
+    cfg = QuantConfig(w_bits=4, group_size=g, ordering_mode="diag_h", semantics="intended")
+    f = G.factor_hessian((x.T @ x).astype(np.float32), cfg)
+    w = torch.from_numpy((rng.standard_normal((m, n)) * 0.02).astype(np.float32)).cuda()
+    lib = _lib.lib()
+    outs = {}
+    try:
+        for r in (-1, 1, 2, 4):
+            assert lib.gq_set_sweep_row_groups(r) == 0
+            outs[r] = G.gptq_sweep(w, f.u, f.perm, cfg)
+    finally:
+        lib.gq_set_sweep_row_groups(0)
+    for r in (1, 2, 4):
+        for key in ("dequant", "codes", "scales", "zeros", "g_idx"):
+            assert torch.equal(getattr(outs[-1], key), getattr(outs[r], key)), (r, key)
+
+
 def test_sweep_single_warp_and_four_warp_block_steps_agree():
-    """Grids larger than one wave of four-warp CTAs take the single-warp block
-    step; rows are independent, so sweeping halves of the rows (four-warp
-    step) must reproduce the whole sweep bit for bit."""
+    """Grids larger than one wave of four-group CTAs take the single-warp
+    block step; rows are independent, so sweeping halves of the rows (four
+    warps per 32 rows, four row groups per CTA) must reproduce the whole
+    sweep bit for bit."""
     sms = torch.cuda.get_device_properties(0).multi_processor_count
     m, n = 32 * (4 * sms + 8), 512
     rng = np.random.default_rng(5)
