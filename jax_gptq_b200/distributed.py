@@ -237,6 +237,10 @@ def hessians_token_sharded(inputs_local: dict[str, torch.Tensor], group=None,
 # across the ranks (factor_hessian_sharded_attempt0); smaller ones are factored
 # whole on every rank.
 FACTOR_SHARD_MIN_D = 2048
+# Below the top level, diagonal blocks at least this wide are split again
+# across the ranks; narrower ones are factored whole by every rank (their
+# products are too small to outweigh the all-gathers).
+FACTOR_SPLIT_MIN_N = 4096
 _FACTOR_GROUPS: dict = {}
 
 
@@ -260,18 +264,121 @@ def _split_n1(n: int, nb: int = 128) -> int:
     return n - nb if n1 >= n else n1
 
 
-def _factor_top_split(h: torch.Tensor, cfg: QuantConfig, world: int, mine: list, gather):
-    """Attempt 0 of the damped inverse-Cholesky factor with the top split's
-    products divided by output rows over ``world`` ranks.
+def _inv_chol_split(b: torch.Tensor, o: int, n: int, world: int, mine: list, gather,
+                    ws: torch.Tensor, status: torch.Tensor, min_split: int) -> None:
+    """In-place inverse Cholesky of the n x n lower block of ``b`` at
+    (o, o): on return it holds X = L^-1.  Split at n1 (``_split_n1``):
+    X11 and X22 come from this function again while at least ``min_split``
+    wide (else ``gq_inv_chol`` on every rank); L21 = B21 X11^T,
+    T^T = L21 X11, the Schur update B22 -= L21 L21^T and X21 = -X22 T^T are
+    each computed for this rank's row slices (``mine``: the rank indices
+    whose slices this process computes) and combined by
+    ``gather(part, rows_per_rank)`` into all ranks' rows.  At one level those
+    four products are three quarters of the block's flops."""
+    from . import gptq_ref as GR
+    st = A.stream()
+    call = GR._lib.call
+    d = b.shape[1]
+    if n < min_split:
+        call("gq_inv_chol", A.ptr(b[o:, o:]), n, d, A.ptr(ws), ws.numel(), A.ptr(status), st)
+        return
+    n1 = _split_n1(n)
+    n2 = n - n1
+    p1 = o + n1  # first row / column of the trailing block
+    _inv_chol_split(b, o, n1, world, mine, gather, ws, status, min_split)
+    # row slices: equal for the products whose rows cost the same (L21, T^T);
+    # for the lower-triangular outputs (Schur update, X21), whose row i costs
+    # about i, boundaries at n2 sqrt(r / world) give every rank the same work
+    flat = _row_spans(n2, world, triangular=False)
+    tri = _row_spans(n2, world, triangular=True)
 
-    With B = J (H_perm + damp I) J (lower) split at n1 (``_split_n1``):
-    X11 = L11^-1 and X22 = L22^-1 are computed by every rank (``gq_inv_chol``);
-    L21 = B21 X11^T, T^T = L21 X11, the Schur update B22 -= L21 L21^T and
-    X21 = -X22 T^T are each computed for this rank's row slices (``mine``:
-    the rank indices whose slices this process computes) and combined by
-    ``gather(part, rows_per_rank)`` into all ranks' rows.  Those four
-    products are three quarters of the factor's flops.  Returns the factor
-    (U = J X J) and its device status word (0 = positive definite)."""
+    def assemble(parts, spans, width):
+        pmax = max(r1 - r0 for r0, r1 in spans)
+        full = gather(parts, pmax)
+        return torch.cat([full[r * pmax:r * pmax + (r1 - r0)] for r, (r0, r1) in
+                          enumerate(spans)], dim=0) if len(spans) > 1 else full[:n2]
+
+    def slot(spans, width):
+        pmax = max(r1 - r0 for r0, r1 in spans)
+        return torch.zeros((pmax, width), dtype=torch.float32, device="cuda")
+
+    def row_ptr(t, row, col=0):
+        return A.ptr(t[row:, col:]) if row < t.shape[0] else A.ptr(t)
+
+    def sgemm_tri(m, nn, k, alpha, a, lda, bb, ldb, beta, c, ldc, tri_mode):
+        if m > 0 and nn > 0 and k > 0:
+            call("gq_sgemm_tri", 0, 1, m, nn, k, float(alpha), a, lda, bb, ldb, float(beta), c,
+                 ldc, tri_mode, st)
+
+    xt = b[o:p1, o:p1].t().contiguous()           # X11^T (upper)
+    # 1. L21 = B21 X11^T (B operand lower: tri 3)
+    parts = {}
+    for r in mine:
+        r0, r1 = flat[r]
+        out = slot(flat, n1)
+        sgemm_tri(r1 - r0, n1, n1, 1.0, row_ptr(b, p1 + r0, o), d, A.ptr(b[o:, o:]), d, 0.0,
+                  A.ptr(out), n1, 3)
+        parts[r] = out
+    l21 = assemble(parts, flat, n1)               # [n2, n1]
+    # 2. T^T = L21 X11 (B = X11^T upper: tri 4)
+    parts = {}
+    for r in mine:
+        r0, r1 = flat[r]
+        out = slot(flat, n1)
+        sgemm_tri(r1 - r0, n1, n1, 1.0, row_ptr(l21, r0), n1, A.ptr(xt), n1, 0.0, A.ptr(out), n1,
+                  4)
+        parts[r] = out
+    tt = assemble(parts, flat, n1).t().contiguous()  # T [n1, n2]
+    # 3. B22 -= L21 L21^T on this rank's rows: columns left of its diagonal
+    #    block in full, the diagonal block's lower tiles
+    parts = {}
+    for r in mine:
+        r0, r1 = tri[r]
+        if r1 > r0 and r0 > 0:
+            call("gq_sgemm", 0, 1, r1 - r0, r0, n1, -1.0, row_ptr(l21, r0), n1, A.ptr(l21), n1,
+                 1.0, row_ptr(b, p1 + r0, p1), d, 0, st)
+        if r1 > r0:
+            call("gq_sgemm", 0, 1, r1 - r0, r1 - r0, n1, -1.0, row_ptr(l21, r0), n1,
+                 row_ptr(l21, r0), n1, 1.0, row_ptr(b, p1 + r0, p1 + r0), d, 1, st)
+        out = slot(tri, n2)
+        out[:r1 - r0] = b[p1 + r0:p1 + r1, p1:o + n]
+        parts[r] = out
+    b[p1:o + n, p1:o + n] = assemble(parts, tri, n2)
+    # 4. X22 = L22^-1
+    _inv_chol_split(b, p1, n2, world, mine, gather, ws, status, min_split)
+    # 5. X21 = -X22 T^T: rows [r0, r1) of the lower X22 are zero past column
+    #    r1, so K stops there (no triangle of the call's own: tri 0)
+    parts = {}
+    for r in mine:
+        r0, r1 = tri[r]
+        out = slot(tri, n1)
+        sgemm_tri(r1 - r0, n1, r1, -1.0, row_ptr(b, p1 + r0, p1), d, A.ptr(tt), n2, 0.0,
+                  A.ptr(out), n1, 0)
+        parts[r] = out
+    b[p1:o + n, o:p1] = assemble(parts, tri, n1)
+
+
+def _row_spans(n: int, world: int, triangular: bool, nb: int = 128) -> list:
+    """Per rank, the rows [r0, r1) of an n-row product it computes: nb-aligned
+    boundaries, equal counts, or (``triangular``) at n sqrt(r / world) so
+    that the lower-triangular work (row i costs ~i) is split evenly."""
+    import math
+    bounds = [0]
+    for r in range(1, world):
+        x = n * (math.sqrt(r / world) if triangular else r / world)
+        bounds.append(min(n, max(bounds[-1], int(-(-round(x) // nb)) * nb)))
+    bounds.append(n)
+    return [(bounds[r], bounds[r + 1]) for r in range(world)]
+
+
+def _factor_top_split(h: torch.Tensor, cfg: QuantConfig, world: int, mine: list, gather,
+                      min_split: int | None = None):
+    """Attempt 0 of the damped inverse-Cholesky factor with its split
+    products divided by output rows over ``world`` ranks (``_inv_chol_split``
+    on B = J (H_perm + damp I) J, lower; blocks at least ``min_split`` wide,
+    default ``FACTOR_SPLIT_MIN_N``, are split again below the top level).
+    Returns the factor (U = J X J) and its device status word (0 = positive
+    definite)."""
     from . import gptq_ref as GR
     GR._check_hessian(h, cfg)
     d = h.shape[0]
@@ -283,68 +390,12 @@ def _factor_top_split(h: torch.Tensor, cfg: QuantConfig, world: int, mine: list,
     status = torch.zeros((1,), dtype=torch.int32, device="cuda")
     call("gq_hessian_prepare", A.ptr(h), d, h.stride(0), A.ptr(perm), float(cfg.damp_percent), 0,
          A.ptr(b), None, A.ptr(mean), st)
-    n1 = _split_n1(d)
-    n2 = d - n1
     lib = GR._lib.lib()
-    ws = A.workspace(lib.gq_inv_chol_workspace_size(max(n1, n2)))
-    call("gq_inv_chol", A.ptr(b), n1, d, A.ptr(ws), ws.numel(), A.ptr(status), st)
-    per = -(-n2 // (world * 128)) * 128  # rows per rank, a multiple of 128
-
-    def span(r):
-        return min(n2, r * per), min(n2, (r + 1) * per)
-
-    def row_ptr(t, row, col=0):
-        return A.ptr(t[row:, col:]) if row < t.shape[0] else A.ptr(t)
-
-    def sgemm_tri(m, n, k, alpha, a, lda, bb, ldb, beta, c, ldc, tri):
-        if m > 0 and n > 0:
-            call("gq_sgemm_tri", 0, 1, m, n, k, float(alpha), a, lda, bb, ldb, float(beta), c,
-                 ldc, tri, st)
-
-    xt = b[:n1, :n1].t().contiguous()            # X11^T (upper)
-    # 1. L21 = B21 X11^T (B operand lower: tri 3)
-    parts = {}
-    for r in mine:
-        r0, r1 = span(r)
-        out = torch.zeros((per, n1), dtype=torch.float32, device="cuda")
-        sgemm_tri(r1 - r0, n1, n1, 1.0, row_ptr(b, n1 + r0), d, A.ptr(b), d, 0.0, A.ptr(out), n1, 3)
-        parts[r] = out
-    l21 = gather(parts, per)[:n2]                 # [n2, n1]
-    # 2. T^T = L21 X11 (B = X11^T upper: tri 4)
-    parts = {}
-    for r in mine:
-        r0, r1 = span(r)
-        out = torch.zeros((per, n1), dtype=torch.float32, device="cuda")
-        sgemm_tri(r1 - r0, n1, n1, 1.0, row_ptr(l21, r0), n1, A.ptr(xt), n1, 0.0, A.ptr(out), n1,
-                  4)
-        parts[r] = out
-    tt = gather(parts, per)[:n2].t().contiguous()  # T [n1, n2]
-    # 3. B22 -= L21 L21^T on this rank's rows: columns left of its diagonal
-    #    block in full, the diagonal block's lower tiles
-    parts = {}
-    for r in mine:
-        r0, r1 = span(r)
-        if r1 > r0 and r0 > 0:
-            call("gq_sgemm", 0, 1, r1 - r0, r0, n1, -1.0, row_ptr(l21, r0), n1, A.ptr(l21), n1,
-                 1.0, row_ptr(b, n1 + r0, n1), d, 0, st)
-        if r1 > r0:
-            call("gq_sgemm", 0, 1, r1 - r0, r1 - r0, n1, -1.0, row_ptr(l21, r0), n1,
-                 row_ptr(l21, r0), n1, 1.0, row_ptr(b, n1 + r0, n1 + r0), d, 1, st)
-        out = torch.zeros((per, n2), dtype=torch.float32, device="cuda")
-        out[:r1 - r0] = b[n1 + r0:n1 + r1, n1:]
-        parts[r] = out
-    b[n1:, n1:] = gather(parts, per)[:n2]
-    # 4. X22 = L22^-1 (every rank)
-    call("gq_inv_chol", row_ptr(b, n1, n1), n2, d, A.ptr(ws), ws.numel(), A.ptr(status), st)
-    # 5. X21 = -X22 T^T: a row slice of the lower X22 has no triangle of its own (tri 0)
-    parts = {}
-    for r in mine:
-        r0, r1 = span(r)
-        out = torch.zeros((per, n1), dtype=torch.float32, device="cuda")
-        sgemm_tri(r1 - r0, n1, n2, -1.0, row_ptr(b, n1 + r0, n1), d, A.ptr(tt), n2, 0.0,
-                  A.ptr(out), n1, 0)
-        parts[r] = out
-    b[n1:, :n1] = gather(parts, per)[:n2]
+    n1 = _split_n1(d)
+    ws = A.workspace(lib.gq_inv_chol_workspace_size(max(n1, d - n1)))
+    inner = FACTOR_SPLIT_MIN_N if min_split is None else min_split
+    # the top level is always split (the caller checked the width)
+    _inv_chol_split(b, 0, d, world, mine, gather, ws, status, min(d, max(inner, 256)))
     u = A.empty((d, d))
     call("gq_reverse_lower", A.ptr(b), d, d, A.ptr(u), d, st)
     return GR.HessianFactor(u, perm, 0, None), status
@@ -374,12 +425,13 @@ def factor_hessian_sharded_attempt0(h: torch.Tensor, cfg: QuantConfig, group=Non
     return _factor_top_split(h, cfg, world, [rank], gather)
 
 
-def factor_hessian_split_emulated(h: torch.Tensor, cfg: QuantConfig, world: int):
+def factor_hessian_split_emulated(h: torch.Tensor, cfg: QuantConfig, world: int,
+                                  min_split: int | None = None):
     """The sharded factor's arithmetic on one GPU: every rank's row slices
     computed in turn and concatenated instead of all-gathered (for tests)."""
     def gather(parts, per):
         return torch.cat([parts[r] for r in range(world)], dim=0)
-    return _factor_top_split(A.to_device(h), cfg, world, list(range(world)), gather)
+    return _factor_top_split(A.to_device(h), cfg, world, list(range(world)), gather, min_split)
 
 
 def _members(shapes, grp):

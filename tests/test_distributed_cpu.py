@@ -40,6 +40,24 @@ def test_shard_range_rejects_bad_arguments():
         D.shard_range(-1, 0, 1)
 
 
+@pytest.mark.parametrize("n,world", [(14336, 8), (5504, 2), (1280, 3), (2816, 4), (128, 8),
+                                     (640, 8)])
+def test_split_factor_row_spans_cover_and_balance(n, world):
+    """The split factor's per-rank row slices: contiguous, 128-aligned,
+    covering [0, n); the triangular partition gives every rank about the same
+    lower-triangular work (row i costs ~i) where the rows allow it."""
+    for tri in (False, True):
+        spans = D._row_spans(n, world, triangular=tri)
+        assert len(spans) == world and spans[0][0] == 0 and spans[-1][1] == n
+        for (a0, a1), (b0, b1) in zip(spans, spans[1:]):
+            assert a1 == b0
+        for r0, r1 in spans:
+            assert r0 <= r1 and r0 % 128 == 0 and (r1 % 128 == 0 or r1 == n)
+    if n >= 2048 * world // 2:
+        work = [(r1 - r0) * (r0 + r1) / 2 for r0, r1 in D._row_spans(n, world, True)]
+        assert max(work) <= 1.2 * (n * n / 2) / world, work
+
+
 def test_lpt_assign_is_a_deterministic_partition_within_the_lpt_bound():
     rng = np.random.default_rng(0)
     for world in (1, 2, 3, 4):

@@ -106,6 +106,8 @@ def _factor_rank(rank, world, port, out_dir):
         h = torch.empty((4096, 4096), dtype=torch.float32, device="cuda")
         stats.syrk_into(h, x, accumulate=False)
         cfg = QuantConfig(w_bits=4, group_size=128, ordering_mode="diag_h", semantics="intended")
+        # split the diagonal blocks down to 1024 wide: 4096 -> 2048 -> 1024
+        D.FACTOR_SPLIT_MIN_N = 1024
         f, status = D.factor_hessian_sharded_attempt0(h, cfg)
         torch.cuda.synchronize()
         whole = factor_hessian(h, cfg)
@@ -119,9 +121,9 @@ def _factor_rank(rank, world, port, out_dir):
 
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two GPUs")
 def test_two_gpu_split_factor(tmp_path):
-    """The factor with its top-level products split across two GPUs (NCCL
-    all-gathers): the same U on both ranks, bit for bit, within 1e-5 of the
-    unsplit factor."""
+    """The factor with its split products divided across two GPUs (NCCL
+    all-gathers, three levels of splits): the same U on both ranks, bit for
+    bit, within 1e-5 of the unsplit factor."""
     import socket
     with socket.socket() as s:
         s.bind(("127.0.0.1", 0))

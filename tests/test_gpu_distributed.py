@@ -94,18 +94,21 @@ def test_empty_row_shard_still_writes_group_indices():
     assert empty.g_idx.equal(whole.g_idx)
 
 
-@pytest.mark.parametrize("world", [1, 2, 3, 8])
-def test_split_factor_matches_the_whole_factor(world):
-    """The factor with its top-level products split by rows over `world`
+@pytest.mark.parametrize("world,min_split", [(1, None), (2, None), (3, None), (8, None),
+                                             (2, 1024), (3, 512), (8, 512)])
+def test_split_factor_matches_the_whole_factor(world, min_split):
+    """The factor with its split products divided by rows over `world`
     ranks (emulated on one GPU: every slice computed in turn) equals the
     unsplit factor to float32 rounding: same permutation, U upper
-    triangular, within 1e-5 relative."""
+    triangular, within 1e-5 relative.  With `min_split` the diagonal blocks
+    at least that wide are split again (2560 -> 1280 -> 640 -> 320 at 512:
+    three levels of split products)."""
     x = LS.synth_activations(8192, 2560, 21)[0]
     h = torch.empty((2560, 2560), dtype=torch.float32, device="cuda")
     stats.syrk_into(h, x, accumulate=False)
     cfg = QuantConfig(w_bits=4, group_size=128, ordering_mode="diag_h", semantics="intended")
     whole = factor_hessian(h, cfg)
-    split, status = D.factor_hessian_split_emulated(h, cfg, world)
+    split, status = D.factor_hessian_split_emulated(h, cfg, world, min_split)
     assert int(status.item()) == 0
     assert split.perm.equal(whole.perm)
     assert torch.equal(torch.tril(split.u, -1), torch.zeros_like(split.u))
