@@ -7,9 +7,12 @@ across GPUs, each tied to an independence in the computation:
   sum over tokens): every rank forms the Gram matrix of its own tokens on its
   tensor cores, then one in-place float32 all-reduce per input group (NCCL
   over NVLink; the reduction of one group overlaps the next group's SYRK);
-* replicated factor -- every rank factors the identical reduced H
-  (``gptq_ref.py:44-93``); the factorization is deterministic, so the ranks'
-  ``U`` agree bit for bit and nothing is broadcast;
+* split factor -- the inverse-Cholesky recursion of the identical reduced H
+  (``gptq_ref.py:44-93``) has its products divided by rows across the ranks
+  and joined by all-gathers, recursively for wide diagonal blocks; narrow
+  diagonal blocks are factored by every rank (deterministic), so the ranks'
+  ``U`` agree bit for bit (``shard_factor=False``: every rank factors the
+  whole H, nothing is communicated);
 * row-sharded sweep -- rows of ``W`` are independent once ``U`` and the
   permutation are fixed (``gptq_ref.py:136-155`` quantizes row-wise), so each
   rank sweeps a contiguous block of rows with no communication, and one
@@ -233,9 +236,9 @@ def hessians_token_sharded(inputs_local: dict[str, torch.Tensor], group=None,
     return (hs, gs) if inputs_float_local is not None else hs
 
 
-# Hessians at least this wide split their factor's top-level products
-# across the ranks (factor_hessian_sharded_attempt0); smaller ones are factored
-# whole on every rank.
+# Hessians at least this wide split their factor's products across the
+# ranks (factor_hessian_sharded_attempt0); smaller ones are factored whole on
+# every rank.
 FACTOR_SHARD_MIN_D = 2048
 # Below the top level, diagonal blocks at least this wide are split again
 # across the ranks; narrower ones are factored whole by every rank (their
@@ -407,8 +410,9 @@ def _factor_top_split(h: torch.Tensor, cfg: QuantConfig, world: int, mine: list,
 
 def factor_hessian_sharded_attempt0(h: torch.Tensor, cfg: QuantConfig, group=None):
     """Attempt 0 of the damped factor (``gptq_ref.factor_hessian_attempt0``)
-    with its top-level products split across the ranks of ``group``: every
-    rank passes the same (all-reduced) H and gets the same factor.  Hessians
+    with its products split by rows across the ranks of ``group``
+    (``_inv_chol_split``): every rank passes the same (all-reduced) H and
+    gets the same factor.  Hessians
     narrower than ``FACTOR_SHARD_MIN_D`` or a single rank use the unsplit
     factor.  Returns ``(factor, status)``; a non-zero status (damping too
     small) is the same on every rank, which then redo the group with the
@@ -467,8 +471,8 @@ def quantize_layer_gptq_sharded(weights: dict, inputs_local: dict, cfg: QuantCon
     to the next group's partial H.  The factor's first damping attempt reads
     no status on the host; a group that needed more damping is redone at the
     end.  With ``shard_factor`` the factors of Hessians at least
-    ``FACTOR_SHARD_MIN_D`` wide split their top-level products across the
-    ranks (``factor_hessian_sharded_attempt0``); every rank still ends with the
+    ``FACTOR_SHARD_MIN_D`` wide split their products across the ranks
+    (``factor_hessian_sharded_attempt0``); every rank still ends with the
     same factor.  The results equal the sequential order bit for bit."""
     rank, world = rank_world(group)
     out: dict[str, SweepResult] = {}
