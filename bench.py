@@ -885,6 +885,7 @@ def sharded_layer_set(model, tokens, steps, warmup, world, rank, local, check=Tr
     or None."""
     import torch
     import torch.distributed as dist
+    from jax_gptq_b200 import _lib
     from jax_gptq_b200 import distributed as D
     from jax_gptq_b200 import layerset as LS
     from jax_gptq_b200 import stats
@@ -936,7 +937,7 @@ def sharded_layer_set(model, tokens, steps, warmup, world, rank, local, check=Tr
             _barrier(world)
             ar0 = torch.cuda.Event(enable_timing=True)
             ar0.record()
-            D.allreduce_sum_(h)
+            D.allreduce_sym_(h)  # packed upper triangle: pack, all-reduce, unpack
             ev[2].record()
             f, fst = D.factor_hessian_sharded_attempt0(h, cfg)
             if int(fst.item()) != 0:  # the same on every rank: redo with more damping
@@ -951,7 +952,7 @@ def sharded_layer_set(model, tokens, steps, warmup, world, rank, local, check=Tr
             t = [ev[0].elapsed_time(ev[1]), ar0.elapsed_time(ev[2]), ev[2].elapsed_time(ev[3]),
                  ev[3].elapsed_time(ev[4])]
             t = [_max_over_ranks(v, world) for v in t]
-            ar_bytes = 4 * d * d
+            ar_bytes = 4 * _lib.lib().gq_sym_packed_size(d)
             # NCCL's bus-bandwidth convention for all-reduce: 2 (N - 1) / N of the buffer per rank
             bus = ar_bytes * 2 * (world - 1) / world / (t[1] / 1e3) / 1e9 if world > 1 else None
             phases[grp] = {"d": d, "rows_per_rank": r1 - r0, "h_partial_ms": t[0],

@@ -424,6 +424,21 @@ int gq_masked_nll(const void* logits, int dtype, int64_t batch, int64_t tokens, 
                   int64_t workspace_bytes, void* stream);
 
 /* ------------------------------------------------------------------------
+ * Packed upper triangle of a symmetric d x d float32 matrix (row-major, ld
+ * ldh), for summing token-sharded Hessians across GPUs with about half the
+ * bytes.  128-row blocks b hold rows [128 b, 128 b + 128) from column 128 b
+ * on, row-major, back to back (block b starts at 128 (b d - 64 b (b - 1))).
+ * gq_sym_packed_size   floats of the packed form (about d^2 / 2 + 64 d).
+ * gq_sym_pack_upper    packed <- h (h must be symmetric; the diagonal tiles
+ *                      are copied whole).
+ * gq_sym_unpack_upper  h <- the packed entries on or above the diagonal,
+ *                      mirrored below it: exactly symmetric.
+ * GQ_EINVAL for d < 0, NULL pointers with d > 0, or ldh < d. */
+int64_t gq_sym_packed_size(int64_t d);
+int gq_sym_pack_upper(const float* h, int64_t d, int64_t ldh, float* packed, void* stream);
+int gq_sym_unpack_upper(const float* packed, int64_t d, float* h, int64_t ldh, void* stream);
+
+/* ------------------------------------------------------------------------
  * Multi-GPU: a per-device handle with an optional NCCL communicator and the
  * in-place fp32 sum all-reduce used for token-sharded Hessians (H = sum over
  * ranks of X_r^T X_r).  The reference is single-device and has no
@@ -443,6 +458,11 @@ int gq_masked_nll(const void* logits, int dtype, int64_t batch, int64_t tokens, 
  *                       inside NCCL until a host-side watchdog (a heartbeat
  *                       or a timeout on another thread) calls
  *                       gq_handle_abort, which ends the wait with an error.
+ * gq_allreduce_sym_f32  the symmetric d x d x (ld ldx) summed over the ranks
+ *                       in place through its packed upper triangle (half
+ *                       the bytes): gq_sym_pack_upper into `packed`
+ *                       (gq_sym_packed_size(d) floats, device memory), the
+ *                       all-reduce, gq_sym_unpack_upper back into x.
  * gq_comm_check         polls NCCL's asynchronous error state (a failed or
  *                       lost peer); GQ_ENCCL when set, after aborting the
  *                       communicator if abort_on_error and the handle owns it.
@@ -458,6 +478,8 @@ int gq_handle_create_nccl(int device, const void* unique_id, int nranks, int ran
 int gq_handle_destroy(gq_handle* h);
 int gq_handle_ranks(const gq_handle* h, int* nranks, int* rank);
 int gq_allreduce_sum_f32(gq_handle* h, float* buf, int64_t count, void* stream);
+int gq_allreduce_sym_f32(gq_handle* h, float* x, int64_t d, int64_t ldx, float* packed,
+                         void* stream);
 int gq_comm_check(gq_handle* h, int abort_on_error);
 int gq_handle_abort(gq_handle* h);
 

@@ -41,6 +41,10 @@ SIGNATURES = {
     "gq_handle_destroy": (c_int, [_P]),
     "gq_handle_ranks": (c_int, [_P, ctypes.POINTER(c_int), ctypes.POINTER(c_int)]),
     "gq_allreduce_sum_f32": (c_int, [_P, _P, c_int64, _P]),
+    "gq_allreduce_sym_f32": (c_int, [_P, _P, c_int64, c_int64, _P, _P]),
+    "gq_sym_packed_size": (c_int64, [c_int64]),
+    "gq_sym_pack_upper": (c_int, [_P, c_int64, c_int64, _P, _P]),
+    "gq_sym_unpack_upper": (c_int, [_P, c_int64, _P, c_int64, _P]),
     "gq_comm_check": (c_int, [_P, c_int]),
     "gq_handle_abort": (c_int, [_P]),
     "gq_rtn": (c_int, [_P, c_int64, c_int64, c_int64, _P, c_int, c_int, c_int, _P, _P, _P, _P, _P]),

@@ -14,6 +14,12 @@
 
 #include "gq_common.cuh"
 
+namespace gq {
+int64_t sym_packed_size(int64_t d);
+int sym_pack(const float* h, int64_t d, int64_t ldh, float* packed, cudaStream_t st);
+int sym_unpack(const float* packed, int64_t d, float* h, int64_t ldh, cudaStream_t st);
+}  // namespace gq
+
 struct gq_handle {
   int device;
   ncclComm_t comm;  // NULL: no collectives
@@ -198,6 +204,26 @@ int gq_allreduce_sum_f32(gq_handle* h, float* buf, int64_t count, void* stream) 
                                               h->comm, gq::as_stream(stream));
   if (r != ncclSuccess) return gq::comm::nccl_fail("ncclAllReduce", r);
   return GQ_OK;
+}
+
+int gq_allreduce_sym_f32(gq_handle* h, float* x, int64_t d, int64_t ldx, float* packed,
+                         void* stream) {
+  GQ_REQUIRE(h != nullptr, "gq_allreduce_sym_f32: NULL handle");
+  if (h->aborted) return gq::fail(GQ_ENCCL, "gq_allreduce_sym_f32: the communicator was aborted");
+  GQ_REQUIRE(h->comm != nullptr, "gq_allreduce_sym_f32: the handle has no communicator");
+  GQ_REQUIRE(d >= 0 && d <= (int64_t)INT32_MAX && (d == 0 || (x != nullptr && packed != nullptr &&
+                                                               ldx >= d)),
+             "gq_allreduce_sym_f32: bad arguments (d=%lld ldx=%lld)", (long long)d,
+             (long long)ldx);
+  if (d == 0) return GQ_OK;
+  gq::comm::DeviceScope scope(h->device);
+  GQ_CHECK_CUDA(scope.err);
+  cudaStream_t st = gq::as_stream(stream);
+  GQ_TRY(gq::sym_pack(x, d, ldx, packed, st));
+  ncclResult_t r = gq::comm::api().all_reduce(packed, packed, (size_t)gq::sym_packed_size(d),
+                                              ncclFloat32, ncclSum, h->comm, st);
+  if (r != ncclSuccess) return gq::comm::nccl_fail("ncclAllReduce", r);
+  return gq::sym_unpack(packed, d, x, ldx, st);
 }
 
 }  // extern "C"

@@ -35,6 +35,7 @@ from typing import Hashable
 import torch
 
 from . import _arrays as A
+from . import _lib
 from . import stats
 from .config import QuantConfig
 from .gptq_ref import SweepResult, factor_hessian, gptq_sweep
@@ -153,6 +154,47 @@ def allreduce_sum_(t: torch.Tensor, group=None, async_op: bool = False):
     return _Work("all_reduce", work) if async_op else work
 
 
+class _SymWork:
+    """An in-flight packed all-reduce of a symmetric matrix: ``wait`` makes
+    the current stream wait for the sum, then unpacks it into the matrix on
+    that stream (upper entries, mirrored)."""
+
+    def __init__(self, work, packed: torch.Tensor, h: torch.Tensor):
+        self._work, self._packed, self._h = work, packed, h
+
+    def wait(self):
+        self._work.wait()
+        # the unpack may run on another stream than the one that allocated
+        # the buffer: keep it from being reused before the unpack has read it
+        self._packed.record_stream(torch.cuda.current_stream())
+        d = self._h.shape[0]
+        _lib.call("gq_sym_unpack_upper", A.ptr(self._packed), d, A.ptr(self._h),
+                  self._h.stride(0), A.stream())
+        self._packed = None
+
+
+def allreduce_sym_(h: torch.Tensor, group=None, async_op: bool = False):
+    """In-place sum over the ranks of ``group`` of a symmetric float32 CUDA
+    matrix through its packed upper triangle (``gq_sym_pack_upper``: about
+    half the bytes of the full matrix).  The result is exactly symmetric.
+    Returns the work handle when ``async_op`` (its ``wait`` also unpacks, on
+    the stream current at that time); None for a single rank."""
+    dist = _dist()
+    if not (dist.is_available() and dist.is_initialized()) or dist.get_world_size(group) == 1:
+        return None
+    if h.dtype != torch.float32 or not h.is_cuda or h.dim() != 2 or h.shape[0] != h.shape[1] \
+            or h.stride(1) != 1:
+        raise ValueError("allreduce_sym_ needs a square float32 CUDA matrix with unit column stride")
+    d = h.shape[0]
+    packed = torch.empty((_lib.lib().gq_sym_packed_size(d),), dtype=torch.float32, device=h.device)
+    _lib.call("gq_sym_pack_upper", A.ptr(h), d, h.stride(0), A.ptr(packed), A.stream())
+    work = _SymWork(allreduce_sum_(packed, group, async_op=True), packed, h)
+    if async_op:
+        return work
+    work.wait()
+    return None
+
+
 class Heartbeat:
     """Host-side liveness check between steps, through a ``torch.distributed``
     key-value store (``TCPStore`` / ``FileStore``).
@@ -223,7 +265,7 @@ def hessians_token_sharded(inputs_local: dict[str, torch.Tensor], group=None,
         d = x.shape[1]
         h = torch.empty((d, d), dtype=torch.float32, device=x.device)
         stats.syrk_into(h, x, accumulate=False)
-        pending.append(allreduce_sum_(h, group, async_op=True))
+        pending.append(allreduce_sym_(h, group, async_op=True))
         hs[grp] = h
         if inputs_float_local is not None:
             g = torch.empty((d, d), dtype=torch.float32, device=x.device)
@@ -488,12 +530,13 @@ def quantize_layer_gptq_sharded(weights: dict, inputs_local: dict, cfg: QuantCon
             d = x.shape[1]
             h = torch.empty((d, d), dtype=torch.float32, device=x.device)
             stats.syrk_into(h, x, accumulate=False, token_chunk=chunk)
-            works[grp] = allreduce_sum_(h, group, async_op=True)
+            works[grp] = allreduce_sym_(h, group, async_op=True)
             return h
 
         def prepare(grp, h):
             if works.get(grp) is not None:
-                works[grp].wait()  # the side stream (current here) waits for the all-reduce
+                # the side stream (current here) waits for the all-reduce and unpacks
+                works[grp].wait()
             if shard_factor:
                 return factor_hessian_sharded_attempt0(h, cfg, group)
             return factor_hessian_attempt0(h, cfg)
@@ -586,6 +629,19 @@ class CommHandle:
             raise ValueError("allreduce_sum_ needs a contiguous float32 CUDA tensor")
         self._lib.call("gq_allreduce_sum_f32", self._h, A.ptr(t), t.numel(), A.stream())
 
+    def allreduce_sym_(self, h: torch.Tensor) -> None:
+        """In-place sum of a symmetric float32 matrix through its packed upper
+        triangle (``gq_allreduce_sym_f32``: half the bytes), ordered on the
+        current stream; the result is exactly symmetric."""
+        if h.dtype != torch.float32 or not h.is_cuda or h.dim() != 2 or \
+                h.shape[0] != h.shape[1] or h.stride(1) != 1:
+            raise ValueError("allreduce_sym_ needs a square float32 CUDA matrix")
+        d = h.shape[0]
+        packed = torch.empty((self._lib.lib().gq_sym_packed_size(d),), dtype=torch.float32,
+                             device=h.device)
+        self._lib.call("gq_allreduce_sym_f32", self._h, A.ptr(h), d, h.stride(0),
+                       A.ptr(packed), A.stream())
+
     def check(self, abort: bool = True) -> None:
         """Raise ``GQError`` (GQ_ENCCL) if NCCL reports an asynchronous error
         (a failed or lost peer); the communicator is aborted first when
@@ -612,6 +668,6 @@ class CommHandle:
 __all__ = [
     "SWEEP_ROW_ALIGN", "RankFailure", "Heartbeat", "FACTOR_SHARD_MIN_D",
     "factor_hessian_sharded_attempt0", "factor_hessian_split_emulated", "rank_world", "shard_range", "lpt_assign", "layer_set_cost",
-    "allreduce_sum_", "gather_rows", "hessians_token_sharded", "quantize_layer_gptq_sharded",
+    "allreduce_sum_", "allreduce_sym_", "gather_rows", "hessians_token_sharded", "quantize_layer_gptq_sharded",
     "layer_sets_for_rank", "tokens_for_rank", "CommHandle",
 ]

@@ -99,6 +99,25 @@ def test_pair_kernel_switch_validates_its_argument():
     assert lib.gq_set_pair_kernels(2) != 0
 
 
+def test_packed_symmetric_size_and_argument_checks():
+    """gq_sym_packed_size against the layout restated here (128-row blocks,
+    row r from column 128 (r // 128) on), and the pack / unpack / packed
+    all-reduce entries reject bad arguments before launching anything."""
+    lib = _lib.lib()
+    for d in (0, 1, 127, 128, 129, 1000, 4096, 11008, 28672):
+        expect = sum(d - 128 * (r // 128) for r in range(d))
+        assert lib.gq_sym_packed_size(d) == expect, d
+    assert lib.gq_sym_packed_size(28672) * 4 < 0.51 * 4 * 28672 ** 2
+    p = ctypes.c_void_p(256)
+    assert lib.gq_sym_pack_upper(p, -1, 4, p, None) == _lib.GQ_EINVAL
+    assert lib.gq_sym_pack_upper(None, 4, 4, p, None) == _lib.GQ_EINVAL
+    assert lib.gq_sym_pack_upper(p, 4, 3, p, None) == _lib.GQ_EINVAL
+    assert lib.gq_sym_unpack_upper(p, 4, None, 4, None) == _lib.GQ_EINVAL
+    assert lib.gq_sym_unpack_upper(p, 4, p, 3, None) == _lib.GQ_EINVAL
+    assert lib.gq_sym_pack_upper(None, 0, 0, None, None) == 0
+    assert lib.gq_allreduce_sym_f32(None, p, 4, 4, p, None) == _lib.GQ_EINVAL
+
+
 def test_sweep_row_group_switch_validates_its_argument():
     lib = _lib.lib()
     for r in (-1, 1, 2, 4, 0):

@@ -41,15 +41,19 @@ def _rank(rank, world, uid, out_dir):
     t0, t1 = D.shard_range(x.shape[0], rank, world)
     h = torch.empty((384, 384), dtype=torch.float32, device="cuda")
     stats.syrk_into(h, x[t0:t1], accumulate=False)
+    hs = h.clone()
     handle = D.CommHandle(rank, uid, world, rank)
     try:
         handle.allreduce_sum_(h)
+        handle.allreduce_sym_(hs)  # packed upper triangle
         torch.cuda.synchronize()
         full = torch.empty_like(h)
         stats.syrk_into(full, x, accumulate=False)
         rel = (torch.linalg.norm(h - full) / torch.linalg.norm(full)).item()
+        rel_sym = (torch.linalg.norm(hs - full) / torch.linalg.norm(full)).item()
         with open(os.path.join(out_dir, f"r{rank}.pkl"), "wb") as f:
-            pickle.dump({"rel": rel, "h": h.cpu().numpy()}, f)
+            pickle.dump({"rel": rel, "h": h.cpu().numpy(), "rel_sym": rel_sym,
+                         "hs": hs.cpu().numpy(), "sym_exact": bool(hs.equal(hs.t()))}, f)
     finally:
         handle.close()
 
@@ -68,7 +72,27 @@ def test_two_gpu_hessian_allreduce(tmp_path):
     outs = [pickle.load(open(tmp_path / f"r{r}.pkl", "rb")) for r in range(world)]
     for o in outs:
         assert o["rel"] < 1e-6, o["rel"]
+        assert o["rel_sym"] < 1e-6 and o["sym_exact"], o["rel_sym"]
     assert np.array_equal(outs[0]["h"], outs[1]["h"])
+    assert np.array_equal(outs[0]["hs"], outs[1]["hs"])
+
+
+def test_single_rank_packed_symmetric_allreduce_is_identity():
+    """gq_allreduce_sym_f32 with one rank: pack, all-reduce, unpack give back
+    the symmetric input bit for bit, for a width that is not a multiple of
+    128 and a leading dimension wider than the matrix."""
+    uid = D.CommHandle.unique_id()
+    h = D.CommHandle(torch.cuda.current_device(), uid, 1, 0)
+    try:
+        a = torch.randn(300, 300, device="cuda")
+        buf = torch.zeros(300, 320, device="cuda")
+        buf[:, :300] = a + a.t()
+        ref = buf.clone()
+        h.allreduce_sym_(buf[:, :300])
+        torch.cuda.synchronize()
+        assert buf.equal(ref)
+    finally:
+        h.close()
 
 
 def test_single_rank_check_then_abort():
@@ -112,9 +136,26 @@ def _factor_rank(rank, world, port, out_dir):
         torch.cuda.synchronize()
         whole = factor_hessian(h, cfg)
         rel = (torch.linalg.norm(f.u - whole.u) / torch.linalg.norm(whole.u)).item()
+        # token-shard partial H summed through the packed upper triangle, once
+        # synchronously and once asynchronously with the unpack on a side stream
+        t0, t1 = D.shard_range(x.shape[0], rank, world)
+        hp = torch.empty_like(h)
+        stats.syrk_into(hp, x[t0:t1], accumulate=False)
+        hp2 = hp.clone()
+        D.allreduce_sym_(hp)
+        side = torch.cuda.Stream()
+        side.wait_stream(torch.cuda.current_stream())
+        work = D.allreduce_sym_(hp2, async_op=True)
+        with torch.cuda.stream(side):
+            work.wait()
+        torch.cuda.current_stream().wait_stream(side)
+        torch.cuda.synchronize()
+        sym_rel = max((torch.linalg.norm(t - h) / torch.linalg.norm(h)).item() for t in (hp, hp2))
         with open(os.path.join(out_dir, f"f{rank}.pkl"), "wb") as fh:
             pickle.dump({"status": int(status.item()), "rel": rel,
-                         "u": f.u.cpu().numpy(), "perm_equal": bool(f.perm.equal(whole.perm))}, fh)
+                         "u": f.u.cpu().numpy(), "perm_equal": bool(f.perm.equal(whole.perm)),
+                         "sym_rel": sym_rel, "sym_exact": bool(hp.equal(hp.t())),
+                         "sym_same": bool(hp.equal(hp2)), "hp": hp.cpu().numpy()}, fh)
     finally:
         dist.destroy_process_group()
 
@@ -123,7 +164,10 @@ def _factor_rank(rank, world, port, out_dir):
 def test_two_gpu_split_factor(tmp_path):
     """The factor with its split products divided across two GPUs (NCCL
     all-gathers, three levels of splits): the same U on both ranks, bit for
-    bit, within 1e-5 of the unsplit factor."""
+    bit, within 1e-5 of the unsplit factor.  Also the token-sharded H summed
+    through its packed upper triangle (``allreduce_sym_``, synchronous and
+    asynchronous): within 1e-6 of the whole H, exactly symmetric, the same
+    on both ranks."""
     import socket
     with socket.socket() as s:
         s.bind(("127.0.0.1", 0))
@@ -140,4 +184,6 @@ def test_two_gpu_split_factor(tmp_path):
     outs = [pickle.load(open(tmp_path / f"f{r}.pkl", "rb")) for r in range(world)]
     for o in outs:
         assert o["status"] == 0 and o["perm_equal"] and o["rel"] <= 1e-5, o["rel"]
+        assert o["sym_rel"] < 1e-6 and o["sym_exact"] and o["sym_same"], o["sym_rel"]
     assert np.array_equal(outs[0]["u"], outs[1]["u"])
+    assert np.array_equal(outs[0]["hp"], outs[1]["hp"])
