@@ -33,6 +33,8 @@
 // past it (its parameters are taken from the columns at its start, before
 // the far update); other group sizes fall back to 128-column super-blocks.
 // Finally codes/dequant are scattered back to original column order.
+#include <atomic>
+
 #include "gq_common.cuh"
 #include "gq_quant.cuh"
 
@@ -717,21 +719,22 @@ int transpose2d(const float* src, int64_t rows, int64_t cols, int64_t lds, float
 // Row groups per CTA of the four-warp block step (gq_set_sweep_row_groups):
 // 0 picks by row count, 1, 2 or 4 force that many, -1 forces the one-warp
 // kernel.
-static int g_row_groups = 0;
+static std::atomic<int> g_row_groups{0};
 
 // The four-warp block step takes the band and its row groups' buffers in
 // dynamic shared memory above the default 48 KB; allowed once per (device,
 // instance).
 template <int G, int R>
 static int launch_rows4(const SweepArgs& a, unsigned grid, cudaStream_t st) {
-  static int done_dev = -1;
+  // setting the attribute twice (two threads racing here) is harmless
+  static std::atomic<int> done_dev{-1};
   int dev = 0;
   GQ_CHECK_CUDA(cudaGetDevice(&dev));
-  if (done_dev != dev) {
+  if (done_dev.load(std::memory_order_relaxed) != dev) {
     GQ_CHECK_CUDA(cudaFuncSetAttribute(sweep_rows_kernel<G, R>,
                                        cudaFuncAttributeMaxDynamicSharedMemorySize,
                                        (int)sr_smem_bytes(R)));
-    done_dev = dev;
+    done_dev.store(dev, std::memory_order_relaxed);
   }
   sweep_rows_kernel<G, R><<<grid, SR_THREADS * R, sr_smem_bytes(R), st>>>(a);
   return GQ_OK;
@@ -768,7 +771,8 @@ static int launch_rows1_g(int group_size, const SweepArgs& a, unsigned grid, cud
 // fit in one wave; four (194 KB, one per SM) while those do; beyond that the
 // one-warp kernel, whose 34 KB CTAs keep a wave of them resident.
 static int pick_row_groups(int64_t m, int sms) {
-  if (g_row_groups != 0) return g_row_groups < 0 ? 0 : g_row_groups;
+  const int forced = g_row_groups.load(std::memory_order_relaxed);
+  if (forced != 0) return forced < 0 ? 0 : forced;
   const int64_t rows32 = ceil_div(m, 32);
   if (rows32 <= 2 * (int64_t)sms) return 1;
   if (rows32 <= 4 * (int64_t)sms) return 4;
@@ -784,7 +788,7 @@ int64_t gq_gptq_sweep_workspace_size(int64_t m, int64_t n) { return gq::sweep_ws
 int gq_set_sweep_row_groups(int r) {
   GQ_REQUIRE(r == -1 || r == 0 || r == 1 || r == 2 || r == 4,
              "gq_set_sweep_row_groups: %d is not one of -1, 0, 1, 2, 4", r);
-  gq::g_row_groups = r;
+  gq::g_row_groups.store(r, std::memory_order_relaxed);
   return GQ_OK;
 }
 

@@ -163,6 +163,8 @@ class _SymWork:
         self._work, self._packed, self._h = work, packed, h
 
     def wait(self):
+        if self._packed is None:  # already waited for and unpacked
+            return
         self._work.wait()
         # the unpack may run on another stream than the one that allocated
         # the buffer: keep it from being reused before the unpack has read it
