@@ -395,6 +395,9 @@ def _inv_chol_split(b: torch.Tensor, o: int, n: int, world: int, mine: list, gat
         out[:r1 - r0] = b[p1 + r0:p1 + r1, p1:o + n]
         parts[r] = out
     b[p1:o + n, p1:o + n] = assemble(parts, tri, n2)
+    # only T is read after the recursion below: free X11^T and L21 first
+    # (stream-ordered, so the pending kernels that read them are unaffected)
+    del xt, l21, parts
     # 4. X22 = L22^-1
     _inv_chol_split(b, p1, n2, world, mine, gather, ws, status, min_split)
     # 5. X21 = -X22 T^T: rows [r0, r1) of the lower X22 are zero past column
