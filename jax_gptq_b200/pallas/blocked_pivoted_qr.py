@@ -321,8 +321,9 @@ def benchmark(n: int = 4096, panel: int = 64, reps: int = 2, seed: int = 1,
               variants: str | None = None) -> dict:
     """Time the 4096 x 4096 fp32 benchmark matrix (:func:`benchmark_matrix`)
     in both semantics, and the rank-deficient variant in ``smallest`` mode
-    (the survey's setting) and ``largest`` mode (rank revealing: its numerical
-    rank is the 3840 of the construction).  GFLOP/s counts (4/3) n^3."""
+    (the pivot order the reference's rank-deficient QRCP case uses) and
+    ``largest`` mode (rank revealing: its numerical rank is the 3840 of the
+    construction).  GFLOP/s counts (4/3) n^3."""
     a = torch.from_numpy(benchmark_matrix(n, seed)).cuda()
     a_def = torch.from_numpy(benchmark_matrix(n, seed, rank_deficient=True)).cuda()
     flops = 4.0 / 3.0 * n ** 3
