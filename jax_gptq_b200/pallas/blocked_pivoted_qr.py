@@ -2,10 +2,12 @@
 ``src/jax_gptq/pallas/blocked_pivoted_qr.py``.
 
 The factorization runs in ``libgq`` (``csrc/gq_qr.cu``): per pivot step a
-single-CTA kernel (pivot, swap, reflector, compact-WY append) and an
-all-SM kernel that exposes one row of the deferred trailing block and
-downdates the column norms; per panel three fp32 GEMMs apply the compact WY
-update and one kernel refreshes the norms.
+kernel on a cluster of eight CTAs (pivot, swap, reflector, compact-WY
+append, the exposed-row weights) and an all-SM kernel that exposes one row
+of the deferred trailing block and downdates the column norms, launched as
+programmatic dependents; per panel two fp32 tensor-core GEMMs around a small
+T application apply the compact WY update, and one kernel refreshes the
+norms.
 
 ``semantics="reference"`` (default) reproduces the reference's default
 (jit-compiled) path bit for bit in control flow, including two index slips:
